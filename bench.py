@@ -1,0 +1,455 @@
+#!/usr/bin/env python
+"""Benchmark of the fused relu(A.B + C) hot path (MiniXLA's OP_FUSED node) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one fused relu(A.B + C) over one batch of rows, fp32 in and out.
+Workload: every GPU owns an 8192-row shard of A and C with the full 8192 x 8192
+B (weak scaling: the single-GPU case is the 8192^3 headline shape; at 4 GPUs
+the job is the 32768 x 8192 x 8192 row-sharded shape).  Output rows stay on
+their GPU; no collective runs on the data path.  `--workload config5` runs the
+fixed 32768 x 8192 x 8192 job split over N GPUs instead (strong scaling).
+
+ours:      `value` = whole-job TFLOP/s with inputs resident in HBM, K launches of
+           the fused kernel through the device-pointer C ABI, timed with CUDA
+           events on the launch stream, max over ranks.  `e2e` = the same metric
+           through gpu_execute_into() (the reference-facing entry point) with
+           pinned host buffers, uploads and the download inside the timed region.
+reference: MiniXLA's own CPU execute() (eval_fused, graph.c:64-115), compiled
+           unmodified from the reference sources into oracle/_ref, on a bounded
+           row sample of the same workload using all host cores (one process per
+           core, row-parallel), rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import datetime as dt
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+NDIM = 8192       # N = K = 8192
+ROWS_PER_GPU = 8192
+CONFIG5_M = 32768
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=400)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--precision", choices=["tf32", "3xtf32"], default="tf32")
+    p.add_argument("--workload", choices=["weak", "config5"], default="weak")
+    p.add_argument("--e2e-steps", type=int, default=10)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def shard_rows(world: int, rank: int, workload: str):
+    """Row range [r0, r1) of this rank and the job's total M."""
+    if workload == "config5":
+        m_total = CONFIG5_M
+        base, extra = divmod(m_total, world)
+        r0 = rank * base + min(rank, extra)
+        return r0, r0 + base + (1 if rank < extra else 0), m_total
+    return rank * ROWS_PER_GPU, (rank + 1) * ROWS_PER_GPU, ROWS_PER_GPU * world
+
+
+# ------------------------------------------------------------------ clocks
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, physical_index: str):
+        self.idx = physical_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "50", "-i", self.idx], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.5)
+
+    def stop(self, t0: float, t1: float):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.1)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = []
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                ts = dt.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        inside = [r for r in rows if t0 <= r[0] <= t1] or sorted(rows, key=lambda r: abs(r[0] - (t0 + t1) / 2))[:3]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in inside for i, v in enumerate(r[3]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(r[1] for r in inside) if inside else None,
+                "sm_max_mhz": max(r[2] for r in inside) if inside else None,
+                "reasons": reasons, "samples": len(inside)}
+
+
+def physical_gpu(local_rank: int) -> str:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids):
+            return ids[local_rank]
+    return str(local_rank)
+
+
+# ------------------------------------------------------------------ reference CPU workers
+
+
+def _ref_worker(rows, setup_q, go, result_q, steps):
+    """One host process running MiniXLA's execute() on `rows` of the 8192^3 workload."""
+    sys.path.insert(0, str(ROOT))
+    from minixla_b200 import datagen
+    from oracle.bindings import REF_LIB, RefGraph, fused_oracle
+
+    kind = "reference" if REF_LIB.exists() else "port"
+    B = datagen.uniform((NDIM, NDIM), 1)
+    A = datagen.uniform((len(rows), NDIM), 0, row_offset=rows[0])
+    Cm = datagen.normal((len(rows), NDIM), 2, row_offset=rows[0])
+    if kind == "reference":
+        rg = RefGraph()
+        L = rg.lib
+        root = rg.optimize(L.g_relu(L.g_add(L.g_matmul(rg.input(A), rg.input(B)), rg.input(Cm))))
+        del B
+
+        def run():
+            node = root.contents
+            if node.owns_output and node.output:
+                L.free_tensor(node.output)     # drop the memoized result (bench.c:230-231)
+            node.output = None
+            node.owns_output = 0
+            if not L.execute(root):
+                raise RuntimeError("execute() failed")
+    else:
+        def run():
+            fused_oracle(A, B, [("add", Cm), ("relu",)], threads=1)
+    setup_q.put(kind)
+    for _ in range(steps):
+        go.wait()
+        t0 = time.perf_counter()
+        run()
+        result_q.put(time.perf_counter() - t0)
+
+
+def run_reference_steps(total_steps: int, rows_per_worker: int, workers: int):
+    """Runs `total_steps` synchronized steps over `workers` processes; returns
+    (per-step wall seconds, rows per step, kind)."""
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    go = ctx.Barrier(workers + 1)
+    setup_q, result_q = ctx.Queue(), ctx.Queue()
+    procs = []
+    for w in range(workers):
+        r0 = w * (ROWS_PER_GPU // workers)
+        rows = list(range(r0, r0 + rows_per_worker))
+        p = ctx.Process(target=_ref_worker, args=(rows, setup_q, go, result_q, total_steps), daemon=True)
+        p.start()
+        procs.append(p)
+    kinds = {setup_q.get(timeout=600) for _ in range(workers)}
+    walls = []
+    for _ in range(total_steps):
+        t0 = time.perf_counter()
+        go.wait()
+        for _ in range(workers):
+            result_q.get(timeout=3600)
+        walls.append(time.perf_counter() - t0)
+    for p in procs:
+        p.join(timeout=60)
+    return walls, rows_per_worker * workers, ("reference" if kinds == {"reference"} else "port")
+
+
+def host_workers() -> int:
+    return max(1, min(os.cpu_count() or 1, 16))
+
+
+def cpu_baseline(rows_target: int = 16):
+    workers = host_workers()
+    rpw = max(1, round(rows_target / workers))
+    walls, rows, kind = run_reference_steps(2, rpw, workers)
+    wall = walls[-1]
+    tflops = 2.0 * rows * NDIM * NDIM / wall / 1e12
+    return {"value": tflops, "unit": "TFLOP/s", "cores": workers, "kind": kind,
+            "sample": f"{rows} output rows of relu(A.B+C) at K=N=8192 ({rpw} per process, {workers} processes "
+                      f"in parallel) through MiniXLA's execute(); second of two timed passes; "
+                      f"{wall:.2f} s wall"}
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    workers = host_workers()
+    walls, rows, kind = run_reference_steps(args.warmup + args.steps, 1, workers)
+    timed = walls[args.warmup:]
+    total = sum(timed)
+    value = 2.0 * rows * len(timed) * NDIM * NDIM / total / 1e12
+    line = {
+        "metric": "fused relu(A.B+C) TFLOP/s (fp32 in/out)", "impl": "reference", "value": value,
+        "unit": "TFLOP/s", "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / len(timed), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded splitmix64: A,B ~ U[-1,1], C ~ N(0,1))",
+        "config": {"workload": "relu(A.B+C) 8192x8192x8192 per shard, row sample per step",
+                   "rows_per_step": rows, "N": NDIM, "K": NDIM, "parallelism": f"{workers} host processes"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": workers, "kind": kind,
+                         "sample": f"{rows} output rows per step ({workers} processes x 1 row) through "
+                                   "MiniXLA's execute()"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ our arm
+
+
+def measured_tf32_peak():
+    """TF32 dense peak: the measured bf16 burst GEMM rate of this pool halved
+    (TF32 tensor-core math runs at half the bf16 rate on B200)."""
+    f = ROOT / "MEASURED_PEAKS.json"
+    try:
+        bf16 = float(json.loads(f.read_text())["bf16_tflops"])
+        return bf16 / 2.0, f"measured bf16 burst {bf16:.1f} TFLOP/s / 2 (MEASURED_PEAKS.json)"
+    except Exception:
+        return 1590.0 / 2.0, "fallback bf16 burst 1590 TFLOP/s / 2"
+
+
+def traffic_from_profile(precision: str, m: int):
+    f = ROOT / "profiles" / f"fused_gemm_{precision}_{ROWS_PER_GPU}.json"
+    try:
+        d = json.loads(f.read_text())
+        return float(d["dram_bytes_per_launch"]) * m / float(d["rows"])
+    except Exception:
+        return None
+
+
+def ours_arm(args, rank, local_rank, world):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from minixla_b200 import datagen
+    from minixla_b200 import lib as mlib
+    from minixla_b200.abi import OP_ADD, OP_RELU, HostGraph
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=dt.timedelta(seconds=300), device_id=dev)
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # CPU baseline first, before this process touches its GPU (rank 0, one GPU).
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_baseline()
+
+    lib = mlib.load()
+    prec = mlib.GPU_PRECISION_TF32 if args.precision == "tf32" else mlib.GPU_PRECISION_3XTF32
+    r0, r1, m_total = shard_rows(world, rank, args.workload)
+    M, N, K = r1 - r0, NDIM, NDIM
+    A = datagen.uniform((M, K), 0, row_offset=r0)
+    B = datagen.uniform((K, N), 1)
+    Cm = datagen.normal((M, N), 2, row_offset=r0)
+
+    ctx = lib.gpu_ctx_create_on(local_rank)
+    if not ctx:
+        raise RuntimeError(f"gpu_ctx_create_on({local_rank}) failed: {mlib.last_error()}")
+    lib.gpu_ctx_set_precision(ctx, prec)
+
+    # ---- device-resident timing (value)
+    A_d, B_d, C_d = (torch.from_numpy(x).to(dev) for x in (A, B, Cm))
+    out_d = torch.empty((M, N), device=dev, dtype=torch.float32)
+    steps = (mlib.EpStepDev * 2)()
+    steps[0] = mlib.EpStepDev(mlib.MXB_EP_ADD_FULL, 0, C_d.data_ptr(), N, 0.0, 0)
+    steps[1] = mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0)
+    stream = torch.cuda.current_stream(dev)
+
+    def launch():
+        rc = lib.mxb_fused_gemm(ctx, A_d.data_ptr(), K, B_d.data_ptr(), N, out_d.data_ptr(), N, M, N, K, steps, 2,
+                                prec, stream.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"mxb_fused_gemm failed: {mlib.last_error()}")
+
+    for _ in range(args.warmup):
+        launch()
+    torch.cuda.synchronize()
+    if lib.mxb_check_device_error(ctx) != 0:
+        raise RuntimeError(mlib.last_error())
+
+    sampler = ClockSampler(physical_gpu(local_rank))
+    sampler.start()
+    ev_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    launches0 = lib.mxb_launch_count()
+    h0 = time.time()
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev_s[i].record(stream)
+        launch()
+        ev_e[i].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    h1 = time.time()
+    launches = lib.mxb_launch_count() - launches0
+    barrier()
+    clocks = sampler.stop(h0, h1)
+    if lib.mxb_check_device_error(ctx) != 0:
+        raise RuntimeError(mlib.last_error())
+    total_ms = max_over_ranks(t_start.elapsed_time(t_end))
+    per_launch_ms = statistics.mean(ev_s[i].elapsed_time(ev_e[i]) for i in range(args.steps))
+    per_launch_ms = max_over_ranks(per_launch_ms)
+
+    flops_rank = 2.0 * M * N * K
+    flops_job = 2.0 * m_total * N * K
+    value = flops_job * args.steps / (total_ms * 1e-3) / 1e12
+
+    # spot check of this rank's result against the oracle on a few rows
+    from oracle.bindings import fused_oracle
+
+    rows = [0, M // 2, M - 1]
+    want = fused_oracle(A, B, [("add", Cm), ("relu",)], rows=rows)
+    got = out_d[rows].cpu().numpy()
+    rel = float(np.linalg.norm(got - want) / np.linalg.norm(want))
+    tol = 2e-3 if prec == mlib.GPU_PRECISION_TF32 else 1e-5
+    if not rel <= tol:
+        raise RuntimeError(f"bench result check failed: relative error {rel:.3g} > {tol}")
+
+    # cuBLAS TF32 on the same shape, for context only (not on the product path)
+    cublas = None
+    if rank == 0:
+        torch.backends.cuda.matmul.allow_tf32 = True
+        x = A_d[:, :].contiguous()
+        for _ in range(3):
+            torch.matmul(x, B_d)
+        torch.cuda.synchronize()
+        best = math.inf
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(x, B_d)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        cublas = flops_rank / (best * 1e-3) / 1e12
+        torch.backends.cuda.matmul.allow_tf32 = False
+        del x
+    del out_d
+    torch.cuda.empty_cache()
+
+    # ---- end to end through the reference-facing C ABI with pinned host buffers
+    A_h = torch.from_numpy(A).pin_memory()
+    B_h = torch.from_numpy(B).pin_memory()
+    C_h = torch.from_numpy(Cm).pin_memory()
+    O_h = torch.empty((M, N), dtype=torch.float32).pin_memory()
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A_h), hg.input_node(B_h), [(OP_ADD, hg.input_node(C_h)), (OP_RELU, None)])
+    out_t = hg.tensor(O_h)
+    for _ in range(2):
+        if lib.gpu_execute_into(root, ctx, out_t) != 0:
+            raise RuntimeError(mlib.last_error())
+    barrier()
+    e0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        if lib.gpu_execute_into(root, ctx, out_t) != 0:
+            raise RuntimeError(mlib.last_error())
+    e_ms = max_over_ranks((time.perf_counter() - e0) * 1e3 / args.e2e_steps)
+    e2e_value = flops_job / (e_ms * 1e-3) / 1e12
+    rel_e2e = float(np.linalg.norm(O_h[rows].numpy() - want) / np.linalg.norm(want))
+    if not rel_e2e <= tol:
+        raise RuntimeError(f"e2e result check failed: relative error {rel_e2e:.3g} > {tol}")
+
+    peak, peak_src = measured_tf32_peak()
+    if prec == mlib.GPU_PRECISION_3XTF32:
+        peak, peak_src = peak / 3.0, peak_src + " / 3 (three TF32 products per multiply-add)"
+    achieved = flops_rank / (per_launch_ms * 1e-3) / 1e12
+    lib.gpu_ctx_destroy(ctx)
+
+    if rank == 0:
+        line = {
+            "metric": "fused relu(A.B+C) TFLOP/s (fp32 in/out)",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "strong" if args.workload == "config5" else "weak",
+            "vs_baseline": None, "dtype": args.precision,
+            "data": "synthetic (seeded splitmix64: A,B ~ U[-1,1], C ~ N(0,1))",
+            "config": {
+                "workload": ("relu(A.B+C) 32768x8192x8192 split over N GPUs" if args.workload == "config5"
+                             else "relu(A.B+C) 8192x8192x8192 per GPU (8192-row shard each)"),
+                "M_total": m_total, "N": N, "K": K, "rows_per_gpu": M, "precision": args.precision,
+                "parallelism": f"row-shard x{world}",
+                "l2": "inputs larger than L2 (A+B+C = 768 MiB per GPU step), no flush",
+            },
+            "gpu_launches": int(launches),
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e_ms, "steps": args.e2e_steps,
+                    "entry_point": "gpu_execute_into (pinned host buffers)",
+                    "h2d_bytes_per_step": 4 * (M * K + K * N + M * N), "d2h_bytes_per_step": 4 * M * N},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic_from_profile(args.precision, M),
+                         "peak_source": peak_src, "kernel_ms": per_launch_ms},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+            "cublas_tf32_tflops_same_shape": cublas,
+            "result_check_rel_err": rel,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    rank, local_rank, world = env_rank()
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    return ours_arm(args, rank, local_rank, world)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,222 @@
+/*
+ * minixla_b200 -- a B200 (sm_100a) backend for MiniXLA's OP_FUSED hot path.
+ *
+ * libminixla_b200.so is a drop-in replacement for MiniXLA's gpu_exec.c +
+ * runtime.c + ptx.c.  A MiniXLA program keeps building its graph with the
+ * reference's own tensor.c / graph.c / optimizer.c and links this library in
+ * place of those three GPU files; it can keep including the reference's
+ * gpu_exec.h / runtime.h unchanged.  Include this header (after the
+ * reference's headers, if both are used) only for the additive API below.
+ *
+ * Conventions kept from the reference (gpu_exec.c:63-69, 240-248, 547-549):
+ * failures return NULL or -1.0 and print one line to stderr; nothing aborts;
+ * every device buffer is released on every path; calls are synchronous
+ * (the result is on the host when the call returns); a GpuCtx is used from
+ * one host thread.
+ */
+#ifndef MINIXLA_B200_H
+#define MINIXLA_B200_H
+
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define MXB_API __attribute__((visibility("default")))
+#else
+#define MXB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------
+ * Host data model.  These are the reference's layouts, restated byte for
+ * byte because the library reads caller-built graphs in place:
+ *   Tensor  -- tensor.h:6-12
+ *   OpType  -- graph.h:6-15
+ *   EpStep  -- graph.h:17-18
+ *   Node    -- graph.h:20-31
+ * If the reference's tensor.h / graph.h were included first, their
+ * definitions are used instead (same include guards' presence is checked).
+ * ---------------------------------------------------------------------- */
+#if !defined(TENSOR_H) && !defined(MXB_TENSOR_DEFINED)
+#define MXB_TENSOR_DEFINED
+typedef struct {
+    float*  data;      /* row-major fp32, `size` elements; malloc'd        */
+    int*    shape;     /* ndim extents                                      */
+    size_t* strides;   /* ndim element strides (row-major)                  */
+    int     ndim;
+    size_t  size;      /* product of shape                                  */
+} Tensor;
+#endif
+
+#if !defined(GRAPH_H) && !defined(MXB_GRAPH_DEFINED)
+#define MXB_GRAPH_DEFINED
+typedef enum {
+    OP_INPUT,
+    OP_MATMUL,
+    OP_ADD,
+    OP_MUL,
+    OP_RELU,
+    OP_SOFTMAX,
+    OP_TRANSPOSE,
+    OP_FUSED
+} OpType;
+
+struct Node;
+typedef struct { OpType op; struct Node* operand; } EpStep;
+
+typedef struct Node {
+    OpType        op;
+    struct Node** inputs;      /* OP_FUSED: [A, B, ADD operands in step order] */
+    int           n_inputs;
+    Tensor*       output;      /* set on OP_INPUT leaves                       */
+    int           owns_output;
+    char          visited;
+    int           uses;
+    char          is_const;
+    EpStep*       epilogue;    /* OP_FUSED only: ADD(operand) / RELU steps     */
+    int           n_epilogue;
+} Node;
+#endif
+
+/* ------------------------------------------------------------------------
+ * The reference's GPU entry points, same signatures and ownership
+ * (gpu_exec.h:7-42, runtime.h:9).  Behavioural differences of this backend:
+ *  - kernels are hand-written sm_100a (tcgen05 / TMEM / TMA) CUDA, picked per
+ *    node signature; no PTX is generated or JIT-compiled;
+ *  - gpu_execute also accepts a bare OP_MATMUL, standalone OP_ADD / OP_RELU
+ *    nodes, and ADD operands of any size (a [N] bias row, or any operand by
+ *    eval_fused's modulo rule, graph.c:100-105), where the reference GPU path
+ *    refused them (gpu_exec.c:472-482, 515-518);
+ *  - precision: gpu_execute / gpu_time_kernel_ms / gpu_run_fused compute in
+ *    the context's precision mode (default 3xTF32, fp32-faithful);
+ *    gpu_run_tensorcore / gpu_time_kernel_tc_ms always use one TF32 product,
+ *    as the reference's tensor-core path does (ptx.c:352-595).
+ * ---------------------------------------------------------------------- */
+#ifndef GPU_EXEC_H
+typedef struct GpuCtx GpuCtx;
+
+/* Context on device 0 (or on $MINIXLA_DEVICE) -- gpu_exec.h:12-13. */
+MXB_API GpuCtx* gpu_ctx_create(void);
+/* Releases the context's streams, pooled device memory and kernels -- gpu_exec.h:14. */
+MXB_API void    gpu_ctx_destroy(GpuCtx* ctx);
+/* Runs the optimized DAG; returns a fresh host tensor for the root (caller
+ * frees it with free_tensor).  Does not modify the graph -- gpu_exec.h:16-20. */
+MXB_API Tensor* gpu_execute(Node* root, GpuCtx* ctx);
+/* Kernel-only timing of one OP_FUSED node: inputs uploaded once, `warmup`
+ * launches, then the minimum over `reps` CUDA-event-timed launches, in ms;
+ * -1.0 on failure -- gpu_exec.h:21-32. */
+MXB_API double  gpu_time_kernel_ms(Node* root, GpuCtx* ctx, int warmup, int reps);
+/* One OP_FUSED node through a single TF32 tensor-core product -- gpu_exec.h:34-39. */
+MXB_API Tensor* gpu_run_tensorcore(const Node* fused, GpuCtx* ctx);
+/* Kernel-only timing of the TF32 path -- gpu_exec.h:41-42. */
+MXB_API double  gpu_time_kernel_tc_ms(Node* root, GpuCtx* ctx, int warmup, int reps);
+#endif
+
+#ifndef RUNTIME_H
+/* Self-contained single-node run -- runtime.h:9.  `ptx` is accepted for ABI
+ * compatibility and ignored: the kernel is chosen from the node itself. */
+MXB_API Tensor* gpu_run_fused(const Node* fused, const char* ptx);
+#endif
+
+/* ------------------------------------------------------------------------
+ * Additive API (no counterpart in the reference).
+ * ---------------------------------------------------------------------- */
+
+/* Precision modes. */
+#define GPU_PRECISION_TF32    1   /* one TF32 product per k, fp32 accumulate        */
+#define GPU_PRECISION_3XTF32  3   /* x = big + small split, three TF32 products:
+                                     fp32-faithful results                          */
+
+/* Context on a given CUDA device (one process per GPU).  NULL on failure. */
+MXB_API GpuCtx* gpu_ctx_create_on(int device);
+/* Sets / reads the precision used by gpu_execute, gpu_time_kernel_ms and
+ * gpu_run_fused.  The initial mode comes from $MINIXLA_PRECISION ("tf32" or
+ * "3xtf32"), else 3xTF32.  Returns 0, or -1 for an unknown mode. */
+MXB_API int     gpu_ctx_set_precision(GpuCtx* ctx, int mode);
+MXB_API int     gpu_ctx_get_precision(const GpuCtx* ctx);
+/* Device index of the context, or -1. */
+MXB_API int     gpu_ctx_device(const GpuCtx* ctx);
+
+/* ---- Device-pointer entry points ----------------------------------------
+ * For callers that keep operands resident in HBM (benchmarks, frameworks):
+ * no host copies.  All pointers are device pointers of the context's device;
+ * `stream` is a cudaStream_t (NULL = the context's own stream).  Launches are
+ * asynchronous on that stream.  Return 0 on success, a negative MXB_E* code
+ * on failure (and one stderr line).
+ */
+enum {
+    MXB_EP_ADD_FULL = 0,  /* x += operand[i*ld + j]      (M x N operand, row pitch ld) */
+    MXB_EP_ADD_ROW  = 1,  /* x += operand[j]             ([N] bias row)                */
+    MXB_EP_ADD_MOD  = 2,  /* x += operand[(i*N + j) % size]  (eval_fused's rule)       */
+    MXB_EP_RELU     = 3,  /* x = x > 0 ? x : 0                                         */
+    MXB_EP_SCALE    = 4   /* x *= scale                                                */
+};
+#define MXB_MAX_EPILOGUE 16   /* the reference fuses at most 16 steps (optimizer.c:104-107) */
+
+typedef struct {
+    int          kind;       /* MXB_EP_*                                  */
+    int          reserved;
+    const float* operand;    /* ADD_*: device pointer                     */
+    long long    ld_or_size; /* ADD_FULL: row pitch; ADD_MOD: element count */
+    float        scale;      /* SCALE                                     */
+    int          reserved2;
+} mxb_ep_step;
+
+enum {
+    MXB_OK          = 0,
+    MXB_E_ARG       = -1,   /* bad shape / pointer / pitch / mode          */
+    MXB_E_CUDA      = -2,   /* a CUDA runtime call failed                  */
+    MXB_E_NOMEM     = -3,   /* device allocation failed                    */
+    MXB_E_TIMEOUT   = -4,   /* a bounded device-side wait ran out          */
+    MXB_E_UNSUPPORTED = -5  /* node or shape outside what the backend runs */
+};
+
+/* Like gpu_execute, but downloads the root into a caller-provided host
+ * tensor with the same element count (for example one backed by pinned
+ * memory, so the download runs at full link speed).  0 or an MXB_E_* code. */
+MXB_API int gpu_execute_into(Node* root, GpuCtx* ctx, Tensor* out);
+
+/* out[M,N] = epi(A[M,K] @ B[K,N]).  Row pitches lda, ldb, ldo in elements.
+ * A and B must be 16-byte aligned with lda % 4 == 0 and ldb % 4 == 0 (TMA);
+ * other shapes go through gpu_execute, which pads.  precision is
+ * GPU_PRECISION_TF32 or GPU_PRECISION_3XTF32 (3xTF32 uses pooled workspace
+ * from the context).  n_steps <= MXB_MAX_EPILOGUE. */
+MXB_API int mxb_fused_gemm(GpuCtx* ctx,
+                   const float* A, long long lda,
+                   const float* B, long long ldb,
+                   float* out, long long ldo,
+                   int M, int N, int K,
+                   const mxb_ep_step* steps, int n_steps,
+                   int precision, void* stream);
+
+/* Standalone element-wise nodes (tensor.c:64-86 and 110-120 semantics):
+ * out[i] = a[i] + b[i % b_size]  and  out[i] = x[i] > 0 ? x[i] : 0. */
+MXB_API int mxb_add(GpuCtx* ctx, const float* a, long long n, const float* b, long long b_size,
+            float* out, void* stream);
+MXB_API int mxb_relu(GpuCtx* ctx, const float* x, long long n, float* out, void* stream);
+
+/* Synchronises the context's device work and reports a device-side error
+ * recorded by a kernel (MXB_E_TIMEOUT after a bounded wait ran out), then
+ * clears it.  0 when clean. */
+MXB_API int mxb_check_device_error(GpuCtx* ctx);
+
+/* Test hook for the failure path: launches a kernel that waits, with a limit
+ * of `timeout_ns`, on a barrier that nothing completes; the kernel records
+ * MXB_E_TIMEOUT and returns, leaving the context usable.  Returns the status
+ * the host read back (MXB_E_TIMEOUT expected). */
+MXB_API int mxb_selftest_wait_timeout(GpuCtx* ctx, unsigned long long timeout_ns);
+
+/* Number of kernels this library has launched in this process (all
+ * contexts); used by benchmarks to report launches in a timed region. */
+MXB_API unsigned long long mxb_launch_count(void);
+
+/* Short description of the last failure on this thread ("" if none). */
+MXB_API const char* mxb_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MINIXLA_B200_H */

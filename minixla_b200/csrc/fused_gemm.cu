@@ -1,0 +1,505 @@
+// Fused GEMM + element-wise epilogue for sm_100a:  out = epi(A @ B), fp32 in/out.
+//
+// This is the kernel behind an OP_FUSED node (graph.c:32-52 builds the node,
+// eval_fused at graph.c:64-115 defines its value).  Design:
+//
+//  * Persistent CTAs, one per SM (grid = min(tiles, SMs)), each walking a
+//    grouped tile order so concurrently running tiles share A row-blocks and
+//    B column-blocks in L2.
+//  * Output tile 128 x BN.  k advances in blocks of 32 fp32 = one 128-byte
+//    swizzle row, staged in a STAGES-deep shared-memory ring by TMA:
+//      A box [128 rows][32 k]     K-major, SWIZZLE_128B  (16 KiB)
+//      B boxes [32 k][32 n] x BN/32, MN-major, SWIZZLE_128B (4 KiB each)
+//    B is consumed MN-major straight from its row-major [K, N] layout, so no
+//    transpose pass exists anywhere.
+//  * Warp roles (192 threads):
+//      warp 0      one thread issues the TMA loads
+//      warp 1      allocates TMEM; one thread issues tcgen05.mma (kind::tf32,
+//                  M=128, N=BN, K=8) into an fp32 accumulator in TMEM
+//      warps 2..5  epilogue: tcgen05.ld the accumulator (warp w reads TMEM
+//                  lanes 32*(w%4)..+31, i.e. one output row per thread),
+//                  apply the node's epilogue steps in order, store once.
+//    TMEM holds two accumulators (2*BN columns) so the epilogue of tile i
+//    overlaps the main loop of tile i+1.
+//  * 3xTF32 mode: the host splits A and B into tf32-exact high parts and
+//    the low remainders; per k-step the MMA warp issues
+//    big*big + big*small + small*big into the same accumulator.
+//  * Every mbarrier wait is bounded (global-timer limit).  A wait that runs
+//    out records an error bit in global memory, raises a CTA-wide abort flag,
+//    waits (bounded) for its own copies / MMAs in flight, frees TMEM and
+//    returns; the host reports MXB_E_TIMEOUT.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdio>
+#include <mutex>
+
+#include "internal.h"
+#include "sm100_ptx.cuh"
+
+namespace mxb {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 32;           // fp32 elements per 128-byte swizzle row
+constexpr int kThreads = 192;
+constexpr int kBoxBytes = 32 * 32 * 4;  // one B box: 32 k-rows x 128 bytes
+
+struct FusedParams {
+    float* out;
+    long long ldo;
+    int M, N, K;
+    int n_steps;
+    int tiles_m, tiles_n, num_tiles, num_kb;
+    int group_m;
+    int pad;
+    unsigned long long timeout_ns;
+    int* err;
+    EpStepDev steps[MXB_MAX_EPILOGUE];
+};
+
+template <int BN, int STAGES, bool SPLIT3>
+struct Cfg {
+    static constexpr int kABytes = kBM * kBK * 4;
+    static constexpr int kBBytes = BN * kBK * 4;
+    static constexpr int kOperandBytes = kABytes + kBBytes;
+    static constexpr int kStageBytes = (SPLIT3 ? 2 : 1) * kOperandBytes;
+    static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kBarOffset = STAGES * kStageBytes;
+    static constexpr int kNumBars = 2 * STAGES + 5;
+    static constexpr int kSmemBytes = 1024 + kBarOffset + kNumBars * 8 + 16;
+    static_assert(kStageBytes % 1024 == 0, "stages must keep 1 KiB swizzle alignment");
+    static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+    static_assert(kTmemCols == 64 || kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512,
+                  "TMEM allocation must be a power of two >= 32 columns");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+// Error bits written to the device error word.
+enum : int { kErrProducer = 1, kErrMma = 2, kErrEpilogue = 4, kErrProbe = 8 };
+
+__device__ __forceinline__ void tile_coords(int t, const FusedParams& p, int& mb, int& nb) {
+    // Groups of group_m row-blocks; inside a group the row-block varies fastest,
+    // so a wave of CTAs covers a compact group_m x (wave/group_m) patch.
+    const int group_tiles = p.group_m * p.tiles_n;
+    const int g = t / group_tiles;
+    const int first_m = g * p.group_m;
+    const int gm = min(p.tiles_m - first_m, p.group_m);
+    const int r = t - g * group_tiles;
+    mb = first_m + r % gm;
+    nb = r / gm;
+}
+
+__device__ __forceinline__ void raise_error(const FusedParams& p, volatile int* abort_flag, int bit) {
+    atomicOr(p.err, bit);
+    *abort_flag = 1;
+}
+
+// Applies the node's epilogue steps, in order, to 32 consecutive outputs of
+// one row (cols col..col+31), exactly as eval_fused does per cell
+// (graph.c:98-109): ADD adds the operand element, RELU is x > 0 ? x : 0.
+__device__ __forceinline__ void apply_epilogue(float (&v)[32], int row, int col, bool row_ok,
+                                               const FusedParams& p) {
+    const bool full_cols = col + 32 <= p.N;
+    for (int s = 0; s < p.n_steps; ++s) {
+        const int kind = p.steps[s].kind;
+        const float* ptr = p.steps[s].ptr;
+        if (kind == MXB_EP_RELU) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = v[i] > 0.0f ? v[i] : 0.0f;
+        } else if (kind == MXB_EP_SCALE) {
+            const float sc = p.steps[s].scale;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = v[i] * sc;
+        } else if (kind == MXB_EP_ADD_FULL) {
+            if (!row_ok) continue;
+            const long long ld = p.steps[s].ld_or_size;
+            const float* src = ptr + static_cast<long long>(row) * ld + col;
+            if (full_cols && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+                const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float4 c = __ldcs(s4 + i);
+                    v[4 * i + 0] += c.x;
+                    v[4 * i + 1] += c.y;
+                    v[4 * i + 2] += c.z;
+                    v[4 * i + 3] += c.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (col + i < p.N) v[i] += __ldg(src + i);
+            }
+        } else if (kind == MXB_EP_ADD_ROW) {
+            const float* src = ptr + col;
+            if (full_cols && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+                const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float4 c = __ldg(s4 + i);
+                    v[4 * i + 0] += c.x;
+                    v[4 * i + 1] += c.y;
+                    v[4 * i + 2] += c.z;
+                    v[4 * i + 3] += c.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (col + i < p.N) v[i] += __ldg(src + i);
+            }
+        } else if (kind == MXB_EP_ADD_MOD) {
+            if (!row_ok) continue;
+            const unsigned long long size = static_cast<unsigned long long>(p.steps[s].ld_or_size);
+            const unsigned long long base =
+                static_cast<unsigned long long>(row) * static_cast<unsigned long long>(p.N) + col;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (col + i < p.N) v[i] += __ldg(ptr + (base + i) % size);
+        }
+    }
+}
+
+__device__ __forceinline__ void store_row_chunk(const float (&v)[32], int row, int col,
+                                                const FusedParams& p) {
+    float* dst = p.out + static_cast<long long>(row) * p.ldo + col;
+    if (col + 32 <= p.N && (p.ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            __stcs(d4 + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (col + i < p.N) dst[i] = v[i];
+    }
+}
+
+template <int BN, int STAGES, bool SPLIT3>
+__global__ void __launch_bounds__(kThreads, 1)
+    fused_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+                      const __grid_constant__ FusedParams p) {
+    using C = Cfg<BN, STAGES, SPLIT3>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t bar0 = smem_addr(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), 128);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+        if (SPLIT3) {
+            tma_prefetch_desc(&tmA2);
+            tma_prefetch_desc(&tmB2);
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_addr(tmem_slot), C::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            long long issued = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+                int mb, nb;
+                tile_coords(t, p, mb, nb);
+                const int m0 = mb * kBM, n0 = nb * BN;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (*abort_flag) { ok = false; break; }
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns)) {
+                        raise_error(p, abort_flag, kErrProducer);
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = smem + stage * C::kStageBytes;
+                    const uint32_t fb = full_bar(stage);
+                    mbar_arrive_expect_tx(fb, C::kStageBytes);
+                    const int k0 = kb * kBK;
+                    tma_load_2d(smem_addr(st), &tmA, fb, k0, m0);
+#pragma unroll
+                    for (int j = 0; j < BN / 32; ++j)
+                        tma_load_2d(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb, n0 + 32 * j, k0);
+                    if (SPLIT3) {
+                        uint8_t* st2 = st + C::kOperandBytes;
+                        tma_load_2d(smem_addr(st2), &tmA2, fb, k0, m0);
+#pragma unroll
+                        for (int j = 0; j < BN / 32; ++j)
+                            tma_load_2d(smem_addr(st2 + C::kABytes + j * kBoxBytes), &tmB2, fb,
+                                        n0 + 32 * j, k0);
+                    }
+                    ++issued;
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!ok) {
+                // Let the copies still in flight land before the CTA leaves.
+                const long long n = issued < STAGES ? issued : STAGES;
+                for (long long i = 1; i <= n; ++i) {
+                    const long long idx = issued - i;
+                    const int s = static_cast<int>(idx % STAGES);
+                    const uint32_t ph = static_cast<uint32_t>((idx / STAGES) & 1);
+                    mbar_wait(full_bar(s), ph, p.timeout_ns);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_tf32(kBM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+                if (*abort_flag) break;
+                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns)) {
+                    raise_error(p, abort_flag, kErrMma);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(full_bar(stage), phase, p.timeout_ns)) {
+                        raise_error(p, abort_flag, kErrMma);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_addr(smem + stage * C::kStageBytes);
+                    const uint32_t b_addr = a_addr + C::kABytes;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 8; ++kk) {
+                        // A: K-major, advance 8 fp32 = 32 bytes inside the swizzled row.
+                        const uint64_t da = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+                        // B: MN-major, advance one 8-k-row atom = 1024 bytes; 32-col boxes 4 KiB apart.
+                        const uint64_t db = smem_desc_sw128(b_addr + kk * 1024, kBoxBytes, 1024);
+                        mma_tf32(d_tmem, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
+                        if (SPLIT3) {
+                            const uint64_t da2 = smem_desc_sw128(a_addr + C::kOperandBytes + kk * 32, 16, 1024);
+                            const uint64_t db2 =
+                                smem_desc_sw128(b_addr + C::kOperandBytes + kk * 1024, kBoxBytes, 1024);
+                            mma_tf32(d_tmem, da, db2, idesc, 1u);
+                            mma_tf32(d_tmem, da2, db, idesc, 1u);
+                        }
+                    }
+                    mma_commit(empty_bar(stage));
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                mma_commit(tfull_bar(acc));
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            // All MMAs issued by this thread must finish before TMEM is freed.
+            mma_commit(drain_bar);
+            if (!mbar_wait(drain_bar, 0, p.timeout_ns)) raise_error(p, abort_flag, kErrMma);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+        const int row_in_tile = quad * 32 + lane;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+            const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
+            if (stop) break;
+            const bool got = mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns);
+            if (!__all_sync(0xffffffffu, got)) {
+                if (lane == 0) raise_error(p, abort_flag, kErrEpilogue);
+                break;
+            }
+            tc_fence_after();
+            int mb, nb;
+            tile_coords(t, p, mb, nb);
+            const int row = mb * kBM + row_in_tile;
+            const bool row_ok = row < p.M;
+            const int col0 = nb * BN;
+            int chunks = (p.N - col0 + 31) / 32;
+            if (chunks > BN / 32) chunks = BN / 32;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN);
+            for (int c = 0; c < chunks; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(taddr + 32 * c, r);
+                tmem_ld_wait();
+                if (c == chunks - 1) {
+                    // Accumulator fully read: hand it back to the MMA warp.
+                    tc_fence_before();
+                    mbar_arrive(tempty_bar(acc));
+                }
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                const int col = col0 + 32 * c;
+                apply_epilogue(v, row, col, row_ok, p);
+                if (row_ok) store_row_chunk(v, row, col, p);
+            }
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// Row-major [rows, cols] fp32 with row pitch `ld` elements; box [box_rows][box_cols].
+bool make_map(CUtensorMap* map, const float* base, long long rows, long long cols, long long ld,
+              int box_cols, int box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES, bool SPLIT3>
+cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
+    using C = Cfg<BN, STAGES, SPLIT3>;
+    auto kernel = fused_gemm_kernel<BN, STAGES, SPLIT3>;
+    // The shared-memory opt-in is per device: remember which devices have it.
+    static std::mutex mu;
+    static uint64_t configured = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (dev >= 64 || !(configured & (1ull << dev))) {
+            e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+            if (e != cudaSuccess) return e;
+            if (dev < 64) configured |= 1ull << dev;
+        }
+    }
+
+    const float* a_hi = SPLIT3 ? g.A_big : g.A;
+    const float* b_hi = SPLIT3 ? g.B_big : g.B;
+    CUtensorMap mA, mB, mA2, mB2;
+    if (!make_map(&mA, a_hi, g.M, g.K, g.lda, kBK, kBM) || !make_map(&mB, b_hi, g.K, g.N, g.ldb, 32, kBK))
+        return cudaErrorInvalidValue;
+    if (SPLIT3) {
+        if (!make_map(&mA2, g.A_small, g.M, g.K, g.lda, kBK, kBM) ||
+            !make_map(&mB2, g.B_small, g.K, g.N, g.ldb, 32, kBK))
+            return cudaErrorInvalidValue;
+    } else {
+        mA2 = mA;
+        mB2 = mB;
+    }
+
+    FusedParams p{};
+    p.out = g.out;
+    p.ldo = g.ldo;
+    p.M = g.M;
+    p.N = g.N;
+    p.K = g.K;
+    p.n_steps = g.n_steps;
+    p.tiles_m = (g.M + kBM - 1) / kBM;
+    p.tiles_n = (g.N + BN - 1) / BN;
+    p.num_tiles = p.tiles_m * p.tiles_n;
+    p.num_kb = (g.K + kBK - 1) / kBK;
+    p.group_m = 16;
+    p.timeout_ns = g.timeout_ns;
+    p.err = g.err;
+    for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
+
+    const int grid = p.num_tiles < g.num_sms ? p.num_tiles : g.num_sms;
+    kernel<<<grid, kThreads, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p);
+    note_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
+    if (g.precision == GPU_PRECISION_3XTF32) return run_variant<128, 3, true>(g, stream);
+    // One TF32 product.  Narrow or small problems use 128-wide tiles so more SMs get work.
+    const long long tiles_m = (g.M + kBM - 1) / kBM;
+    const long long tiles256 = tiles_m * ((g.N + 255) / 256);
+    const long long tiles128 = tiles_m * ((g.N + 127) / 128);
+    if (g.N <= 128 || (tiles256 < g.num_sms && tiles128 > tiles256)) return run_variant<128, 6, false>(g, stream);
+    return run_variant<256, 4, false>(g, stream);
+}
+
+// ------------------------------------------------------------------ bounded-wait probe
+
+namespace {
+__global__ void wait_timeout_probe_kernel(int* err, unsigned long long timeout_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_addr(&bar), 1);
+        fence_barrier_init();
+        // Nothing ever arrives on this barrier: the wait must give up by itself.
+        if (!mbar_wait(smem_addr(&bar), 0, timeout_ns)) atomicOr(err, kErrProbe);
+    }
+}
+}  // namespace
+
+cudaError_t launch_wait_timeout_probe(int* err, unsigned long long timeout_ns, cudaStream_t stream) {
+    wait_timeout_probe_kernel<<<1, 32, 0, stream>>>(err, timeout_ns);
+    note_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace mxb

@@ -1,0 +1,56 @@
+// Internal declarations shared by the library's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <cstddef>
+
+#include "../../include/minixla_b200.h"
+
+namespace mxb {
+
+// Device-side copy of one epilogue step; byte-identical to mxb_ep_step.
+struct EpStepDev {
+    int kind;
+    int reserved;
+    const float* ptr;
+    long long ld_or_size;
+    float scale;
+    int reserved2;
+};
+static_assert(sizeof(EpStepDev) == sizeof(mxb_ep_step), "EpStepDev must mirror mxb_ep_step");
+
+// Everything a fused-GEMM launch needs besides the tensor maps.
+struct GemmLaunch {
+    const float* A; long long lda;     // M x K, lda % 4 == 0
+    const float* B; long long ldb;     // K x N, ldb % 4 == 0
+    const float* A_small;              // 3xTF32 only: low parts, same pitches
+    const float* B_small;
+    const float* A_big;                // 3xTF32 only: tf32-exact high parts
+    const float* B_big;
+    float* out; long long ldo;
+    int M, N, K;
+    const EpStepDev* steps; int n_steps;
+    int precision;                     // GPU_PRECISION_TF32 / GPU_PRECISION_3XTF32
+    int* err;                          // device error word
+    unsigned long long timeout_ns;
+    int num_sms;
+};
+
+// Kernel launchers (fused_gemm.cu, elementwise.cu).  Return cudaError_t.
+cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream);
+cudaError_t launch_split_tf32(const float* x, long long rows, long long cols, long long ld_in,
+                              float* big, float* small, long long ld_out, int num_sms,
+                              cudaStream_t stream);
+cudaError_t launch_add(const float* a, long long n, const float* b, long long b_size, float* out,
+                       int num_sms, cudaStream_t stream);
+cudaError_t launch_relu(const float* x, long long n, float* out, int num_sms, cudaStream_t stream);
+cudaError_t launch_wait_timeout_probe(int* err, unsigned long long timeout_ns, cudaStream_t stream);
+
+// Process-wide count of kernel launches issued by this library.
+void note_launch(unsigned n = 1);
+
+// Records a failure message for mxb_last_error() and prints it to stderr.
+void set_error(const char* fmt, ...);
+
+}  // namespace mxb

@@ -1,0 +1,1015 @@
+// Host runtime behind the C ABI: GpuCtx, a caching device pool, the DAG
+// executor (gpu_execute) and the kernel-only timers.
+//
+// Replaces gpu_exec.c / runtime.c of gouthamk16/miniXLA:
+//  - gpu_exec.c:57-93   GpuCtx create/destroy  -> GpuCtx below (runtime API,
+//                       one non-blocking stream, device pool, error word)
+//  - gpu_exec.c:34-53   PTX-string module cache -> none needed: kernels are
+//                       compiled sm_100a code, chosen by node signature
+//  - gpu_exec.c:419-551 gpu_execute -> execute_graph(): topological order,
+//                       last-use release into the pool (not cuMemFree), all
+//                       work stream-ordered, one synchronise before download
+//  - gpu_exec.c:327-410, 251-323 kernel-only timers -> time_fused()
+//  - runtime.c:16-128   gpu_run_fused -> run_single()
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+#include <unordered_set>
+#include <vector>
+
+#include "internal.h"
+
+// ---------------------------------------------------------------- ABI checks
+// The library reads caller-built Tensor / Node / EpStep structs in place, so
+// their layout must be the reference's (tensor.h:6-12, graph.h:17-31) on LP64.
+static_assert(sizeof(Tensor) == 40, "Tensor layout");
+static_assert(offsetof(Tensor, data) == 0 && offsetof(Tensor, shape) == 8 &&
+                  offsetof(Tensor, strides) == 16 && offsetof(Tensor, ndim) == 24 &&
+                  offsetof(Tensor, size) == 32,
+              "Tensor field offsets");
+static_assert(sizeof(EpStep) == 16 && offsetof(EpStep, operand) == 8, "EpStep layout");
+static_assert(sizeof(Node) == 64, "Node layout");
+static_assert(offsetof(Node, inputs) == 8 && offsetof(Node, n_inputs) == 16 &&
+                  offsetof(Node, output) == 24 && offsetof(Node, owns_output) == 32 &&
+                  offsetof(Node, visited) == 36 && offsetof(Node, uses) == 40 &&
+                  offsetof(Node, is_const) == 44 && offsetof(Node, epilogue) == 48 &&
+                  offsetof(Node, n_epilogue) == 56,
+              "Node field offsets");
+
+namespace mxb {
+
+// ---------------------------------------------------------------- errors, counters
+
+static std::atomic<unsigned long long> g_launches{0};
+static thread_local std::string t_last_error;
+
+void note_launch(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+void set_error(const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    fprintf(stderr, "minixla_b200: %s\n", buf);
+}
+
+static bool cuda_ok(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return true;
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return false;
+}
+
+// ---------------------------------------------------------------- device pool
+//
+// Size-class free lists.  A released block carries an event recorded on the
+// stream that last used it; handing it to a different stream makes that
+// stream wait on the event, so reuse is always stream-ordered.  A failed
+// cudaMalloc first returns every cached block to the driver and retries.
+// MINIXLA_FAIL_ALLOC_AT=n makes the n-th pool allocation of the process fail
+// (host-side fault injection for the out-of-memory path).
+
+static std::atomic<long long> g_alloc_calls{0};
+
+class DevicePool {
+  public:
+    explicit DevicePool(int device) : device_(device) {}
+    ~DevicePool() {
+        trim();
+        for (auto& kv : live_) cudaFree(kv.first);
+        for (cudaEvent_t e : spare_events_) cudaEventDestroy(e);
+    }
+
+    void* alloc(size_t bytes, cudaStream_t stream) {
+        const long long call = g_alloc_calls.fetch_add(1) + 1;
+        if (const char* fail = getenv("MINIXLA_FAIL_ALLOC_AT")) {
+            if (atoll(fail) == call) {
+                set_error("device allocation of %zu bytes failed (injected by MINIXLA_FAIL_ALLOC_AT)", bytes);
+                return nullptr;
+            }
+        }
+        const size_t cls = size_class(bytes);
+        auto it = free_.find(cls);
+        if (it != free_.end() && !it->second.empty()) {
+            Cached c = it->second.back();
+            it->second.pop_back();
+            cached_bytes_ -= cls;
+            if (c.stream != stream) cudaStreamWaitEvent(stream, c.ready, 0);
+            spare_events_.push_back(c.ready);
+            live_[c.ptr] = cls;
+            return c.ptr;
+        }
+        void* p = nullptr;
+        if (cudaMalloc(&p, cls) != cudaSuccess) {
+            cudaGetLastError();
+            trim();
+            if (cudaMalloc(&p, cls) != cudaSuccess) {
+                cudaGetLastError();
+                set_error("device allocation of %zu bytes failed", cls);
+                return nullptr;
+            }
+        }
+        live_[p] = cls;
+        return p;
+    }
+
+    void release(void* p, cudaStream_t stream) {
+        if (!p) return;
+        auto it = live_.find(p);
+        if (it == live_.end()) return;
+        const size_t cls = it->second;
+        live_.erase(it);
+        cudaEvent_t ev = take_event();
+        if (ev) cudaEventRecord(ev, stream);
+        free_[cls].push_back(Cached{p, stream, ev});
+        cached_bytes_ += cls;
+        if (!ev) {  // could not make an event: fall back to a full sync before reuse
+            cudaStreamSynchronize(stream);
+        }
+    }
+
+    void trim() {
+        for (auto& kv : free_) {
+            for (Cached& c : kv.second) {
+                if (c.ready) {
+                    cudaEventSynchronize(c.ready);
+                    spare_events_.push_back(c.ready);
+                }
+                cudaFree(c.ptr);
+            }
+            kv.second.clear();
+        }
+        cached_bytes_ = 0;
+    }
+
+    size_t live_bytes() const {
+        size_t s = 0;
+        for (auto& kv : live_) s += kv.second;
+        return s;
+    }
+    size_t cached_bytes() const { return cached_bytes_; }
+
+  private:
+    struct Cached {
+        void* ptr;
+        cudaStream_t stream;
+        cudaEvent_t ready;
+    };
+
+    static size_t size_class(size_t bytes) {
+        if (bytes == 0) bytes = 1;
+        if (bytes <= (1u << 20)) return (bytes + 511) & ~static_cast<size_t>(511);
+        const size_t mb2 = static_cast<size_t>(2) << 20;
+        return (bytes + mb2 - 1) / mb2 * mb2;
+    }
+
+    cudaEvent_t take_event() {
+        if (!spare_events_.empty()) {
+            cudaEvent_t e = spare_events_.back();
+            spare_events_.pop_back();
+            return e;
+        }
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        return e;
+    }
+
+    int device_;
+    std::unordered_map<size_t, std::vector<Cached>> free_;
+    std::unordered_map<void*, size_t> live_;
+    std::vector<cudaEvent_t> spare_events_;
+    size_t cached_bytes_ = 0;
+};
+
+// Keeps the caller's current device and restores it on scope exit.
+struct DeviceScope {
+    int prev = -1;
+    explicit DeviceScope(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) {
+            cudaGetLastError();
+            prev = -1;
+        }
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceScope() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace mxb
+
+using mxb::cuda_ok;
+using mxb::set_error;
+
+struct GpuCtx {
+    int device = 0;
+    int num_sms = 148;
+    int precision = GPU_PRECISION_3XTF32;
+    unsigned long long timeout_ns = 5ull * 1000 * 1000 * 1000;
+    cudaStream_t stream = nullptr;
+    int* d_err = nullptr;
+    mxb::DevicePool* pool = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+};
+
+namespace mxb {
+
+// ---------------------------------------------------------------- graph analysis
+
+struct Info {
+    const Node* node = nullptr;
+    std::vector<int> dims;        // logical output shape
+    long long size = 0;           // element count
+    int last_use = -1;            // index of the last consumer in topo order
+    float* dev = nullptr;         // device buffer (compact, row-major)
+};
+
+// Post-order DFS over inputs: every node after all of its inputs
+// (graph.c:171-190 defines the same order; this copy does not touch the
+// nodes' `visited` flags, so the caller's graph is never written).
+static std::vector<const Node*> topo_order(const Node* root) {
+    std::vector<const Node*> order;
+    std::unordered_set<const Node*> seen;
+    std::vector<std::pair<const Node*, int>> stack;
+    stack.push_back({root, 0});
+    seen.insert(root);
+    while (!stack.empty()) {
+        auto& top = stack.back();
+        const Node* n = top.first;
+        if (top.second < n->n_inputs) {
+            const Node* in = n->inputs[top.second++];
+            if (in && seen.insert(in).second) stack.push_back({in, 0});
+        } else {
+            order.push_back(n);
+            stack.pop_back();
+        }
+    }
+    return order;
+}
+
+static bool same_dims(const std::vector<int>& a, const std::vector<int>& b) { return a == b; }
+
+// tensor_add's broadcast rule (tensor.c:57-63): b's shape is a trailing suffix of a's.
+static bool trailing_suffix(const std::vector<int>& a, const std::vector<int>& b) {
+    if (b.size() > a.size()) return false;
+    for (size_t i = 0; i < b.size(); ++i)
+        if (b[i] != a[a.size() - b.size() + i]) return false;
+    return true;
+}
+
+static long long product(const std::vector<int>& d) {
+    long long s = 1;
+    for (int x : d) s *= x;
+    return s;
+}
+
+// Fills dims/size for every node; false (with a message) for anything this
+// backend cannot run.
+static bool infer_shapes(const std::vector<const Node*>& order,
+                         std::unordered_map<const Node*, int>& index, std::vector<Info>& info) {
+    info.resize(order.size());
+    for (size_t i = 0; i < order.size(); ++i) {
+        const Node* n = order[i];
+        index[n] = static_cast<int>(i);
+        Info& f = info[i];
+        f.node = n;
+        switch (n->op) {
+            case OP_INPUT: {
+                const Tensor* t = n->output;
+                if (!t || !t->data || t->ndim <= 0 || !t->shape) {
+                    set_error("gpu_execute: OP_INPUT node without a host tensor");
+                    return false;
+                }
+                f.dims.assign(t->shape, t->shape + t->ndim);
+                f.size = static_cast<long long>(t->size);
+                if (f.size != product(f.dims)) {
+                    set_error("gpu_execute: input tensor size does not match its shape");
+                    return false;
+                }
+                break;
+            }
+            case OP_FUSED:
+            case OP_MATMUL: {
+                if (n->n_inputs < 2 || !n->inputs[0] || !n->inputs[1]) {
+                    set_error("gpu_execute: matmul node needs two inputs");
+                    return false;
+                }
+                const Info& a = info[index.at(n->inputs[0])];
+                const Info& b = info[index.at(n->inputs[1])];
+                if (a.dims.size() != 2 || b.dims.size() != 2) {
+                    set_error("gpu_execute: only 2-D matmul operands run on the GPU (got rank %zu x %zu)",
+                              a.dims.size(), b.dims.size());
+                    return false;
+                }
+                if (a.dims[1] != b.dims[0]) {
+                    set_error("gpu_execute: incompatible matmul operand shapes [%d,%d] x [%d,%d]", a.dims[0],
+                              a.dims[1], b.dims[0], b.dims[1]);
+                    return false;
+                }
+                f.dims = {a.dims[0], b.dims[1]};
+                f.size = static_cast<long long>(a.dims[0]) * b.dims[1];
+                if (n->op == OP_FUSED) {
+                    if (n->n_epilogue > MXB_MAX_EPILOGUE) {
+                        set_error("gpu_execute: %d epilogue steps exceed the limit of %d", n->n_epilogue,
+                                  MXB_MAX_EPILOGUE);
+                        return false;
+                    }
+                    for (int e = 0; e < n->n_epilogue; ++e) {
+                        const EpStep& s = n->epilogue[e];
+                        if (s.op == OP_ADD && (!s.operand || !index.count(s.operand))) {
+                            set_error("gpu_execute: ADD epilogue operand is not an input of its fused node");
+                            return false;
+                        }
+                    }
+                }
+                break;
+            }
+            case OP_ADD: {
+                if (n->n_inputs != 2) {
+                    set_error("gpu_execute: add node needs two inputs");
+                    return false;
+                }
+                const Info& a = info[index.at(n->inputs[0])];
+                const Info& b = info[index.at(n->inputs[1])];
+                if (!same_dims(a.dims, b.dims) && !trailing_suffix(a.dims, b.dims)) {
+                    set_error("gpu_execute: add operand shape must match, or be a trailing suffix of, the first");
+                    return false;
+                }
+                f.dims = a.dims;
+                f.size = a.size;
+                break;
+            }
+            case OP_RELU: {
+                if (n->n_inputs != 1) {
+                    set_error("gpu_execute: relu node needs one input");
+                    return false;
+                }
+                const Info& a = info[index.at(n->inputs[0])];
+                f.dims = a.dims;
+                f.size = a.size;
+                break;
+            }
+            default:
+                set_error("gpu_execute: op %d is not supported on the GPU (supported: input, fused, matmul, "
+                          "add, relu)",
+                          static_cast<int>(n->op));
+                return false;
+        }
+    }
+    for (size_t j = 0; j < order.size(); ++j) {
+        const Node* n = order[j];
+        for (int a = 0; a < n->n_inputs; ++a) {
+            auto it = index.find(n->inputs[a]);
+            if (it != index.end() && static_cast<int>(j) > info[it->second].last_use)
+                info[it->second].last_use = static_cast<int>(j);
+        }
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------- GEMM dispatch
+
+// Device operand of a fused GEMM, with its row pitch; `owned` buffers are
+// temporaries to hand back to the pool after the launch.
+struct Operand {
+    const float* ptr = nullptr;
+    long long ld = 0;
+    float* owned = nullptr;
+};
+
+// TMA needs 16-byte row pitches: a matrix whose width is not a multiple of 4
+// is copied into a pitch-padded temporary (one strided device copy).
+static bool tma_operand(GpuCtx* ctx, const float* src, long long rows, long long cols, Operand& op,
+                        cudaStream_t stream) {
+    if (cols % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        op.ptr = src;
+        op.ld = cols;
+        return true;
+    }
+    const long long ld = (cols + 3) / 4 * 4;
+    float* tmp = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(rows * ld) * 4, stream));
+    if (!tmp) return false;
+    if (!cuda_ok(cudaMemcpy2DAsync(tmp, ld * 4, src, cols * 4, cols * 4, rows, cudaMemcpyDeviceToDevice,
+                                   stream),
+                 "pitch-padding copy")) {
+        ctx->pool->release(tmp, stream);
+        return false;
+    }
+    op.ptr = tmp;
+    op.ld = ld;
+    op.owned = tmp;
+    return true;
+}
+
+// Launches epi(A @ B) with already-validated, TMA-ready operands.  For
+// 3xTF32 the high/low split of A and B goes to pooled workspace first.
+static int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
+                       long long ldo, int M, int N, int K, const EpStepDev* steps, int n_steps, int precision,
+                       cudaStream_t stream) {
+    GemmLaunch g{};
+    g.A = A;
+    g.lda = lda;
+    g.B = B;
+    g.ldb = ldb;
+    g.out = out;
+    g.ldo = ldo;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.steps = steps;
+    g.n_steps = n_steps;
+    g.precision = precision;
+    g.err = ctx->d_err;
+    g.timeout_ns = ctx->timeout_ns;
+    g.num_sms = ctx->num_sms;
+    float* ws[4] = {nullptr, nullptr, nullptr, nullptr};
+    int rc = MXB_OK;
+    if (precision == GPU_PRECISION_3XTF32) {
+        const size_t a_bytes = static_cast<size_t>(M) * lda * 4, b_bytes = static_cast<size_t>(K) * ldb * 4;
+        ws[0] = static_cast<float*>(ctx->pool->alloc(a_bytes, stream));
+        ws[1] = ws[0] ? static_cast<float*>(ctx->pool->alloc(a_bytes, stream)) : nullptr;
+        ws[2] = ws[1] ? static_cast<float*>(ctx->pool->alloc(b_bytes, stream)) : nullptr;
+        ws[3] = ws[2] ? static_cast<float*>(ctx->pool->alloc(b_bytes, stream)) : nullptr;
+        if (!ws[3]) {
+            rc = MXB_E_NOMEM;
+        } else if (!cuda_ok(launch_split_tf32(A, M, K, lda, ws[0], ws[1], lda, ctx->num_sms, stream),
+                            "split A") ||
+                   !cuda_ok(launch_split_tf32(B, K, N, ldb, ws[2], ws[3], ldb, ctx->num_sms, stream),
+                            "split B")) {
+            rc = MXB_E_CUDA;
+        } else {
+            g.A_big = ws[0];
+            g.A_small = ws[1];
+            g.B_big = ws[2];
+            g.B_small = ws[3];
+        }
+    }
+    if (rc == MXB_OK && !cuda_ok(launch_fused_gemm(g, stream), "fused GEMM launch")) rc = MXB_E_CUDA;
+    for (float* w : ws) ctx->pool->release(w, stream);
+    return rc;
+}
+
+// Builds the device epilogue of an OP_FUSED node from its EpSteps
+// (graph.h:17-18): ADD operands become FULL (same element count as the
+// output: flat index i*N+j of the compact operand), ROW ([N]: index j) or
+// MOD (any other size, eval_fused's modulo rule, graph.c:100-105); RELU maps
+// to RELU; other step ops are skipped, as eval_fused skips them.
+static int build_epilogue(const Node* n, int N, long long MN,
+                          const std::unordered_map<const Node*, const float*>& dev_of,
+                          const std::unordered_map<const Node*, long long>& size_of, EpStepDev* out) {
+    int k = 0;
+    for (int e = 0; e < n->n_epilogue; ++e) {
+        const EpStep& s = n->epilogue[e];
+        EpStepDev d{};
+        if (s.op == OP_ADD) {
+            const long long sz = size_of.at(s.operand);
+            d.ptr = dev_of.at(s.operand);
+            if (sz == MN) {
+                d.kind = MXB_EP_ADD_FULL;
+                d.ld_or_size = N;
+            } else if (sz == N) {
+                d.kind = MXB_EP_ADD_ROW;
+                d.ld_or_size = N;
+            } else {
+                d.kind = MXB_EP_ADD_MOD;
+                d.ld_or_size = sz;
+            }
+        } else if (s.op == OP_RELU) {
+            d.kind = MXB_EP_RELU;
+        } else {
+            continue;
+        }
+        out[k++] = d;
+    }
+    return k;
+}
+
+// Runs one matmul-anchored node on device buffers.
+static int run_gemm_node(GpuCtx* ctx, const Node* n, const float* dA, int M, int K, const float* dB, int N,
+                         float* dOut, const std::unordered_map<const Node*, const float*>& dev_of,
+                         const std::unordered_map<const Node*, long long>& size_of, int precision,
+                         cudaStream_t stream) {
+    EpStepDev steps[MXB_MAX_EPILOGUE];
+    const int n_steps =
+        n->op == OP_FUSED ? build_epilogue(n, N, static_cast<long long>(M) * N, dev_of, size_of, steps) : 0;
+    Operand a, b;
+    int rc = MXB_OK;
+    if (!tma_operand(ctx, dA, M, K, a, stream) || !tma_operand(ctx, dB, K, N, b, stream)) {
+        rc = MXB_E_NOMEM;
+    } else {
+        rc = launch_gemm(ctx, a.ptr, a.ld, b.ptr, b.ld, dOut, N, M, N, K, steps, n_steps, precision, stream);
+    }
+    ctx->pool->release(a.owned, stream);
+    ctx->pool->release(b.owned, stream);
+    return rc;
+}
+
+// Synchronises the context stream and folds a device-side error word into a code.
+static int finish(GpuCtx* ctx) {
+    if (!cuda_ok(cudaStreamSynchronize(ctx->stream), "stream synchronize")) return MXB_E_CUDA;
+    int err = 0;
+    if (!cuda_ok(cudaMemcpy(&err, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost), "error word read"))
+        return MXB_E_CUDA;
+    if (err) {
+        cudaMemset(ctx->d_err, 0, sizeof(int));
+        set_error("a device-side wait ran out of time (error bits 0x%x); results discarded", err);
+        return MXB_E_TIMEOUT;
+    }
+    return MXB_OK;
+}
+
+static Tensor* new_host_tensor(const std::vector<int>& dims) {
+    // Same allocation pattern as create_tensor (tensor.c:8-53), so the caller
+    // releases the result with the reference's free_tensor.
+    Tensor* t = static_cast<Tensor*>(calloc(1, sizeof(Tensor)));
+    if (!t) return nullptr;
+    t->ndim = static_cast<int>(dims.size());
+    t->shape = static_cast<int*>(malloc(dims.size() * sizeof(int)));
+    t->strides = static_cast<size_t*>(malloc(dims.size() * sizeof(size_t)));
+    size_t size = 1;
+    if (t->shape && t->strides) {
+        for (int i = t->ndim - 1; i >= 0; --i) {
+            t->shape[i] = dims[i];
+            t->strides[i] = size;
+            size *= static_cast<size_t>(dims[i]);
+        }
+    }
+    t->size = size;
+    t->data = static_cast<float*>(malloc(size * sizeof(float)));
+    if (!t->shape || !t->strides || !t->data) {
+        free(t->data);
+        free(t->shape);
+        free(t->strides);
+        free(t);
+        return nullptr;
+    }
+    return t;
+}
+
+// The DAG executor behind gpu_execute / gpu_execute_into.  When `dst` is
+// given the root is downloaded into it (its size must match), otherwise a
+// new host tensor is returned through *result.
+static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) {
+    if (!root || !ctx) {
+        set_error("gpu_execute: NULL root or context");
+        return MXB_E_ARG;
+    }
+    DeviceScope scope(ctx->device);
+    cudaStream_t stream = ctx->stream;
+    const std::vector<const Node*> order = topo_order(root);
+    std::unordered_map<const Node*, int> index;
+    std::vector<Info> info;
+    if (!infer_shapes(order, index, info)) return MXB_E_UNSUPPORTED;
+
+    std::unordered_map<const Node*, const float*> dev_of;
+    std::unordered_map<const Node*, long long> size_of;
+    int rc = MXB_OK;
+    for (size_t i = 0; i < order.size() && rc == MXB_OK; ++i) {
+        const Node* n = order[i];
+        Info& f = info[i];
+        f.dev = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(f.size) * 4, stream));
+        if (!f.dev) {
+            rc = MXB_E_NOMEM;
+            break;
+        }
+        dev_of[n] = f.dev;
+        size_of[n] = f.size;
+        switch (n->op) {
+            case OP_INPUT:
+                if (!cuda_ok(cudaMemcpyAsync(f.dev, n->output->data, static_cast<size_t>(f.size) * 4,
+                                             cudaMemcpyHostToDevice, stream),
+                             "input upload"))
+                    rc = MXB_E_CUDA;
+                break;
+            case OP_FUSED:
+            case OP_MATMUL: {
+                const Info& a = info[index.at(n->inputs[0])];
+                const Info& b = info[index.at(n->inputs[1])];
+                rc = run_gemm_node(ctx, n, a.dev, a.dims[0], a.dims[1], b.dev, b.dims[1], f.dev, dev_of, size_of,
+                                   ctx->precision, stream);
+                break;
+            }
+            case OP_ADD: {
+                const Info& a = info[index.at(n->inputs[0])];
+                const Info& b = info[index.at(n->inputs[1])];
+                if (!cuda_ok(launch_add(a.dev, a.size, b.dev, b.size, f.dev, ctx->num_sms, stream), "add launch"))
+                    rc = MXB_E_CUDA;
+                break;
+            }
+            case OP_RELU: {
+                const Info& a = info[index.at(n->inputs[0])];
+                if (!cuda_ok(launch_relu(a.dev, a.size, f.dev, ctx->num_sms, stream), "relu launch"))
+                    rc = MXB_E_CUDA;
+                break;
+            }
+            default:
+                rc = MXB_E_UNSUPPORTED;
+        }
+        if (rc != MXB_OK) break;
+        // Last-use release (gpu_exec.c:520-528), stream-ordered into the pool.
+        for (int a = 0; a < n->n_inputs; ++a) {
+            Info& in = info[index.at(n->inputs[a])];
+            if (in.last_use == static_cast<int>(i) && in.dev) {
+                ctx->pool->release(in.dev, stream);
+                in.dev = nullptr;
+            }
+        }
+    }
+
+    Info& r = info.back();  // the root is last in post-order
+    if (rc == MXB_OK) rc = finish(ctx);
+    if (rc == MXB_OK) {
+        if (dst) {
+            if (!dst->data || static_cast<long long>(dst->size) != r.size) {
+                set_error("gpu_execute_into: destination holds %zu elements, result has %lld",
+                          dst ? static_cast<size_t>(dst->size) : 0, r.size);
+                rc = MXB_E_ARG;
+            } else if (!cuda_ok(cudaMemcpyAsync(dst->data, r.dev, static_cast<size_t>(r.size) * 4,
+                                                cudaMemcpyDeviceToHost, stream),
+                                "result download") ||
+                       !cuda_ok(cudaStreamSynchronize(stream), "download synchronize")) {
+                rc = MXB_E_CUDA;
+            }
+        } else {
+            Tensor* t = new_host_tensor(r.dims);
+            if (!t) {
+                set_error("gpu_execute: host allocation of the result failed");
+                rc = MXB_E_NOMEM;
+            } else if (!cuda_ok(cudaMemcpyAsync(t->data, r.dev, static_cast<size_t>(r.size) * 4,
+                                                cudaMemcpyDeviceToHost, stream),
+                                "result download") ||
+                       !cuda_ok(cudaStreamSynchronize(stream), "download synchronize")) {
+                free(t->data);
+                free(t->shape);
+                free(t->strides);
+                free(t);
+                rc = MXB_E_CUDA;
+            } else {
+                *result = t;
+            }
+        }
+    }
+    for (Info& f : info) {
+        if (f.dev) ctx->pool->release(f.dev, stream);
+        f.dev = nullptr;
+    }
+    if (rc != MXB_OK) cudaStreamSynchronize(stream);
+    return rc;
+}
+
+// ---------------------------------------------------------------- single-node paths
+
+// Device copies of one fused node's operands, taken from the host tensors
+// hanging off its inputs (runtime.c:17-84 and gpu_exec.c:339-362 do the same).
+struct SingleNode {
+    int M = 0, N = 0, K = 0;
+    float *dA = nullptr, *dB = nullptr, *dOut = nullptr;
+    std::vector<float*> ops;
+    std::unordered_map<const Node*, const float*> dev_of;
+    std::unordered_map<const Node*, long long> size_of;
+
+    void release(GpuCtx* ctx) {
+        ctx->pool->release(dA, ctx->stream);
+        ctx->pool->release(dB, ctx->stream);
+        ctx->pool->release(dOut, ctx->stream);
+        for (float* p : ops) ctx->pool->release(p, ctx->stream);
+        dA = dB = dOut = nullptr;
+        ops.clear();
+    }
+};
+
+static float* upload(GpuCtx* ctx, const Tensor* t) {
+    float* d = static_cast<float*>(ctx->pool->alloc(t->size * 4, ctx->stream));
+    if (!d) return nullptr;
+    if (!cuda_ok(cudaMemcpyAsync(d, t->data, t->size * 4, cudaMemcpyHostToDevice, ctx->stream), "upload")) {
+        ctx->pool->release(d, ctx->stream);
+        return nullptr;
+    }
+    return d;
+}
+
+static int prepare_single(const Node* fused, GpuCtx* ctx, const char* who, SingleNode& s) {
+    if (!fused || !ctx) {
+        set_error("%s: NULL node or context", who);
+        return MXB_E_ARG;
+    }
+    if (fused->op != OP_FUSED && fused->op != OP_MATMUL) {
+        set_error("%s: node is not OP_FUSED", who);
+        return MXB_E_ARG;
+    }
+    const Tensor* a = fused->n_inputs >= 2 && fused->inputs[0] ? fused->inputs[0]->output : nullptr;
+    const Tensor* b = fused->n_inputs >= 2 && fused->inputs[1] ? fused->inputs[1]->output : nullptr;
+    if (!a || !b) {
+        set_error("%s: matmul operands need host tensors", who);
+        return MXB_E_ARG;
+    }
+    if (a->ndim != 2 || b->ndim != 2) {
+        set_error("%s: only 2D tensors supported", who);
+        return MXB_E_UNSUPPORTED;
+    }
+    if (a->shape[1] != b->shape[0]) {
+        set_error("%s: incompatible matmul operand shapes", who);
+        return MXB_E_ARG;
+    }
+    if (fused->op == OP_FUSED && fused->n_epilogue > MXB_MAX_EPILOGUE) {
+        set_error("%s: too many epilogue steps", who);
+        return MXB_E_UNSUPPORTED;
+    }
+    s.M = a->shape[0];
+    s.K = a->shape[1];
+    s.N = b->shape[1];
+    if (!(s.dA = upload(ctx, a)) || !(s.dB = upload(ctx, b))) return MXB_E_NOMEM;
+    if (fused->op == OP_FUSED) {
+        for (int e = 0; e < fused->n_epilogue; ++e) {
+            const EpStep& st = fused->epilogue[e];
+            if (st.op != OP_ADD) continue;
+            const Tensor* t = st.operand ? st.operand->output : nullptr;
+            if (!t || !t->data) {
+                set_error("%s: ADD epilogue operand needs a host tensor", who);
+                return MXB_E_ARG;
+            }
+            if (s.dev_of.count(st.operand)) continue;
+            float* d = upload(ctx, t);
+            if (!d) return MXB_E_NOMEM;
+            s.ops.push_back(d);
+            s.dev_of[st.operand] = d;
+            s.size_of[st.operand] = static_cast<long long>(t->size);
+        }
+    }
+    s.dOut = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(s.M) * s.N * 4, ctx->stream));
+    return s.dOut ? MXB_OK : MXB_E_NOMEM;
+}
+
+static Tensor* run_single(const Node* fused, GpuCtx* ctx, int precision, const char* who) {
+    DeviceScope scope(ctx ? ctx->device : 0);
+    SingleNode s;
+    Tensor* result = nullptr;
+    int rc = prepare_single(fused, ctx, who, s);
+    if (rc == MXB_OK)
+        rc = run_gemm_node(ctx, fused, s.dA, s.M, s.K, s.dB, s.N, s.dOut, s.dev_of, s.size_of, precision,
+                           ctx->stream);
+    if (rc == MXB_OK) rc = finish(ctx);
+    if (rc == MXB_OK) {
+        result = new_host_tensor({s.M, s.N});
+        if (!result ||
+            !cuda_ok(cudaMemcpy(result->data, s.dOut, static_cast<size_t>(s.M) * s.N * 4, cudaMemcpyDeviceToHost),
+                     "result download")) {
+            if (result) {
+                free(result->data);
+                free(result->shape);
+                free(result->strides);
+                free(result);
+            }
+            result = nullptr;
+        }
+    }
+    if (ctx) {
+        s.release(ctx);
+        cudaStreamSynchronize(ctx->stream);
+    }
+    return result;
+}
+
+// Kernel-only timing (gpu_exec.c:327-410): operands uploaded once, `warmup`
+// untimed launches each followed by a synchronise, then the minimum over
+// `reps` CUDA-event-timed launches on the context stream.  In 3xTF32 mode a
+// launch includes the operand split, which is part of that mode's work.
+static double time_fused(Node* root, GpuCtx* ctx, int warmup, int reps, int precision, const char* who) {
+    if (!root || !ctx || root->op != OP_FUSED) return -1.0;
+    if (root->n_inputs < 2 || !root->inputs[0]->output || !root->inputs[1]->output) return -1.0;
+    if (reps < 1) return -1.0;
+    DeviceScope scope(ctx->device);
+    SingleNode s;
+    double best = -1.0;
+    int rc = prepare_single(root, ctx, who, s);
+    if (rc == MXB_OK) {
+        for (int w = 0; w < warmup && rc == MXB_OK; ++w) {
+            rc = run_gemm_node(ctx, root, s.dA, s.M, s.K, s.dB, s.N, s.dOut, s.dev_of, s.size_of, precision,
+                               ctx->stream);
+            if (rc == MXB_OK) rc = finish(ctx);
+        }
+        double lo = 1e30;
+        for (int r = 0; r < reps && rc == MXB_OK; ++r) {
+            cudaEventRecord(ctx->ev0, ctx->stream);
+            rc = run_gemm_node(ctx, root, s.dA, s.M, s.K, s.dB, s.N, s.dOut, s.dev_of, s.size_of, precision,
+                               ctx->stream);
+            cudaEventRecord(ctx->ev1, ctx->stream);
+            if (rc == MXB_OK && cuda_ok(cudaEventSynchronize(ctx->ev1), "event synchronize")) {
+                float ms = 0.f;
+                cudaEventElapsedTime(&ms, ctx->ev0, ctx->ev1);
+                lo = std::min(lo, static_cast<double>(ms));
+            } else if (rc == MXB_OK) {
+                rc = MXB_E_CUDA;
+            }
+        }
+        if (rc == MXB_OK) rc = finish(ctx);
+        if (rc == MXB_OK) best = lo;
+    }
+    s.release(ctx);
+    cudaStreamSynchronize(ctx->stream);
+    return best;
+}
+
+static int precision_from_env() {
+    const char* p = getenv("MINIXLA_PRECISION");
+    if (!p) return GPU_PRECISION_3XTF32;
+    if (!strcmp(p, "tf32") || !strcmp(p, "TF32")) return GPU_PRECISION_TF32;
+    return GPU_PRECISION_3XTF32;
+}
+
+static bool valid_precision(int p) { return p == GPU_PRECISION_TF32 || p == GPU_PRECISION_3XTF32; }
+
+}  // namespace mxb
+
+// ================================================================== C ABI
+
+extern "C" {
+
+GpuCtx* gpu_ctx_create_on(int device) {
+    int count = 0;
+    if (!cuda_ok(cudaGetDeviceCount(&count), "cudaGetDeviceCount")) return nullptr;
+    if (device < 0 || device >= count) {
+        set_error("gpu_ctx_create: device %d out of range (%d devices)", device, count);
+        return nullptr;
+    }
+    mxb::DeviceScope scope(device);
+    cudaDeviceProp prop;
+    if (!cuda_ok(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties")) return nullptr;
+    if (prop.major != 10) {
+        set_error("gpu_ctx_create: device %d is sm_%d%d; this library carries sm_100a code only", device,
+                  prop.major, prop.minor);
+        return nullptr;
+    }
+    GpuCtx* g = new (std::nothrow) GpuCtx();
+    if (!g) return nullptr;
+    g->device = device;
+    g->num_sms = prop.multiProcessorCount;
+    g->precision = mxb::precision_from_env();
+    if (const char* t = getenv("MINIXLA_WAIT_TIMEOUT_MS")) {
+        const long long ms = atoll(t);
+        if (ms > 0) g->timeout_ns = static_cast<unsigned long long>(ms) * 1000000ull;
+    }
+    bool ok = cuda_ok(cudaFree(nullptr), "context init") &&
+              cuda_ok(cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking), "stream create") &&
+              cuda_ok(cudaMalloc(&g->d_err, sizeof(int)), "error word alloc") &&
+              cuda_ok(cudaMemset(g->d_err, 0, sizeof(int)), "error word clear") &&
+              cuda_ok(cudaEventCreate(&g->ev0), "event create") && cuda_ok(cudaEventCreate(&g->ev1), "event create");
+    if (ok) g->pool = new (std::nothrow) mxb::DevicePool(device);
+    if (!ok || !g->pool) {
+        gpu_ctx_destroy(g);
+        return nullptr;
+    }
+    return g;
+}
+
+GpuCtx* gpu_ctx_create(void) {
+    int dev = 0;
+    if (const char* d = getenv("MINIXLA_DEVICE")) dev = atoi(d);
+    return gpu_ctx_create_on(dev);
+}
+
+void gpu_ctx_destroy(GpuCtx* g) {
+    if (!g) return;
+    {
+        mxb::DeviceScope scope(g->device);
+        if (g->stream) cudaStreamSynchronize(g->stream);
+        delete g->pool;
+        if (g->d_err) cudaFree(g->d_err);
+        if (g->ev0) cudaEventDestroy(g->ev0);
+        if (g->ev1) cudaEventDestroy(g->ev1);
+        if (g->stream) cudaStreamDestroy(g->stream);
+    }
+    delete g;
+}
+
+int gpu_ctx_set_precision(GpuCtx* ctx, int mode) {
+    if (!ctx || !mxb::valid_precision(mode)) {
+        set_error("gpu_ctx_set_precision: unknown mode %d", mode);
+        return -1;
+    }
+    ctx->precision = mode;
+    return 0;
+}
+
+int gpu_ctx_get_precision(const GpuCtx* ctx) { return ctx ? ctx->precision : -1; }
+
+int gpu_ctx_device(const GpuCtx* ctx) { return ctx ? ctx->device : -1; }
+
+Tensor* gpu_execute(Node* root, GpuCtx* ctx) {
+    Tensor* out = nullptr;
+    return mxb::execute_graph(root, ctx, nullptr, &out) == MXB_OK ? out : nullptr;
+}
+
+int gpu_execute_into(Node* root, GpuCtx* ctx, Tensor* out) {
+    if (!out) {
+        set_error("gpu_execute_into: NULL destination");
+        return MXB_E_ARG;
+    }
+    return mxb::execute_graph(root, ctx, out, nullptr);
+}
+
+double gpu_time_kernel_ms(Node* root, GpuCtx* ctx, int warmup, int reps) {
+    return mxb::time_fused(root, ctx, warmup, reps, ctx ? ctx->precision : 0, "gpu_time_kernel_ms");
+}
+
+double gpu_time_kernel_tc_ms(Node* root, GpuCtx* ctx, int warmup, int reps) {
+    return mxb::time_fused(root, ctx, warmup, reps, GPU_PRECISION_TF32, "gpu_time_kernel_tc_ms");
+}
+
+Tensor* gpu_run_tensorcore(const Node* fused, GpuCtx* ctx) {
+    if (!ctx) {
+        set_error("gpu_run_tensorcore: NULL context");
+        return nullptr;
+    }
+    return mxb::run_single(fused, ctx, GPU_PRECISION_TF32, "gpu_run_tensorcore");
+}
+
+Tensor* gpu_run_fused(const Node* fused, const char* ptx) {
+    (void)ptx;  // kernels are compiled sm_100a code chosen from the node itself
+    GpuCtx* ctx = gpu_ctx_create();
+    if (!ctx) return nullptr;
+    Tensor* r = mxb::run_single(fused, ctx, ctx->precision, "gpu_run_fused");
+    gpu_ctx_destroy(ctx);
+    return r;
+}
+
+int mxb_fused_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
+                   long long ldo, int M, int N, int K, const mxb_ep_step* steps, int n_steps, int precision,
+                   void* stream) {
+    if (!ctx || !A || !B || !out || M < 1 || N < 1 || K < 1 || lda < K || ldb < N || ldo < N ||
+        n_steps < 0 || n_steps > MXB_MAX_EPILOGUE || (n_steps > 0 && !steps) || !mxb::valid_precision(precision)) {
+        set_error("mxb_fused_gemm: invalid arguments");
+        return MXB_E_ARG;
+    }
+    if (lda % 4 || ldb % 4 || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15)) {
+        set_error("mxb_fused_gemm: A and B need 16-byte aligned bases and row pitches (lda %% 4 == 0, ldb %% 4 == 0)");
+        return MXB_E_ARG;
+    }
+    mxb::EpStepDev dev_steps[MXB_MAX_EPILOGUE];
+    for (int i = 0; i < n_steps; ++i) {
+        const mxb_ep_step& s = steps[i];
+        const bool is_add = s.kind == MXB_EP_ADD_FULL || s.kind == MXB_EP_ADD_ROW || s.kind == MXB_EP_ADD_MOD;
+        if (s.kind < MXB_EP_ADD_FULL || s.kind > MXB_EP_SCALE || (is_add && !s.operand) ||
+            (s.kind == MXB_EP_ADD_FULL && s.ld_or_size < N) || (s.kind == MXB_EP_ADD_MOD && s.ld_or_size < 1)) {
+            set_error("mxb_fused_gemm: invalid epilogue step %d", i);
+            return MXB_E_ARG;
+        }
+        memcpy(&dev_steps[i], &s, sizeof(s));
+    }
+    mxb::DeviceScope scope(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    return mxb::launch_gemm(ctx, A, lda, B, ldb, out, ldo, M, N, K, dev_steps, n_steps, precision, st);
+}
+
+int mxb_add(GpuCtx* ctx, const float* a, long long n, const float* b, long long b_size, float* out, void* stream) {
+    if (!ctx || !a || !b || !out || n < 0 || b_size < 1) {
+        set_error("mxb_add: invalid arguments");
+        return MXB_E_ARG;
+    }
+    mxb::DeviceScope scope(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    return cuda_ok(mxb::launch_add(a, n, b, b_size, out, ctx->num_sms, st), "add launch") ? MXB_OK : MXB_E_CUDA;
+}
+
+int mxb_relu(GpuCtx* ctx, const float* x, long long n, float* out, void* stream) {
+    if (!ctx || !x || !out || n < 0) {
+        set_error("mxb_relu: invalid arguments");
+        return MXB_E_ARG;
+    }
+    mxb::DeviceScope scope(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    return cuda_ok(mxb::launch_relu(x, n, out, ctx->num_sms, st), "relu launch") ? MXB_OK : MXB_E_CUDA;
+}
+
+int mxb_check_device_error(GpuCtx* ctx) {
+    if (!ctx) return MXB_E_ARG;
+    mxb::DeviceScope scope(ctx->device);
+    if (!cuda_ok(cudaDeviceSynchronize(), "device synchronize")) return MXB_E_CUDA;
+    return mxb::finish(ctx);
+}
+
+int mxb_selftest_wait_timeout(GpuCtx* ctx, unsigned long long timeout_ns) {
+    if (!ctx) return MXB_E_ARG;
+    mxb::DeviceScope scope(ctx->device);
+    if (!cuda_ok(mxb::launch_wait_timeout_probe(ctx->d_err, timeout_ns, ctx->stream), "probe launch"))
+        return MXB_E_CUDA;
+    return mxb::finish(ctx);
+}
+
+unsigned long long mxb_launch_count(void) { return mxb::g_launches.load(); }
+
+const char* mxb_last_error(void) { return mxb::t_last_error.c_str(); }
+
+}  // extern "C"

@@ -1,0 +1,423 @@
+"""GPU parity tests: the sm_100a path against the oracle, through the C ABI.
+
+Tolerances:
+  3xTF32 mode: relative Frobenius error <= 1e-5 against MiniXLA's fp32 execute();
+  TF32 mode:   relative Frobenius error <= 2e-3;
+  both:        no NaN, and no sign flip after relu beyond what the tolerance
+               allows (an output may only change sign / zero-ness where the
+               oracle value is within the error band of zero).
+Small graphs with exactly representable values must match bit for bit.
+"""
+import ctypes as C
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from minixla_b200 import datagen
+from minixla_b200 import lib as mlib
+from minixla_b200.abi import OP_ADD, OP_MUL, OP_RELU, HostGraph, free_host_tensor, tensor_to_numpy
+from oracle import bindings
+from tests.golden.cases import KNOWN_ANSWERS, all_cases
+from tests.graph_eval import HostBuilder, host_graph, oracle_eval, rel_frobenius
+
+pytestmark = pytest.mark.gpu
+
+TF32, X3 = mlib.GPU_PRECISION_TF32, mlib.GPU_PRECISION_3XTF32
+TOL = {TF32: 2e-3, X3: 1e-5}
+CASES = all_cases()
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def run_execute(lib, ctx, root, precision):
+    assert lib.gpu_ctx_set_precision(ctx, precision) == 0
+    t = lib.gpu_execute(root, ctx)
+    assert t, f"gpu_execute failed: {mlib.last_error()}"
+    try:
+        return tensor_to_numpy(t)
+    finally:
+        free_host_tensor(t)
+
+
+def check(got, want, precision, what="", band=None):
+    assert got.shape == want.shape, what
+    assert not np.isnan(got).any(), f"{what}: NaN in GPU output"
+    err = rel_frobenius(got, want)
+    assert err <= TOL[precision], f"{what}: relative Frobenius {err:.3g} > {TOL[precision]:g}"
+    # Zero / sign agreement after relu: only where the oracle is clearly away from 0.
+    band = band if band is not None else 50 * TOL[precision] * (np.abs(want).max() + 1e-30)
+    clear = np.abs(want) > band
+    assert np.array_equal(np.sign(got[clear]), np.sign(want[clear])), f"{what}: sign flips"
+    return err
+
+
+# ---------------------------------------------------------------- golden cases
+
+
+@pytest.mark.parametrize("precision", [X3, TF32], ids=["3xtf32", "tf32"])
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_golden_case(lib, gpu_ctx, golden, case, precision):
+    name, inputs, build = case
+    hg, root = host_graph(inputs, build)
+    got = run_execute(lib, gpu_ctx, root, precision)
+    want = golden[f"{name}:__out__"]
+    check(got, want, precision, name)
+    if name in KNOWN_ANSWERS:  # small integers: exact in every mode
+        assert np.array_equal(got.reshape(-1), np.array(KNOWN_ANSWERS[name], dtype=np.float32))
+
+
+def test_gpu_execute_leaves_graph_untouched(lib, gpu_ctx):
+    name, inputs, build = next(c for c in CASES if c[0] == "mlp_small")
+    hg, root = host_graph(inputs, build)
+    before = bytes(C.string_at(C.addressof(root.contents), C.sizeof(root.contents)))
+    run_execute(lib, gpu_ctx, root, X3)
+    assert bytes(C.string_at(C.addressof(root.contents), C.sizeof(root.contents))) == before
+    assert not root.contents.output
+
+
+# ---------------------------------------------------------------- reference host API + optimize()
+
+needs_ref = pytest.mark.skipif(not bindings.ref_available(), reason="reference host library not shipped")
+
+
+@needs_ref
+@pytest.mark.parametrize("precision", [X3, TF32], ids=["3xtf32", "tf32"])
+def test_reference_graph_through_optimize(lib, gpu_ctx, precision):
+    """A graph built and optimized by MiniXLA's own code runs unchanged on this backend."""
+    name, inputs, build = next(c for c in CASES if c[0] == "mlp_small")
+    rg = bindings.RefGraph()
+    L = rg.lib
+    try:
+        t = {k: rg.input(v) for k, v in inputs.items()}
+        h = L.g_relu(L.g_add(L.g_matmul(t["X"], t["W1"]), t["b1"]))
+        y = L.g_add(L.g_relu(L.g_add(L.g_matmul(h, t["W2"]), t["b2"])), L.g_matmul(h, t["W2p"]))
+        root = rg.own(rg.optimize(L.g_add(L.g_matmul(y, t["W3"]), t["b3"])))
+        got = run_execute(lib, gpu_ctx, root, precision)  # before execute() memoizes anything
+        want = rg.execute(root)
+    finally:
+        rg.close()
+    check(got, want, precision, "mlp via optimize()")
+
+
+# ---------------------------------------------------------------- gpu_test.c mirrors
+
+
+def test_single_fused_via_gpu_run_fused(lib):
+    """gpu_test.c:21-41: 2x3 . 3x2 + C, relu through gpu_run_fused, tol 1e-4."""
+    name, inputs, build = next(c for c in CASES if c[0] == "tests_fused_exec")
+    hg, root = host_graph(inputs, build)
+    t = lib.gpu_run_fused(root, b"ignored ptx")
+    assert t, mlib.last_error()
+    got = tensor_to_numpy(t)
+    free_host_tensor(t)
+    np.testing.assert_allclose(got.reshape(-1), KNOWN_ANSWERS[name], atol=1e-4)
+
+
+def test_broadcast_bias_now_supported(lib, gpu_ctx):
+    """gpu_test.c:48-73 asserted that a [N] bias was refused on the GPU; this
+    backend runs it (eval_fused's broadcast rule, graph.c:100-105) and must
+    match execute(): {0, 0, 19, 4} (tests.c:48-65)."""
+    name, inputs, build = next(c for c in CASES if c[0] == "tests_bias")
+    hg, root = host_graph(inputs, build)
+    np.testing.assert_array_equal(run_execute(lib, gpu_ctx, root, X3).reshape(-1), [0, 0, 19, 4])
+    t = lib.gpu_run_fused(root, None)
+    assert t
+    np.testing.assert_array_equal(tensor_to_numpy(t).reshape(-1), [0, 0, 19, 4])
+    free_host_tensor(t)
+    t = lib.gpu_run_tensorcore(root, gpu_ctx)
+    assert t
+    np.testing.assert_array_equal(tensor_to_numpy(t).reshape(-1), [0, 0, 19, 4])
+    free_host_tensor(t)
+
+
+@pytest.mark.parametrize("name,tol", [("tests_diamond", 1e-3), ("gpu_two_layer", 1e-3), ("gpu_deep_chain", 5e-2)])
+def test_gpu_test_graphs_default_mode(lib, gpu_ctx, golden, name, tol):
+    """gpu_test.c:83-126, 132-188, 201-249 with their absolute tolerances, default precision."""
+    case = next(c for c in CASES if c[0] == name)
+    hg, root = host_graph(case[1], case[2])
+    lib.gpu_ctx_set_precision(gpu_ctx, X3)
+    t = lib.gpu_execute(root, gpu_ctx)
+    assert t
+    got = tensor_to_numpy(t)
+    free_host_tensor(t)
+    assert np.max(np.abs(got - golden[f"{name}:__out__"])) <= tol
+
+
+def test_deep_chain_returns_memory(lib):
+    """gpu_test.c:230-241: device memory back to baseline (within 16 MiB) once
+    the context that ran the graph is destroyed."""
+    import torch
+
+    name, inputs, build = next(c for c in CASES if c[0] == "gpu_deep_chain")
+    hg, root = host_graph(inputs, build)
+    torch.cuda.init()
+    free0, _ = torch.cuda.mem_get_info(0)
+    ctx = lib.gpu_ctx_create()
+    t = lib.gpu_execute(root, ctx)
+    assert t
+    free_host_tensor(t)
+    lib.gpu_ctx_destroy(ctx)
+    free1, _ = torch.cuda.mem_get_info(0)
+    assert free1 >= free0 - 16 * 1024 * 1024
+
+
+def test_module_cache_same_graph_twice(lib, gpu_ctx, golden):
+    """gpu_test.c:254-281: the same graph twice on one context gives the same answer."""
+    case = next(c for c in CASES if c[0] == "config1_128")
+    hg, root = host_graph(case[1], case[2])
+    r1 = run_execute(lib, gpu_ctx, root, X3)
+    r2 = run_execute(lib, gpu_ctx, root, X3)
+    assert np.array_equal(r1, r2)
+    check(r1, golden["config1_128:__out__"], X3)
+
+
+def test_large_relu_matmul_512(lib, gpu_ctx):
+    """gpu_test.c:286-335: relu(512^2 matmul), tol 1e-2, integer-pattern fills."""
+    S = 512
+    a = (((np.arange(S * S) % 17) * 0.01) - 0.08).astype(np.float32).reshape(S, S)
+    b = (((np.arange(S * S) % 13) * 0.01) - 0.06).astype(np.float32).reshape(S, S)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(a), hg.input_node(b), [(OP_RELU, None)])
+    want = bindings.fused_oracle(a, b, [("relu",)])
+    for p in (X3, TF32):
+        got = run_execute(lib, gpu_ctx, root, p)
+        assert np.max(np.abs(got - want)) <= 1e-2
+
+
+def _tc_values(shape, stream):
+    # gpu_test.c:359-365 fills with (rand() % 2000 - 1000) / 100: multiples of 0.01 in [-10, 10).
+    u = datagen.raw_bits(int(np.prod(shape)), stream) % np.uint64(2000)
+    return ((u.astype(np.int64) - 1000) / 100.0).astype(np.float32).reshape(shape)
+
+
+@pytest.mark.parametrize("mkn", [(16, 8, 8), (17, 8, 8), (16, 8, 9), (16, 5, 8), (100, 100, 100), (1024, 1024, 1024),
+                                 (2048, 2048, 2049)])
+def test_tensorcore_correctness(lib, gpu_ctx, mkn):
+    """gpu_test.c:393-403 through gpu_run_tensorcore, with its tolerance
+    atol = 0.05 sqrt(K), rtol = 0.02 (gpu_test.c:349-357)."""
+    M, K, N = mkn
+    a, b = _tc_values((M, K), 60), _tc_values((K, N), 61)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(a), hg.input_node(b), [])
+    t = lib.gpu_run_tensorcore(root, gpu_ctx)
+    assert t, mlib.last_error()
+    got = tensor_to_numpy(t)
+    free_host_tensor(t)
+    want = bindings.fused_oracle(a, b, [])
+    assert np.all(np.abs(got - want) <= 0.05 * np.sqrt(K) + 0.02 * np.abs(want))
+
+
+def test_tensorcore_epilogue(lib, gpu_ctx):
+    """gpu_test.c:407-430: 100^3 with ADD + RELU through the TF32 path."""
+    a, b, c = _tc_values((100, 100), 62), _tc_values((100, 100), 63), _tc_values((100, 100), 64)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(a), hg.input_node(b), [(OP_ADD, hg.input_node(c)), (OP_RELU, None)])
+    t = lib.gpu_run_tensorcore(root, gpu_ctx)
+    assert t
+    got = tensor_to_numpy(t)
+    free_host_tensor(t)
+    want = bindings.fused_oracle(a, b, [("add", c), ("relu",)])
+    assert np.all(np.abs(got - want) <= 0.05 * np.sqrt(100) + 0.02 * np.abs(want))
+
+
+def test_kernel_timers(lib, gpu_ctx):
+    """gpu_time_kernel_ms / _tc_ms return a positive minimum; -1.0 for a non-fused root."""
+    case = next(c for c in CASES if c[0] == "config1_128")
+    hg, root = host_graph(case[1], case[2])
+    assert lib.gpu_time_kernel_ms(root, gpu_ctx, 3, 5) > 0
+    assert lib.gpu_time_kernel_tc_ms(root, gpu_ctx, 3, 5) > 0
+    mm = hg.g_matmul(hg.input_node(case[1]["A"]), hg.input_node(case[1]["B"]))
+    assert lib.gpu_time_kernel_ms(mm, gpu_ctx, 1, 1) == -1.0
+
+
+# ---------------------------------------------------------------- BASELINE configs
+
+
+def _relu_abc(M, N, K, c_normal):
+    A = datagen.uniform((M, K), 0)
+    B = datagen.uniform((K, N), 1)
+    C = datagen.normal((M, N), 2) if c_normal else datagen.uniform((M, N), 2)
+    return A, B, C
+
+
+def _sample_rows(M, n=512, seed=0):
+    rng = np.random.default_rng(seed)
+    edge = {0, M - 1}
+    for t in range(128, M, 128):
+        edge |= {t - 1, t}
+    rows = sorted(edge | set(rng.integers(0, M, size=n).tolist()))
+    return np.array([r for r in rows if 0 <= r < M], dtype=np.int64)
+
+
+@pytest.mark.parametrize("precision", [X3, TF32], ids=["3xtf32", "tf32"])
+@pytest.mark.parametrize("S", [512, 1024, 2048, 4096, 8192])
+def test_config2_square_sweep(lib, gpu_ctx, S, precision, host_threads):
+    A, B, C = _relu_abc(S, S, S, c_normal=True)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A), hg.input_node(B), [(OP_ADD, hg.input_node(C)), (OP_RELU, None)])
+    got = run_execute(lib, gpu_ctx, root, precision)
+    rows = None if S <= 2048 else _sample_rows(S, 384 if S == 8192 else 512)
+    want = bindings.fused_oracle(A, B, [("add", C), ("relu",)], rows=rows, threads=host_threads)
+    check(got if rows is None else got[rows], want, precision, f"{S}^3")
+
+
+@pytest.mark.parametrize("precision", [X3, TF32], ids=["3xtf32", "tf32"])
+@pytest.mark.parametrize("mnk", [(1000, 1000, 1000), (257, 4097, 129), (8191, 127, 3000), (1, 4096, 4096)])
+def test_config3_ragged(lib, gpu_ctx, mnk, precision, host_threads):
+    M, N, K = mnk
+    A, B, C = _relu_abc(M, N, K, c_normal=False)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A), hg.input_node(B), [(OP_ADD, hg.input_node(C)), (OP_RELU, None)])
+    got = run_execute(lib, gpu_ctx, root, precision)
+    want = bindings.fused_oracle(A, B, [("add", C), ("relu",)], threads=host_threads)
+    check(got, want, precision, f"{mnk}")
+
+
+def _mlp_inputs(M=4096, D=1024, H=4096):
+    return {
+        "X": datagen.uniform((M, D), 70),
+        "W1": datagen.normal((D, H), 71, 0.0, 1.0 / np.sqrt(D)),
+        "W2": datagen.normal((H, H), 72, 0.0, 1.0 / np.sqrt(H)),
+        "W2p": datagen.normal((H, H), 73, 0.0, 1.0 / np.sqrt(H)),
+        "W3": datagen.normal((H, D), 74, 0.0, 1.0 / np.sqrt(H)),
+        "b1": datagen.normal((H,), 75, 0.0, 0.1),
+        "b2": datagen.normal((H,), 76, 0.0, 0.1),
+        "b3": datagen.normal((D,), 77, 0.0, 0.1),
+    }
+
+
+@pytest.mark.parametrize("precision", [X3, TF32], ids=["3xtf32", "tf32"])
+def test_config4_mlp_dag(lib, gpu_ctx, precision, host_threads):
+    """3-layer MLP with a shared node (h feeds W2 and W2'), at full size.
+    Rows are independent through every layer, so the oracle evaluates a row sample of X."""
+    inp = _mlp_inputs()
+    build = next(c for c in CASES if c[0] == "mlp_small")[2]
+    hg, root = host_graph(inp, build)
+    got = run_execute(lib, gpu_ctx, root, precision)
+    rows = _sample_rows(4096, 128)
+    sub = dict(inp, X=inp["X"][rows])
+    want = oracle_eval(sub, build)
+    check(got[rows], want, precision, "mlp")
+
+
+@pytest.mark.parametrize("precision", [X3, TF32], ids=["3xtf32", "tf32"])
+def test_full_size_checksums(lib, gpu_ctx, precision):
+    """Size-independent check over every tile at the largest single-GPU shape:
+    for out = A.B + C, column sums equal (1^T A) B + 1^T C and row sums equal
+    A (B 1) + C 1 (float64 on the host)."""
+    M, N, K = 8192, 8192, 8192
+    A, B, C = _relu_abc(M, N, K, c_normal=True)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A), hg.input_node(B), [(OP_ADD, hg.input_node(C))])
+    got = run_execute(lib, gpu_ctx, root, precision).astype(np.float64)
+    A64, B64, C64 = A.astype(np.float64), B.astype(np.float64), C.astype(np.float64)
+    col_want = A64.sum(0) @ B64 + C64.sum(0)
+    row_want = A64 @ B64.sum(1) + C64.sum(1)
+    tol = 5 * TOL[precision]
+    assert rel_frobenius(got.sum(0), col_want) < tol
+    assert rel_frobenius(got.sum(1), row_want) < tol
+
+
+# ---------------------------------------------------------------- device-pointer API
+
+
+def test_device_pointer_api_matches_torch(lib, gpu_ctx):
+    import torch
+
+    M, N, K = 384, 520, 200
+    g = torch.Generator(device="cuda").manual_seed(0)
+    A = torch.rand(M, K, device="cuda", generator=g) * 2 - 1
+    B = torch.rand(K, N, device="cuda", generator=g) * 2 - 1
+    bias = torch.randn(N, device="cuda", generator=g)
+    out = torch.empty(M, N, device="cuda")
+    steps = (mlib.EpStepDev * 3)()
+    steps[0] = mlib.EpStepDev(mlib.MXB_EP_ADD_ROW, 0, bias.data_ptr(), N, 0.0, 0)
+    steps[1] = mlib.EpStepDev(mlib.MXB_EP_SCALE, 0, None, 0, 0.5, 0)
+    steps[2] = mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.mxb_fused_gemm(gpu_ctx, A.data_ptr(), K, B.data_ptr(), N, out.data_ptr(), N, M, N, K, steps, 3,
+                            X3, stream)
+    assert rc == 0, mlib.last_error()
+    torch.cuda.synchronize()
+    ref = torch.relu((A.double() @ B.double() + bias.double()) * 0.5)
+    assert rel_frobenius(out.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+
+
+def test_standalone_elementwise_device_api(lib, gpu_ctx):
+    import torch
+
+    n = 3 * 1024 * 1024 + 3
+    x = torch.randn(n, device="cuda")
+    b = torch.randn(1024 * 3 + 1, device="cuda")
+    a = torch.randn((1024 * 3 + 1) * 7, device="cuda")
+    out = torch.empty_like(x)
+    assert lib.mxb_relu(gpu_ctx, x.data_ptr(), n, out.data_ptr(), None) == 0
+    lib.mxb_check_device_error(gpu_ctx)
+    assert torch.equal(out, torch.where(x > 0, x, torch.zeros_like(x)))
+    out2 = torch.empty_like(a)
+    assert lib.mxb_add(gpu_ctx, a.data_ptr(), a.numel(), b.data_ptr(), b.numel(), out2.data_ptr(), None) == 0
+    lib.mxb_check_device_error(gpu_ctx)
+    assert torch.equal(out2, a + b.repeat(7))
+
+
+# ---------------------------------------------------------------- failure paths (no GPU fault)
+
+
+def test_bounded_wait_times_out_cleanly(lib, gpu_ctx, golden):
+    """A kernel waiting on a barrier nothing completes gives up after its limit,
+    reports MXB_E_TIMEOUT, and the context keeps working."""
+    rc = lib.mxb_selftest_wait_timeout(gpu_ctx, 2_000_000)  # 2 ms
+    assert rc == mlib.MXB_E_TIMEOUT
+    assert lib.mxb_check_device_error(gpu_ctx) == 0
+    case = next(c for c in CASES if c[0] == "config1_128")
+    hg, root = host_graph(case[1], case[2])
+    check(run_execute(lib, gpu_ctx, root, X3), golden["config1_128:__out__"], X3)
+
+
+def test_unsupported_ops_fail_loudly(lib, gpu_ctx):
+    hg = HostGraph()
+    a = hg.input_node(np.ones((2, 2), np.float32))
+    mul = hg._node(OP_MUL, [a, a])
+    assert not lib.gpu_execute(mul, gpu_ctx)
+    assert "not supported" in mlib.last_error()
+    bad = hg.fused_node(hg.input_node(np.ones((2, 3), np.float32)), hg.input_node(np.ones((2, 3), np.float32)), [])
+    assert not lib.gpu_execute(bad, gpu_ctx)
+    assert "incompatible" in mlib.last_error()
+    bad_add = hg.g_add(hg.input_node(np.ones((2, 3), np.float32)), hg.input_node(np.ones((2,), np.float32)))
+    assert not lib.gpu_execute(bad_add, gpu_ctx)
+
+
+_OOM_CHILD = r"""
+import sys, numpy as np
+sys.path.insert(0, sys.argv[1])
+import torch
+from minixla_b200 import lib as mlib
+from minixla_b200.abi import HostGraph, OP_ADD, OP_RELU, free_host_tensor
+lib = mlib.load()
+hg = HostGraph()
+A = np.ones((300, 200), np.float32); B = np.ones((200, 100), np.float32); Cm = np.ones((300, 100), np.float32)
+root = hg.fused_node(hg.input_node(A), hg.input_node(B), [(OP_ADD, hg.input_node(Cm)), (OP_RELU, None)])
+ctx = lib.gpu_ctx_create()
+torch.cuda.init()
+free0 = torch.cuda.mem_get_info(0)[0]
+t = lib.gpu_execute(root, ctx)
+assert not t, "allocation failure must give NULL"
+assert "MINIXLA_FAIL_ALLOC_AT" in mlib.last_error()
+t = lib.gpu_execute(root, ctx)          # the next call succeeds on the same context
+assert t
+free_host_tensor(t)
+lib.gpu_ctx_destroy(ctx)
+assert torch.cuda.mem_get_info(0)[0] >= free0 - 16 * 2**20
+print("OK")
+"""
+
+
+@pytest.mark.parametrize("fail_at", [1, 3, 5, 7])
+def test_allocation_failure_injection(fail_at):
+    env = dict(os.environ, MINIXLA_FAIL_ALLOC_AT=str(fail_at))
+    r = subprocess.run([sys.executable, "-c", _OOM_CHILD, str(ROOT)], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and "OK" in r.stdout, r.stdout + r.stderr
