@@ -305,7 +305,10 @@ def ours_arm(args, rank, local_rank, world):
     steps = (mlib.EpStepDev * 2)()
     steps[0] = mlib.EpStepDev(mlib.MXB_EP_ADD_FULL, 0, C_d.data_ptr(), N, 0.0, 0)
     steps[1] = mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0)
-    stream = torch.cuda.current_stream(dev)
+    # A dedicated stream: torch's default stream has handle 0, which the C ABI
+    # reads as "the context's own stream", and the events must sit on the
+    # stream the kernels run on.
+    stream = torch.cuda.Stream(dev)
 
     def launch():
         rc = lib.mxb_fused_gemm(ctx, A_d.data_ptr(), K, B_d.data_ptr(), N, out_d.data_ptr(), N, M, N, K, steps, 2,
@@ -313,6 +316,7 @@ def ours_arm(args, rank, local_rank, world):
         if rc != 0:
             raise RuntimeError(f"mxb_fused_gemm failed: {mlib.last_error()}")
 
+    torch.cuda.synchronize()
     for _ in range(args.warmup):
         launch()
     torch.cuda.synchronize()

@@ -4,8 +4,9 @@
 //        b is either the same shape as a or a trailing suffix of it (a bias
 //        row), so a plain modulo indexes it.
 // relu : out[i] = x[i] > 0 ? x[i] : 0    -- tensor.c:110-120
-// split: x = big + small with big = x rounded to TF32 (10 explicit mantissa
-//        bits, nearest, ties away), small = x - big (exact in fp32).
+// split: small = x - rne_tf32(x), the part of x a TF32 operand loses.  The
+//        GEMM reads big = rne_tf32(x) from x itself through a rounding
+//        (TFLOAT32) TMA map, so only the low part is materialised.
 //
 // All three are HBM-bound streams: 128-bit loads/stores, grid-stride loops
 // over a grid sized as a multiple of the SM count.
@@ -71,46 +72,35 @@ __global__ void relu_scalar(const float* __restrict__ x, float* __restrict__ out
 }
 
 // TF32 keeps the top 19 bits of an fp32 word (sign, 8 exponent, 10 mantissa).
-// Rounding the magnitude at bit 13 (add half an ulp, clear the low 13 bits)
-// is round-to-nearest with ties away from zero.  Non-finite values pass
-// through as big with small = 0.
-__device__ __forceinline__ void split1(float x, float& big, float& small) {
+// Round to nearest even at bit 13: add 0xFFF plus the kept LSB, clear the low
+// 13 bits; acting on the magnitude bits makes it symmetric in sign.  This is
+// the rounding TMA applies when it loads through a TFLOAT32 map, so
+// x - rne_tf32(x) is exactly the part the GEMM's big operand leaves out (an
+// exact fp32 difference: both values lie within one TF32 ulp).  Non-finite
+// inputs, and values whose rounding overflows, give small = 0.
+__device__ __forceinline__ float small_part(float x) {
     const uint32_t u = __float_as_uint(x);
-    if ((u & 0x7F800000u) == 0x7F800000u) {
-        big = x;
-        small = 0.0f;
-        return;
-    }
-    big = __uint_as_float((u + 0x1000u) & 0xFFFFE000u);
-    small = x - big;
+    if ((u & 0x7F800000u) == 0x7F800000u) return 0.0f;
+    const uint32_t big_bits = (u + 0x0FFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
+    if ((big_bits & 0x7F800000u) == 0x7F800000u) return 0.0f;
+    return x - __uint_as_float(big_bits);
 }
 
 __global__ void split_tf32_kernel(const float* __restrict__ x, long long rows, long long cols,
-                                  long long ld_in, float* __restrict__ big, float* __restrict__ small,
-                                  long long ld_out) {
+                                  long long ld_in, float* __restrict__ small, long long ld_out) {
     const long long n = rows * cols;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
         const long long r = i / cols, c = i - r * cols;
-        float b, s;
-        split1(x[r * ld_in + c], b, s);
-        big[r * ld_out + c] = b;
-        small[r * ld_out + c] = s;
+        small[r * ld_out + c] = small_part(x[r * ld_in + c]);
     }
 }
 
-__global__ void split_tf32_vec4(const float4* __restrict__ x, float4* __restrict__ big,
-                                float4* __restrict__ small, long long n4) {
+__global__ void split_tf32_vec4(const float4* __restrict__ x, float4* __restrict__ small, long long n4) {
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
         const float4 v = __ldcs(x + i);
-        float4 b, s;
-        split1(v.x, b.x, s.x);
-        split1(v.y, b.y, s.y);
-        split1(v.z, b.z, s.z);
-        split1(v.w, b.w, s.w);
-        big[i] = b;
-        small[i] = s;
+        small[i] = make_float4(small_part(v.x), small_part(v.y), small_part(v.z), small_part(v.w));
     }
 }
 
@@ -149,17 +139,14 @@ cudaError_t launch_relu(const float* x, long long n, float* out, int num_sms, cu
 }
 
 cudaError_t launch_split_tf32(const float* x, long long rows, long long cols, long long ld_in,
-                              float* big, float* small, long long ld_out, int num_sms,
-                              cudaStream_t stream) {
+                              float* small, long long ld_out, int num_sms, cudaStream_t stream) {
     const long long n = rows * cols;
     if (n <= 0) return cudaSuccess;
-    if (ld_in == cols && ld_out == cols && n % 4 == 0 && aligned16(x) && aligned16(big) && aligned16(small)) {
+    if (ld_in == cols && ld_out == cols && n % 4 == 0 && aligned16(x) && aligned16(small)) {
         split_tf32_vec4<<<grid_for(n / 4, num_sms), kBlock, 0, stream>>>(
-            reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(big),
-            reinterpret_cast<float4*>(small), n / 4);
+            reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(small), n / 4);
     } else {
-        split_tf32_kernel<<<grid_for(n, num_sms), kBlock, 0, stream>>>(x, rows, cols, ld_in, big, small,
-                                                                      ld_out);
+        split_tf32_kernel<<<grid_for(n, num_sms), kBlock, 0, stream>>>(x, rows, cols, ld_in, small, ld_out);
     }
     note_launch();
     return cudaGetLastError();

@@ -9,7 +9,7 @@
 //  * Output tile 128 x BN.  k advances in blocks of 32 fp32 = one 128-byte
 //    swizzle row, staged in a STAGES-deep shared-memory ring by TMA:
 //      A box [128 rows][32 k]     K-major, SWIZZLE_128B  (16 KiB)
-//      B boxes [32 k][32 n] x BN/32, MN-major, SWIZZLE_128B (4 KiB each)
+//      B boxes [32 k][32 n] x BN/32, MN-major, SWIZZLE_128B_ATOM_32B (4 KiB each)
 //    B is consumed MN-major straight from its row-major [K, N] layout, so no
 //    transpose pass exists anywhere.
 //  * Warp roles (192 threads):
@@ -21,9 +21,17 @@
 //                  apply the node's epilogue steps in order, store once.
 //    TMEM holds two accumulators (2*BN columns) so the epilogue of tile i
 //    overlaps the main loop of tile i+1.
-//  * 3xTF32 mode: the host splits A and B into tf32-exact high parts and
-//    the low remainders; per k-step the MMA warp issues
-//    big*big + big*small + small*big into the same accumulator.
+//  * Every operand goes through a TFLOAT32 tensor map, so TMA rounds fp32 to
+//    TF32 (round to nearest even) on its way into shared memory; fed raw
+//    fp32, the tensor core would truncate instead.
+//  * 3xTF32 mode: a pre-pass writes small = x - rne_tf32(x) for A and B; the
+//    raw operands loaded through the rounding maps are exactly big =
+//    rne_tf32(x).  Per k-step the MMA warp issues big*big + big*small +
+//    small*big into the same accumulator.  The tensor core's fp32
+//    accumulation truncates toward zero, a bias that grows with K, so this
+//    mode accumulates K in segments of kSegKb k-blocks: each segment starts
+//    a fresh TMEM accumulator and the epilogue sums the segments in fp32
+//    registers with round-to-nearest.
 //  * Every mbarrier wait is bounded (global-timer limit).  A wait that runs
 //    out records an error bit in global memory, raises a CTA-wide abort flag,
 //    waits (bounded) for its own copies / MMAs in flight, frees TMEM and
@@ -45,6 +53,8 @@ constexpr int kBK = 32;           // fp32 elements per 128-byte swizzle row
 constexpr int kThreads = 192;
 constexpr int kBoxBytes = 32 * 32 * 4;  // one B box: 32 k-rows x 128 bytes
 
+constexpr int kSegKb = 8;           // k-blocks (of 32) per accumulation segment in 3xTF32 mode
+
 struct FusedParams {
     float* out;
     long long ldo;
@@ -52,7 +62,7 @@ struct FusedParams {
     int n_steps;
     int tiles_m, tiles_n, num_tiles, num_kb;
     int group_m;
-    int pad;
+    int seg_kb;                     // k-blocks per accumulation segment (num_kb: one segment)
     unsigned long long timeout_ns;
     int* err;
     EpStepDev steps[MXB_MAX_EPILOGUE];
@@ -174,7 +184,7 @@ __device__ __forceinline__ void store_row_chunk(const float (&v)[32], int row, i
     }
 }
 
-template <int BN, int STAGES, bool SPLIT3>
+template <int BN, int STAGES, bool SPLIT3, bool SEG>
 __global__ void __launch_bounds__(kThreads, 1)
     fused_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
@@ -284,44 +294,54 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t acc_phase = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-                if (*abort_flag) break;
-                if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns)) {
-                    raise_error(p, abort_flag, kErrMma);
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-                for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait(full_bar(stage), phase, p.timeout_ns)) {
+                for (int k_begin = 0; k_begin < p.num_kb && ok; k_begin += p.seg_kb) {
+                    const int k_end = min(p.num_kb, k_begin + p.seg_kb);
+                    if (*abort_flag) { ok = false; break; }
+                    if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns)) {
                         raise_error(p, abort_flag, kErrMma);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_addr(smem + stage * C::kStageBytes);
-                    const uint32_t b_addr = a_addr + C::kABytes;
-#pragma unroll
-                    for (int kk = 0; kk < kBK / 8; ++kk) {
-                        // A: K-major, advance 8 fp32 = 32 bytes inside the swizzled row.
-                        const uint64_t da = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
-                        // B: MN-major, advance one 8-k-row atom = 1024 bytes; 32-col boxes 4 KiB apart.
-                        const uint64_t db = smem_desc_sw128(b_addr + kk * 1024, kBoxBytes, 1024);
-                        mma_tf32(d_tmem, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
-                        if (SPLIT3) {
-                            const uint64_t da2 = smem_desc_sw128(a_addr + C::kOperandBytes + kk * 32, 16, 1024);
-                            const uint64_t db2 =
-                                smem_desc_sw128(b_addr + C::kOperandBytes + kk * 1024, kBoxBytes, 1024);
-                            mma_tf32(d_tmem, da, db2, idesc, 1u);
-                            mma_tf32(d_tmem, da2, db, idesc, 1u);
+                    const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                    for (int kb = k_begin; kb < k_end; ++kb) {
+                        if (!mbar_wait(full_bar(stage), phase, p.timeout_ns)) {
+                            raise_error(p, abort_flag, kErrMma);
+                            ok = false;
+                            break;
                         }
+                        tc_fence_after();
+                        const uint32_t a_addr = smem_addr(smem + stage * C::kStageBytes);
+                        const uint32_t b_addr = a_addr + C::kABytes;
+#pragma unroll
+                        for (int kk = 0; kk < kBK / 8; ++kk) {
+                            // A: K-major, advance 8 fp32 = 32 bytes inside the swizzled row.
+                            const uint64_t da = smem_desc(a_addr + kk * 32, 16, 1024, kLayoutSW128);
+                            // B: MN-major, advance 8 k-rows = 1 KiB; 4-row atoms 512 B apart,
+                            // 32-column boxes 4 KiB apart.
+                            const uint64_t db = smem_desc(b_addr + kk * 1024, kBoxBytes, 512, kLayoutSW128Base32B);
+                            const uint32_t accumulate = (kb != k_begin || kk != 0) ? 1u : 0u;
+                            if (SPLIT3) {
+                                const uint64_t da2 =
+                                    smem_desc(a_addr + C::kOperandBytes + kk * 32, 16, 1024, kLayoutSW128);
+                                const uint64_t db2 = smem_desc(b_addr + C::kOperandBytes + kk * 1024, kBoxBytes,
+                                                               512, kLayoutSW128Base32B);
+                                // Small cross terms first, the dominant big*big product last.
+                                mma_tf32(d_tmem, da, db2, idesc, accumulate);
+                                mma_tf32(d_tmem, da2, db, idesc, 1u);
+                                mma_tf32(d_tmem, da, db, idesc, 1u);
+                            } else {
+                                mma_tf32(d_tmem, da, db, idesc, accumulate);
+                            }
+                        }
+                        mma_commit(empty_bar(stage));
+                        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                     }
-                    mma_commit(empty_bar(stage));
-                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                    if (!ok) break;
+                    mma_commit(tfull_bar(acc));
+                    acc ^= 1;
+                    if (acc == 0) acc_phase ^= 1u;
                 }
-                if (!ok) break;
-                mma_commit(tfull_bar(acc));
-                acc ^= 1;
-                if (acc == 0) acc_phase ^= 1u;
             }
             // All MMAs issued by this thread must finish before TMEM is freed.
             mma_commit(drain_bar);
@@ -334,14 +354,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
-            const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
-            if (stop) break;
-            const bool got = mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns);
-            if (!__all_sync(0xffffffffu, got)) {
-                if (lane == 0) raise_error(p, abort_flag, kErrEpilogue);
-                break;
-            }
-            tc_fence_after();
             int mb, nb;
             tile_coords(t, p, mb, nb);
             const int row = mb * kBM + row_in_tile;
@@ -349,26 +361,78 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int col0 = nb * BN;
             int chunks = (p.N - col0 + 31) / 32;
             if (chunks > BN / 32) chunks = BN / 32;
-            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                                   static_cast<uint32_t>(acc * BN);
-            for (int c = 0; c < chunks; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(taddr + 32 * c, r);
-                tmem_ld_wait();
-                if (c == chunks - 1) {
-                    // Accumulator fully read: hand it back to the MMA warp.
+            const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+            bool failed = false;
+            if (SEG) {
+                // Sum the K segments in registers (fp32, round to nearest).
+                float total[BN];
+                for (int k_begin = 0; k_begin < p.num_kb; k_begin += p.seg_kb) {
+                    const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
+                    const bool got = !stop && mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns);
+                    if (!__all_sync(0xffffffffu, got)) {
+                        if (lane == 0 && !stop) raise_error(p, abort_flag, kErrEpilogue);
+                        failed = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * BN);
+#pragma unroll
+                    for (int c = 0; c < BN / 32; ++c) {
+                        if (c < chunks) {
+                            uint32_t r[32];
+                            tmem_ld_32x32b_x32(taddr + 32 * c, r);
+                            tmem_ld_wait();
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                total[32 * c + i] = k_begin == 0 ? __uint_as_float(r[i])
+                                                                 : total[32 * c + i] + __uint_as_float(r[i]);
+                        }
+                    }
                     tc_fence_before();
                     mbar_arrive(tempty_bar(acc));
+                    acc ^= 1;
+                    if (acc == 0) acc_phase ^= 1u;
                 }
-                float v[32];
+                if (failed) break;
 #pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-                const int col = col0 + 32 * c;
-                apply_epilogue(v, row, col, row_ok, p);
-                if (row_ok) store_row_chunk(v, row, col, p);
+                for (int c = 0; c < BN / 32; ++c) {
+                    if (c < chunks) {
+                        float v[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = total[32 * c + i];
+                        const int col = col0 + 32 * c;
+                        apply_epilogue(v, row, col, row_ok, p);
+                        if (row_ok) store_row_chunk(v, row, col, p);
+                    }
+                }
+            } else {
+                const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
+                const bool got = !stop && mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns);
+                if (!__all_sync(0xffffffffu, got)) {
+                    if (lane == 0 && !stop) raise_error(p, abort_flag, kErrEpilogue);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * BN);
+                for (int c = 0; c < chunks; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + 32 * c, r);
+                    tmem_ld_wait();
+                    if (c == chunks - 1) {
+                        // Accumulator fully read: hand it back to the MMA warp.
+                        tc_fence_before();
+                        mbar_arrive(tempty_bar(acc));
+                    }
+                    float v[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                    const int col = col0 + 32 * c;
+                    apply_epilogue(v, row, col, row_ok, p);
+                    if (row_ok) store_row_chunk(v, row, col, p);
+                }
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1u;
             }
-            acc ^= 1;
-            if (acc == 0) acc_phase ^= 1u;
         }
     }
 
@@ -402,23 +466,24 @@ EncodeTiledFn encode_fn() {
 
 // Row-major [rows, cols] fp32 with row pitch `ld` elements; box [box_rows][box_cols].
 bool make_map(CUtensorMap* map, const float* base, long long rows, long long cols, long long ld,
-              int box_cols, int box_rows) {
+              int box_cols, int box_rows, CUtensorMapSwizzle swizzle) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
     const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
-                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+    // TFLOAT32: TMA rounds each fp32 element to TF32 (nearest even) on load.
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, 2, const_cast<float*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES, bool SPLIT3>
+template <int BN, int STAGES, bool SPLIT3, bool SEG>
 cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     using C = Cfg<BN, STAGES, SPLIT3>;
-    auto kernel = fused_gemm_kernel<BN, STAGES, SPLIT3>;
+    auto kernel = fused_gemm_kernel<BN, STAGES, SPLIT3, SEG>;
     // The shared-memory opt-in is per device: remember which devices have it.
     static std::mutex mu;
     static uint64_t configured = 0;
@@ -434,14 +499,16 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
         }
     }
 
-    const float* a_hi = SPLIT3 ? g.A_big : g.A;
-    const float* b_hi = SPLIT3 ? g.B_big : g.B;
+    const float* a_hi = g.A;   // through the rounding map this is big = rne_tf32(A)
+    const float* b_hi = g.B;
     CUtensorMap mA, mB, mA2, mB2;
-    if (!make_map(&mA, a_hi, g.M, g.K, g.lda, kBK, kBM) || !make_map(&mB, b_hi, g.K, g.N, g.ldb, 32, kBK))
+    constexpr CUtensorMapSwizzle kSwA = CU_TENSOR_MAP_SWIZZLE_128B;
+    constexpr CUtensorMapSwizzle kSwB = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    if (!make_map(&mA, a_hi, g.M, g.K, g.lda, kBK, kBM, kSwA) || !make_map(&mB, b_hi, g.K, g.N, g.ldb, 32, kBK, kSwB))
         return cudaErrorInvalidValue;
     if (SPLIT3) {
-        if (!make_map(&mA2, g.A_small, g.M, g.K, g.lda, kBK, kBM) ||
-            !make_map(&mB2, g.B_small, g.K, g.N, g.ldb, 32, kBK))
+        if (!make_map(&mA2, g.A_small, g.M, g.K, g.lda, kBK, kBM, kSwA) ||
+            !make_map(&mB2, g.B_small, g.K, g.N, g.ldb, 32, kBK, kSwB))
             return cudaErrorInvalidValue;
     } else {
         mA2 = mA;
@@ -460,6 +527,7 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.num_tiles = p.tiles_m * p.tiles_n;
     p.num_kb = (g.K + kBK - 1) / kBK;
     p.group_m = 16;
+    p.seg_kb = SEG ? kSegKb : p.num_kb;
     p.timeout_ns = g.timeout_ns;
     p.err = g.err;
     for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
@@ -473,13 +541,13 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
-    if (g.precision == GPU_PRECISION_3XTF32) return run_variant<128, 3, true>(g, stream);
+    if (g.precision == GPU_PRECISION_3XTF32) return run_variant<128, 3, true, true>(g, stream);
     // One TF32 product.  Narrow or small problems use 128-wide tiles so more SMs get work.
     const long long tiles_m = (g.M + kBM - 1) / kBM;
     const long long tiles256 = tiles_m * ((g.N + 255) / 256);
     const long long tiles128 = tiles_m * ((g.N + 127) / 128);
-    if (g.N <= 128 || (tiles256 < g.num_sms && tiles128 > tiles256)) return run_variant<128, 6, false>(g, stream);
-    return run_variant<256, 4, false>(g, stream);
+    if (g.N <= 128 || (tiles256 < g.num_sms && tiles128 > tiles256)) return run_variant<128, 6, false, false>(g, stream);
+    return run_variant<256, 4, false, false>(g, stream);
 }
 
 // ------------------------------------------------------------------ bounded-wait probe

@@ -24,10 +24,8 @@ static_assert(sizeof(EpStepDev) == sizeof(mxb_ep_step), "EpStepDev must mirror m
 struct GemmLaunch {
     const float* A; long long lda;     // M x K, lda % 4 == 0
     const float* B; long long ldb;     // K x N, ldb % 4 == 0
-    const float* A_small;              // 3xTF32 only: low parts, same pitches
+    const float* A_small;              // 3xTF32 only: x - rne_tf32(x), same pitches
     const float* B_small;
-    const float* A_big;                // 3xTF32 only: tf32-exact high parts
-    const float* B_big;
     float* out; long long ldo;
     int M, N, K;
     const EpStepDev* steps; int n_steps;
@@ -40,8 +38,7 @@ struct GemmLaunch {
 // Kernel launchers (fused_gemm.cu, elementwise.cu).  Return cudaError_t.
 cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream);
 cudaError_t launch_split_tf32(const float* x, long long rows, long long cols, long long ld_in,
-                              float* big, float* small, long long ld_out, int num_sms,
-                              cudaStream_t stream);
+                              float* small, long long ld_out, int num_sms, cudaStream_t stream);
 cudaError_t launch_add(const float* a, long long n, const float* b, long long b_size, float* out,
                        int num_sms, cudaStream_t stream);
 cudaError_t launch_relu(const float* x, long long n, float* out, int num_sms, cudaStream_t stream);

@@ -414,7 +414,7 @@ static bool tma_operand(GpuCtx* ctx, const float* src, long long rows, long long
 }
 
 // Launches epi(A @ B) with already-validated, TMA-ready operands.  For
-// 3xTF32 the high/low split of A and B goes to pooled workspace first.
+// 3xTF32 the low parts of A and B (x - rne_tf32(x)) go to pooled workspace first.
 static int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
                        long long ldo, int M, int N, int K, const EpStepDev* steps, int n_steps, int precision,
                        cudaStream_t stream) {
@@ -434,26 +434,20 @@ static int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* 
     g.err = ctx->d_err;
     g.timeout_ns = ctx->timeout_ns;
     g.num_sms = ctx->num_sms;
-    float* ws[4] = {nullptr, nullptr, nullptr, nullptr};
+    float* ws[2] = {nullptr, nullptr};
     int rc = MXB_OK;
     if (precision == GPU_PRECISION_3XTF32) {
         const size_t a_bytes = static_cast<size_t>(M) * lda * 4, b_bytes = static_cast<size_t>(K) * ldb * 4;
         ws[0] = static_cast<float*>(ctx->pool->alloc(a_bytes, stream));
-        ws[1] = ws[0] ? static_cast<float*>(ctx->pool->alloc(a_bytes, stream)) : nullptr;
-        ws[2] = ws[1] ? static_cast<float*>(ctx->pool->alloc(b_bytes, stream)) : nullptr;
-        ws[3] = ws[2] ? static_cast<float*>(ctx->pool->alloc(b_bytes, stream)) : nullptr;
-        if (!ws[3]) {
+        ws[1] = ws[0] ? static_cast<float*>(ctx->pool->alloc(b_bytes, stream)) : nullptr;
+        if (!ws[1]) {
             rc = MXB_E_NOMEM;
-        } else if (!cuda_ok(launch_split_tf32(A, M, K, lda, ws[0], ws[1], lda, ctx->num_sms, stream),
-                            "split A") ||
-                   !cuda_ok(launch_split_tf32(B, K, N, ldb, ws[2], ws[3], ldb, ctx->num_sms, stream),
-                            "split B")) {
+        } else if (!cuda_ok(launch_split_tf32(A, M, K, lda, ws[0], lda, ctx->num_sms, stream), "split A") ||
+                   !cuda_ok(launch_split_tf32(B, K, N, ldb, ws[1], ldb, ctx->num_sms, stream), "split B")) {
             rc = MXB_E_CUDA;
         } else {
-            g.A_big = ws[0];
-            g.A_small = ws[1];
-            g.B_big = ws[2];
-            g.B_small = ws[3];
+            g.A_small = ws[0];
+            g.B_small = ws[1];
         }
     }
     if (rc == MXB_OK && !cuda_ok(launch_fused_gemm(g, stream), "fused GEMM launch")) rc = MXB_E_CUDA;

@@ -149,19 +149,27 @@ __device__ __forceinline__ void tmem_ld_wait() {
 
 // ---------------------------------------------------------------- descriptors
 
-// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm_100
-// version field = 1.  Addresses and byte offsets are encoded >> 4.
-//  K-major operand (rows of 128 B along K, 8-row atoms):  lbo unused, sbo = atom stride.
-//  MN-major operand (128 B along MN per k-row):           lbo = stride between 128-B wide
-//                                                          MN blocks, sbo = 8-k-row atom stride.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes,
-                                                    uint32_t sbo_bytes) {
+// Shared-memory matrix descriptor (sm_100 version field = 1); addresses and
+// byte offsets are encoded >> 4.  Two layouts are used:
+//  * kLayoutSW128 (type 2), K-major operand: rows of 128 B along K, 16-byte
+//    chunks XOR-swizzled over 8-row (1 KiB) atoms.  lbo unused, sbo = atom
+//    stride.  Matches a TMA load with CU_TENSOR_MAP_SWIZZLE_128B.
+//  * kLayoutSW128Base32B (type 1), MN-major 32-bit operand: 128 B along MN
+//    per k-row, 32-byte chunks XOR-swizzled over 4-row (512 B) atoms.  lbo =
+//    stride between 128-B wide MN blocks, sbo = stride between 4-k-row atoms.
+//    Matches a TMA load with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.  (MN-major
+//    TF32 reads nothing but zeros through the plain 128-B layout.)
+constexpr uint32_t kLayoutSW128 = 2;
+constexpr uint32_t kLayoutSW128Base32B = 1;
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout) {
     uint64_t d = 0;
     d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
     d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
     d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
     d |= static_cast<uint64_t>(1) << 46;  // descriptor version (sm_100)
-    d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
+    d |= static_cast<uint64_t>(layout & 7u) << 61;
     return d;
 }
 

@@ -21,7 +21,7 @@ from minixla_b200 import datagen
 from minixla_b200 import lib as mlib
 from minixla_b200.abi import OP_ADD, OP_MUL, OP_RELU, HostGraph, free_host_tensor, tensor_to_numpy
 from oracle import bindings
-from tests.golden.cases import KNOWN_ANSWERS, all_cases
+from tests.golden.cases import DEPTH, KNOWN_ANSWERS, all_cases
 from tests.graph_eval import HostBuilder, host_graph, oracle_eval, rel_frobenius
 
 pytestmark = pytest.mark.gpu
@@ -42,13 +42,14 @@ def run_execute(lib, ctx, root, precision):
         free_host_tensor(t)
 
 
-def check(got, want, precision, what="", band=None):
+def check(got, want, precision, what="", band=None, depth=1):
     assert got.shape == want.shape, what
     assert not np.isnan(got).any(), f"{what}: NaN in GPU output"
+    tol = depth * TOL[precision]
     err = rel_frobenius(got, want)
-    assert err <= TOL[precision], f"{what}: relative Frobenius {err:.3g} > {TOL[precision]:g}"
+    assert err <= tol, f"{what}: relative Frobenius {err:.3g} > {tol:g}"
     # Zero / sign agreement after relu: only where the oracle is clearly away from 0.
-    band = band if band is not None else 50 * TOL[precision] * (np.abs(want).max() + 1e-30)
+    band = band if band is not None else 50 * tol * (np.abs(want).max() + 1e-30)
     clear = np.abs(want) > band
     assert np.array_equal(np.sign(got[clear]), np.sign(want[clear])), f"{what}: sign flips"
     return err
@@ -64,7 +65,7 @@ def test_golden_case(lib, gpu_ctx, golden, case, precision):
     hg, root = host_graph(inputs, build)
     got = run_execute(lib, gpu_ctx, root, precision)
     want = golden[f"{name}:__out__"]
-    check(got, want, precision, name)
+    check(got, want, precision, name, depth=DEPTH.get(name, 1))
     if name in KNOWN_ANSWERS:  # small integers: exact in every mode
         assert np.array_equal(got.reshape(-1), np.array(KNOWN_ANSWERS[name], dtype=np.float32))
 
@@ -99,7 +100,7 @@ def test_reference_graph_through_optimize(lib, gpu_ctx, precision):
         want = rg.execute(root)
     finally:
         rg.close()
-    check(got, want, precision, "mlp via optimize()")
+    check(got, want, precision, "mlp via optimize()", depth=DEPTH["mlp_small"])
 
 
 # ---------------------------------------------------------------- gpu_test.c mirrors
@@ -390,6 +391,7 @@ def test_unsupported_ops_fail_loudly(lib, gpu_ctx):
     assert not lib.gpu_execute(bad_add, gpu_ctx)
 
 
+# Allocation order of the first call: A, B, C, out, then the two 3xTF32 low-part buffers.
 _OOM_CHILD = r"""
 import sys, numpy as np
 sys.path.insert(0, sys.argv[1])
@@ -415,7 +417,7 @@ print("OK")
 """
 
 
-@pytest.mark.parametrize("fail_at", [1, 3, 5, 7])
+@pytest.mark.parametrize("fail_at", [1, 3, 4, 5, 6])
 def test_allocation_failure_injection(fail_at):
     env = dict(os.environ, MINIXLA_FAIL_ALLOC_AT=str(fail_at))
     r = subprocess.run([sys.executable, "-c", _OOM_CHILD, str(ROOT)], env=env, capture_output=True, text=True,
