@@ -191,6 +191,26 @@ MXB_API int mxb_fused_gemm(GpuCtx* ctx,
                    const mxb_ep_step* steps, int n_steps,
                    int precision, void* stream);
 
+/* The 3xTF32 fused GEMM for callers that cannot allocate device memory.  No
+ * counterpart in the reference.  Some callers must not call cudaMalloc: a
+ * plugin inside a framework that owns the whole device-memory budget through
+ * its own allocator, or a latency-critical serving loop, where cudaMalloc /
+ * cudaFree synchronise the device.  This entry point allocates nothing and
+ * needs no GpuCtx: the low parts of A and B live in a fixed 16 MiB device
+ * array inside the library (held by every GPU that loads it until exit), so
+ * M*lda + K*ldb must not exceed 4 Mi floats (else MXB_E_ARG).  Same operands,
+ * layout rules and epilogue steps as mxb_fused_gemm; runs on the current
+ * device and on `stream` (NULL = the legacy default stream), and returns once
+ * the work on that stream is finished.  The first call on a device looks up
+ * the array's device address; make it before any stream capture.  Calls share
+ * the array, so calls that overlap on the GPU race and must be serialised. */
+MXB_API int mxb_fused_gemm_noalloc(const float* A, long long lda,
+                                   const float* B, long long ldb,
+                                   float* out, long long ldo,
+                                   int M, int N, int K,
+                                   const mxb_ep_step* steps, int n_steps,
+                                   void* stream);
+
 /* Standalone element-wise nodes (tensor.c:64-86 and 110-120 semantics):
  * out[i] = a[i] + b[i % b_size]  and  out[i] = x[i] > 0 ? x[i] : 0. */
 MXB_API int mxb_add(GpuCtx* ctx, const float* a, long long n, const float* b, long long b_size,

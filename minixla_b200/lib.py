@@ -40,6 +40,11 @@ PROTOTYPES = {
         [C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong,
          C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p],
     ),
+    "mxb_fused_gemm_noalloc": (
+        C.c_int,
+        [C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong,
+         C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p],
+    ),
     "mxb_add": (C.c_int, [C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]),
     "mxb_relu": (C.c_int, [C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]),
     "mxb_check_device_error": (C.c_int, [C.c_void_p]),
