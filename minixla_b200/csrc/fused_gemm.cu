@@ -39,6 +39,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "internal.h"
@@ -444,6 +446,225 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ------------------------------------------------------------------ CTA-pair kernel (TF32)
+//
+// Pair tile 256 x 256 on a 2-CTA cluster (the two SMs of a TPC).  CTA r owns
+// output rows m0 + 128 r .. +128; per k-block it stages its 128 rows of A and
+// B columns n0 + 128 r .. +128 (half of the tile's B).  The leader (rank 0)
+// issues tcgen05.mma.cta_group::2 (M=256, N=256, K=8), which reads the A and
+// B halves from both CTAs' shared memory and leaves each CTA's 128 x 256
+// accumulator in that CTA's TMEM.  Per SM that halves the B bytes staged and
+// read per MMA, so a stage is 32 KiB and six stages fit.
+//
+// Barriers: full[s] lives in the leader and counts both CTAs' TMA bytes (the
+// peer's loads signal it through its cluster address); empty[s] and tfull[a]
+// live in both CTAs and receive the leader's multicast commits; tempty[a]
+// lives in the leader and takes one arrival per epilogue warp of either CTA.
+
+constexpr int kPairBN = 256;
+
+template <int STAGES>
+struct PairCfg {
+    static constexpr int kABytes = 128 * kBK * 4;                // 16 KiB: this CTA's A rows
+    static constexpr int kBBytes = (kPairBN / 2) * kBK * 4;      // 16 KiB: this CTA's B columns
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kTmemCols = 2 * kPairBN;
+    static constexpr int kBarOffset = STAGES * kStageBytes;
+    static constexpr int kNumBars = 2 * STAGES + 5;
+    static constexpr int kSmemBytes = 1024 + kBarOffset + kNumBars * 8 + 16;
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+template <int STAGES>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    fused_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           const __grid_constant__ FusedParams p) {
+    using C = PairCfg<STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t bar0 = smem_addr(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1;
+    const int num_pairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), 8);  // 4 epilogue warps in each of the two CTAs
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_addr(tmem_slot), C::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer (both CTAs)
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            long long issued = 0;
+            bool ok = true;
+            for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+                int mb, nb;
+                tile_coords(t, p, mb, nb);
+                const int m0 = mb * 256 + static_cast<int>(rank) * 128;
+                const int n0 = nb * kPairBN + static_cast<int>(rank) * (kPairBN / 2);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (*abort_flag) { ok = false; break; }
+                    if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1u, p.timeout_ns)) {
+                        raise_error(p, abort_flag, kErrProducer);
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = smem + stage * C::kStageBytes;
+                    if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * C::kStageBytes);
+                    const uint32_t fb = mapa_shared(full_bar(stage), 0);
+                    const int k0 = kb * kBK;
+                    tma_load_2d_pair(smem_addr(st), &tmA, fb, k0, m0);
+#pragma unroll
+                    for (int j = 0; j < kPairBN / 64; ++j)
+                        tma_load_2d_pair(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb, n0 + 32 * j, k0);
+                    ++issued;
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!ok && rank == 0) {
+                // The leader's full barriers count both CTAs' bytes: wait for the copies in flight.
+                const long long n = issued < STAGES ? issued : STAGES;
+                for (long long i = 1; i <= n; ++i) {
+                    const long long idx = issued - i;
+                    mbar_wait_cluster(full_bar(static_cast<int>(idx % STAGES)),
+                                      static_cast<uint32_t>((idx / STAGES) & 1), p.timeout_ns);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer (leader only)
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_tf32(256, kPairBN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+                if (*abort_flag) break;
+                if (!mbar_wait_cluster(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns)) {
+                    raise_error(p, abort_flag, kErrMma);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kPairBN);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait_cluster(full_bar(stage), phase, p.timeout_ns)) {
+                        raise_error(p, abort_flag, kErrMma);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_addr(smem + stage * C::kStageBytes);
+                    const uint32_t b_addr = a_addr + C::kABytes;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 8; ++kk) {
+                        const uint64_t da = smem_desc(a_addr + kk * 32, 16, 1024, kLayoutSW128);
+                        const uint64_t db = smem_desc(b_addr + kk * 1024, kBoxBytes, 512, kLayoutSW128Base32B);
+                        mma_tf32_pair(d_tmem, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    mma_commit_pair(empty_bar(stage), 0x3);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                mma_commit_pair(tfull_bar(acc), 0x3);
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            mma_commit_pair(drain_bar, 0x1);
+            if (!mbar_wait_cluster(drain_bar, 0, p.timeout_ns)) raise_error(p, abort_flag, kErrMma);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        const int quad = warp & 3;
+        const int row_in_tile = static_cast<int>(rank) * 128 + quad * 32 + lane;
+        const uint32_t tempty_leader0 = mapa_shared(tempty_bar(0), 0);
+        const uint32_t tempty_leader1 = mapa_shared(tempty_bar(1), 0);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = pair; t < p.num_tiles; t += num_pairs) {
+            const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
+            const bool got = !stop && mbar_wait_cluster(tfull_bar(acc), acc_phase, p.timeout_ns);
+            if (!__all_sync(0xffffffffu, got)) {
+                if (lane == 0 && !stop) raise_error(p, abort_flag, kErrEpilogue);
+                break;
+            }
+            tc_fence_after();
+            int mb, nb;
+            tile_coords(t, p, mb, nb);
+            const int row = mb * 256 + row_in_tile;
+            const bool row_ok = row < p.M;
+            const int col0 = nb * kPairBN;
+            int chunks = (p.N - col0 + 31) / 32;
+            if (chunks > kPairBN / 32) chunks = kPairBN / 32;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                   static_cast<uint32_t>(acc * kPairBN);
+            for (int c = 0; c < chunks; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(taddr + 32 * c, r);
+                tmem_ld_wait();
+                if (c == chunks - 1) {
+                    // This warp is done with the accumulator: tell the leader's MMA warp.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+                }
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                const int col = col0 + 32 * c;
+                apply_epilogue(v, row, col, row_ok, p);
+                if (row_ok) store_row_chunk(v, row, col, p);
+            }
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, C::kTmemCols);
+    }
+}
+
 // ------------------------------------------------------------------ host side
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -538,11 +759,96 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
+template <int STAGES>
+cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
+    using C = PairCfg<STAGES>;
+    auto kernel = fused_gemm_pair_kernel<STAGES>;
+    static std::mutex mu;
+    static uint64_t configured = 0;
+    static int max_clusters[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    int clusters = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (dev >= 64 || !(configured & (1ull << dev))) {
+            e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+            if (e != cudaSuccess) return e;
+            // How many 2-CTA clusters fit at once with this much shared memory.
+            cudaLaunchConfig_t cfg = {};
+            cudaLaunchAttribute attr;
+            attr.id = cudaLaunchAttributeClusterDimension;
+            attr.val.clusterDim.x = 2;
+            attr.val.clusterDim.y = 1;
+            attr.val.clusterDim.z = 1;
+            cfg.gridDim = dim3(2 * (g.num_sms / 2), 1, 1);
+            cfg.blockDim = dim3(kThreads, 1, 1);
+            cfg.dynamicSmemBytes = C::kSmemBytes;
+            cfg.attrs = &attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n < 1) {
+                cudaGetLastError();
+                n = g.num_sms / 2;
+            }
+            if (dev < 64) {
+                max_clusters[dev] = n;
+                configured |= 1ull << dev;
+            }
+            clusters = n;
+        } else {
+            clusters = max_clusters[dev];
+        }
+    }
+
+    constexpr CUtensorMapSwizzle kSwA = CU_TENSOR_MAP_SWIZZLE_128B;
+    constexpr CUtensorMapSwizzle kSwB = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    CUtensorMap mA, mB;
+    if (!make_map(&mA, g.A, g.M, g.K, g.lda, kBK, 128, kSwA) || !make_map(&mB, g.B, g.K, g.N, g.ldb, 32, kBK, kSwB))
+        return cudaErrorInvalidValue;
+
+    FusedParams p{};
+    p.out = g.out;
+    p.ldo = g.ldo;
+    p.M = g.M;
+    p.N = g.N;
+    p.K = g.K;
+    p.n_steps = g.n_steps;
+    p.tiles_m = (g.M + 255) / 256;
+    p.tiles_n = (g.N + kPairBN - 1) / kPairBN;
+    p.num_tiles = p.tiles_m * p.tiles_n;
+    p.num_kb = (g.K + kBK - 1) / kBK;
+    p.group_m = 8;
+    p.seg_kb = p.num_kb;
+    p.timeout_ns = g.timeout_ns;
+    p.err = g.err;
+    for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
+
+    const int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;
+    kernel<<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(mA, mB, p);
+    note_launch();
+    return cudaGetLastError();
+}
+
+// Which TF32 kernel: the CTA-pair kernel once there are enough 256 x 256
+// tiles to occupy the SMs, else the single-CTA kernel (128 x 256 or 128 x 128
+// tiles spread over more SMs).  MINIXLA_GEMM_VARIANT=pair|single overrides.
+bool use_pair_kernel(const GemmLaunch& g) {
+    if (const char* v = getenv("MINIXLA_GEMM_VARIANT")) {
+        if (!strcmp(v, "pair")) return true;
+        if (!strcmp(v, "single")) return false;
+    }
+    const long long pair_tiles = static_cast<long long>((g.M + 255) / 256) * ((g.N + 255) / 256);
+    return g.M >= 256 && pair_tiles >= g.num_sms / 4;
+}
+
 }  // namespace
 
 cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
     if (g.precision == GPU_PRECISION_3XTF32) return run_variant<128, 3, true, true>(g, stream);
-    // One TF32 product.  Narrow or small problems use 128-wide tiles so more SMs get work.
+    if (use_pair_kernel(g)) return run_pair_variant<6>(g, stream);
+    // One TF32 product on one CTA.  Narrow or small problems use 128-wide tiles so more SMs get work.
     const long long tiles_m = (g.M + kBM - 1) / kBM;
     const long long tiles256 = tiles_m * ((g.N + 255) / 256);
     const long long tiles128 = tiles_m * ((g.N + 127) / 128);

@@ -322,6 +322,25 @@ def test_full_size_checksums(lib, gpu_ctx, precision):
     assert rel_frobenius(got.sum(1), row_want) < tol
 
 
+@pytest.mark.parametrize("variant", ["pair", "single"])
+@pytest.mark.parametrize("mnk", [(256, 256, 32), (300, 520, 100), (1000, 1000, 1000), (257, 4097, 129),
+                                 (8191, 127, 3000), (2048, 2048, 2048), (4096, 300, 1024)])
+def test_tf32_kernel_variants(lib, gpu_ctx, mnk, variant, monkeypatch, host_threads):
+    """Both TF32 kernels (CTA pair, single CTA) on tile-edge shapes, with a
+    full-matrix add, a bias row and relu in the epilogue."""
+    monkeypatch.setenv("MINIXLA_GEMM_VARIANT", variant)
+    M, N, K = mnk
+    A, B, C = _relu_abc(M, N, K, c_normal=True)
+    bias = datagen.normal((N,), 5, 0.0, 0.5)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A), hg.input_node(B),
+                         [(OP_ADD, hg.input_node(C)), (OP_RELU, None), (OP_ADD, hg.input_node(bias))])
+    got = run_execute(lib, gpu_ctx, root, TF32)
+    rows = None if M * N * K <= 2048 ** 3 else _sample_rows(M, 256)
+    want = bindings.fused_oracle(A, B, [("add", C), ("relu",), ("add", bias)], rows=rows, threads=host_threads)
+    check(got if rows is None else got[rows], want, TF32, f"{variant} {mnk}")
+
+
 # ---------------------------------------------------------------- device-pointer API
 
 
