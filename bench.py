@@ -369,25 +369,24 @@ def ours_arm(args, rank, local_rank, world):
     if not rel <= tol:
         raise RuntimeError(f"bench result check failed: relative error {rel:.3g} > {tol}")
 
-    # cuBLAS TF32 on the same shape, for context only (not on the product path)
+    # cuBLAS TF32 on the same shape, for context only (not on the product path):
+    # the same number of back-to-back steps, so both run under the same power cap.
     cublas = None
     if rank == 0:
         torch.backends.cuda.matmul.allow_tf32 = True
-        x = A_d[:, :].contiguous()
-        for _ in range(3):
-            torch.matmul(x, B_d)
+        with torch.cuda.stream(stream):
+            ref_out = torch.empty_like(out_d)
+            for _ in range(args.warmup):
+                torch.matmul(A_d, B_d, out=ref_out)
+            c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c0.record(stream)
+            for _ in range(args.steps):
+                torch.matmul(A_d, B_d, out=ref_out)
+            c1.record(stream)
         torch.cuda.synchronize()
-        best = math.inf
-        for _ in range(5):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            torch.matmul(x, B_d)
-            e1.record()
-            torch.cuda.synchronize()
-            best = min(best, e0.elapsed_time(e1))
-        cublas = flops_rank / (best * 1e-3) / 1e12
+        cublas = flops_rank * args.steps / (c0.elapsed_time(c1) * 1e-3) / 1e12
         torch.backends.cuda.matmul.allow_tf32 = False
-        del x
+        del ref_out
     del out_d
     torch.cuda.empty_cache()
 
@@ -446,7 +445,7 @@ def ours_arm(args, rank, local_rank, world):
                          "peak_source": peak_src, "kernel_ms": per_launch_ms},
             "cpu_baseline": cpu,
             "clocks": clocks,
-            "cublas_tf32_tflops_same_shape": cublas,
+            "cublas_tf32_matmul_tflops_same_shape_same_steps": cublas,
             "result_check_rel_err": rel,
         }
         print(json.dumps(line), flush=True)
