@@ -218,10 +218,13 @@ struct GpuCtx {
     int num_sms = 148;
     int precision = GPU_PRECISION_3XTF32;
     unsigned long long timeout_ns = 5ull * 1000 * 1000 * 1000;
-    cudaStream_t stream = nullptr;
+    cudaStream_t stream = nullptr;   // kernels
+    cudaStream_t h2d = nullptr;      // host-to-device copies of the row-streamed executor
+    cudaStream_t d2h = nullptr;      // device-to-host copies of the row-streamed executor
     int* d_err = nullptr;
     mxb::DevicePool* pool = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    std::vector<cudaEvent_t> sync_events;  // reusable ordering events (no timing)
 };
 
 namespace mxb {
@@ -417,7 +420,7 @@ static bool tma_operand(GpuCtx* ctx, const float* src, long long rows, long long
 // 3xTF32 the low parts of A and B (x - rne_tf32(x)) go to pooled workspace first.
 static int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
                        long long ldo, int M, int N, int K, const EpStepDev* steps, int n_steps, int precision,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, const float* B_small_pre = nullptr) {
     GemmLaunch g{};
     g.A = A;
     g.lda = lda;
@@ -439,15 +442,16 @@ static int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* 
     if (precision == GPU_PRECISION_3XTF32) {
         const size_t a_bytes = static_cast<size_t>(M) * lda * 4, b_bytes = static_cast<size_t>(K) * ldb * 4;
         ws[0] = static_cast<float*>(ctx->pool->alloc(a_bytes, stream));
-        ws[1] = ws[0] ? static_cast<float*>(ctx->pool->alloc(b_bytes, stream)) : nullptr;
-        if (!ws[1]) {
+        if (ws[0] && !B_small_pre) ws[1] = static_cast<float*>(ctx->pool->alloc(b_bytes, stream));
+        if (!ws[0] || (!B_small_pre && !ws[1])) {
             rc = MXB_E_NOMEM;
         } else if (!cuda_ok(launch_split_tf32(A, M, K, lda, ws[0], lda, ctx->num_sms, stream), "split A") ||
-                   !cuda_ok(launch_split_tf32(B, K, N, ldb, ws[1], ldb, ctx->num_sms, stream), "split B")) {
+                   (!B_small_pre &&
+                    !cuda_ok(launch_split_tf32(B, K, N, ldb, ws[1], ldb, ctx->num_sms, stream), "split B"))) {
             rc = MXB_E_CUDA;
         } else {
             g.A_small = ws[0];
-            g.B_small = ws[1];
+            g.B_small = B_small_pre ? B_small_pre : ws[1];
         }
     }
     if (rc == MXB_OK && !cuda_ok(launch_fused_gemm(g, stream), "fused GEMM launch")) rc = MXB_E_CUDA;
@@ -552,6 +556,239 @@ static Tensor* new_host_tensor(const std::vector<int>& dims) {
     return t;
 }
 
+// ---------------------------------------------------------------- row streaming
+//
+// When every computed node is row-wise in one row count M -- a GEMM's output
+// rows follow the rows of its A operand (B is needed whole), add / relu rows
+// follow their inputs -- the graph runs in row chunks.  Leaves needed whole
+// (B operands, bias rows) are uploaded first; leaves whose rows follow M are
+// uploaded chunk by chunk on a copy stream, each chunk's kernels start on the
+// compute stream as soon as its rows have landed, and each chunk's result rows
+// go back on a second copy stream, so copies in both directions overlap the
+// arithmetic.  Graphs that need an intermediate whole (as a B operand, or
+// through eval_fused's modulo rule) keep the one-stream executor.
+
+struct RowStreamPlan {
+    bool ok = false;
+    int M = 0;
+    std::vector<char> chunked;  // per node (leaves only): upload by row chunks
+};
+
+static bool rows_follow(const Info& f, int M) { return f.dims.size() == 2 && f.dims[0] == M; }
+
+static RowStreamPlan plan_row_stream(const std::vector<const Node*>& order,
+                                     const std::unordered_map<const Node*, int>& index,
+                                     const std::vector<Info>& info) {
+    RowStreamPlan plan;
+    const size_t n = order.size();
+    if (order.back()->op == OP_INPUT || info.back().dims.size() != 2) return plan;
+    const int M = info.back().dims[0];
+    std::vector<char> whole(n, 0), rowwise(n, 0);
+    auto row_source = [&](int i) { return order[i]->op == OP_INPUT ? rows_follow(info[i], M) : rowwise[i] != 0; };
+    for (size_t i = 0; i < n; ++i) {
+        const Node* nd = order[i];
+        const Info& f = info[i];
+        if (nd->op == OP_INPUT) continue;
+        if (!rows_follow(f, M)) return plan;
+        if (nd->op == OP_FUSED || nd->op == OP_MATMUL) {
+            const int ia = index.at(nd->inputs[0]), ib = index.at(nd->inputs[1]);
+            whole[ib] = 1;
+            if (!row_source(ia) || info[ia].dims[1] % 4 || info[ib].dims[1] % 4) return plan;
+            if (nd->op == OP_FUSED) {
+                for (int e = 0; e < nd->n_epilogue; ++e) {
+                    if (nd->epilogue[e].op != OP_ADD) continue;
+                    const int io = index.at(nd->epilogue[e].operand);
+                    if (info[io].size == f.size) {
+                        if (!(row_source(io) && info[io].dims == f.dims)) return plan;
+                    } else if (info[io].size == f.dims[1]) {
+                        whole[io] = 1;
+                    } else {
+                        return plan;  // modulo-rule operand: indexed by the global row
+                    }
+                }
+            }
+        } else if (nd->op == OP_ADD) {
+            const int ia = index.at(nd->inputs[0]), ib = index.at(nd->inputs[1]);
+            if (!row_source(ia)) return plan;
+            if (info[ib].size == f.size) {
+                if (!row_source(ib)) return plan;
+            } else {
+                whole[ib] = 1;  // trailing-suffix row of length dims[1]
+            }
+        } else if (nd->op == OP_RELU) {
+            if (!row_source(index.at(nd->inputs[0]))) return plan;
+        } else {
+            return plan;
+        }
+        rowwise[i] = 1;
+    }
+    plan.chunked.assign(n, 0);
+    for (size_t i = 0; i < n; ++i) {
+        if (order[i]->op != OP_INPUT) {
+            if (whole[i]) return plan;
+        } else if (!whole[i] && rows_follow(info[i], M)) {
+            plan.chunked[i] = 1;
+        }
+    }
+    plan.ok = true;
+    plan.M = M;
+    return plan;
+}
+
+static cudaEvent_t sync_event(GpuCtx* ctx, size_t k) {
+    while (ctx->sync_events.size() <= k) {
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        ctx->sync_events.push_back(e);
+    }
+    return ctx->sync_events[k];
+}
+
+// Runs a graph that plan_row_stream accepted; the root's rows are written to
+// `host_dst` (root.size floats).
+static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
+                            const std::unordered_map<const Node*, int>& index, std::vector<Info>& info,
+                            const RowStreamPlan& plan, int chunks, float* host_dst) {
+    cudaStream_t cs = ctx->stream, hs = ctx->h2d, ds = ctx->d2h;
+    const int M = plan.M;
+    const int rows_per = std::max(128, (M + chunks - 1) / chunks);
+    const int n_chunks = (M + rows_per - 1) / rows_per;
+    const size_t n = order.size();
+    std::vector<float*> b_small(n, nullptr);
+    size_t next_event = 0;
+    int rc = MXB_OK;
+    auto order_after = [&](cudaStream_t waiter, cudaStream_t signaller) {
+        cudaEvent_t e = sync_event(ctx, next_event++);
+        if (!e || cudaEventRecord(e, signaller) != cudaSuccess || cudaStreamWaitEvent(waiter, e, 0) != cudaSuccess) {
+            set_error("row streaming: event ordering failed");
+            return false;
+        }
+        return true;
+    };
+
+    for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
+        info[i].dev = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(info[i].size) * 4, cs));
+        if (!info[i].dev) rc = MXB_E_NOMEM;
+    }
+    // Uploads may touch pooled blocks only after the compute stream's earlier work on them.
+    if (rc == MXB_OK && !order_after(hs, cs)) rc = MXB_E_CUDA;
+    for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
+        if (order[i]->op == OP_INPUT && !plan.chunked[i] &&
+            !cuda_ok(cudaMemcpyAsync(info[i].dev, order[i]->output->data, static_cast<size_t>(info[i].size) * 4,
+                                     cudaMemcpyHostToDevice, hs),
+                     "input upload"))
+            rc = MXB_E_CUDA;
+    }
+    if (rc == MXB_OK && !order_after(cs, hs)) rc = MXB_E_CUDA;
+    // 3xTF32: the low part of every B operand, once for all chunks.
+    for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
+        const Node* nd = order[i];
+        if (ctx->precision != GPU_PRECISION_3XTF32 || (nd->op != OP_FUSED && nd->op != OP_MATMUL)) continue;
+        const Info& b = info[index.at(nd->inputs[1])];
+        b_small[i] = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(b.size) * 4, cs));
+        if (!b_small[i]) {
+            rc = MXB_E_NOMEM;
+        } else if (!cuda_ok(launch_split_tf32(b.dev, b.dims[0], b.dims[1], b.dims[1], b_small[i], b.dims[1],
+                                              ctx->num_sms, cs),
+                            "split B")) {
+            rc = MXB_E_CUDA;
+        }
+    }
+    std::vector<cudaEvent_t> computed(n_chunks, nullptr);
+    for (int c = 0; c < n_chunks && rc == MXB_OK; ++c) {
+        const long long r0 = static_cast<long long>(c) * rows_per;
+        const long long r1 = std::min<long long>(M, r0 + rows_per);
+        for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
+            if (!plan.chunked[i]) continue;
+            const long long cols = info[i].size / M;
+            if (!cuda_ok(cudaMemcpyAsync(info[i].dev + r0 * cols, order[i]->output->data + r0 * cols,
+                                         static_cast<size_t>((r1 - r0) * cols) * 4, cudaMemcpyHostToDevice, hs),
+                         "chunk upload"))
+                rc = MXB_E_CUDA;
+        }
+        if (rc == MXB_OK && !order_after(cs, hs)) rc = MXB_E_CUDA;
+        for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
+            const Node* nd = order[i];
+            const Info& f = info[i];
+            const long long cols = f.dims.size() == 2 ? f.dims[1] : 0;
+            if (nd->op == OP_FUSED || nd->op == OP_MATMUL) {
+                const Info& a = info[index.at(nd->inputs[0])];
+                const Info& b = info[index.at(nd->inputs[1])];
+                const int K = a.dims[1], N = b.dims[1];
+                EpStepDev steps[MXB_MAX_EPILOGUE];
+                int n_steps = 0;
+                for (int e = 0; nd->op == OP_FUSED && e < nd->n_epilogue; ++e) {
+                    const EpStep& st = nd->epilogue[e];
+                    EpStepDev d{};
+                    if (st.op == OP_ADD) {
+                        const Info& o = info[index.at(st.operand)];
+                        d.kind = o.size == f.size ? MXB_EP_ADD_FULL : MXB_EP_ADD_ROW;
+                        d.ptr = o.size == f.size ? o.dev + r0 * N : o.dev;
+                        d.ld_or_size = N;
+                    } else if (st.op == OP_RELU) {
+                        d.kind = MXB_EP_RELU;
+                    } else {
+                        continue;
+                    }
+                    steps[n_steps++] = d;
+                }
+                rc = launch_gemm(ctx, a.dev + r0 * K, K, b.dev, N, f.dev + r0 * N, N, static_cast<int>(r1 - r0), N, K,
+                                 steps, n_steps, ctx->precision, cs, b_small[i]);
+            } else if (nd->op == OP_ADD) {
+                const Info& a = info[index.at(nd->inputs[0])];
+                const Info& b = info[index.at(nd->inputs[1])];
+                const bool same = b.size == f.size;
+                if (!cuda_ok(launch_add(a.dev + r0 * cols, (r1 - r0) * cols, same ? b.dev + r0 * cols : b.dev,
+                                        same ? (r1 - r0) * cols : b.size, f.dev + r0 * cols, ctx->num_sms, cs),
+                             "add launch"))
+                    rc = MXB_E_CUDA;
+            } else if (nd->op == OP_RELU) {
+                const Info& a = info[index.at(nd->inputs[0])];
+                if (!cuda_ok(launch_relu(a.dev + r0 * cols, (r1 - r0) * cols, f.dev + r0 * cols, ctx->num_sms, cs),
+                             "relu launch"))
+                    rc = MXB_E_CUDA;
+            }
+        }
+        if (rc == MXB_OK) {
+            computed[c] = sync_event(ctx, next_event++);
+            if (!computed[c] || cudaEventRecord(computed[c], cs) != cudaSuccess) rc = MXB_E_CUDA;
+        }
+    }
+    // Downloads are enqueued after all uploads and kernels: with a pageable
+    // destination each copy blocks the host until it is done.
+    const Info& root = info.back();
+    const long long out_cols = root.size / M;
+    for (int c = 0; c < n_chunks && rc == MXB_OK; ++c) {
+        const long long r0 = static_cast<long long>(c) * rows_per;
+        const long long r1 = std::min<long long>(M, r0 + rows_per);
+        if (cudaStreamWaitEvent(ds, computed[c], 0) != cudaSuccess ||
+            !cuda_ok(cudaMemcpyAsync(host_dst + r0 * out_cols, root.dev + r0 * out_cols,
+                                     static_cast<size_t>((r1 - r0) * out_cols) * 4, cudaMemcpyDeviceToHost, ds),
+                     "chunk download"))
+            rc = MXB_E_CUDA;
+    }
+    // The pool reuses blocks in compute-stream order: join both copy streams first.
+    order_after(cs, ds);
+    order_after(cs, hs);
+    for (size_t i = 0; i < n; ++i) {
+        ctx->pool->release(info[i].dev, cs);
+        ctx->pool->release(b_small[i], cs);
+        info[i].dev = nullptr;
+    }
+    cudaStreamSynchronize(ds);
+    cudaStreamSynchronize(hs);
+    const int done = finish(ctx);
+    return rc != MXB_OK ? rc : done;
+}
+
+static int stream_chunks() {
+    const char* c = getenv("MINIXLA_STREAM_CHUNKS");
+    return c ? atoi(c) : 8;
+}
+
 // The DAG executor behind gpu_execute / gpu_execute_into.  When `dst` is
 // given the root is downloaded into it (its size must match), otherwise a
 // new host tensor is returned through *result.
@@ -566,6 +803,36 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
     std::unordered_map<const Node*, int> index;
     std::vector<Info> info;
     if (!infer_shapes(order, index, info)) return MXB_E_UNSUPPORTED;
+
+    const int chunks = stream_chunks();
+    if (chunks > 1 && info.back().dims.size() == 2 && info.back().dims[0] >= 2 * 128) {
+        const RowStreamPlan plan = plan_row_stream(order, index, info);
+        if (plan.ok) {
+            if (dst) {
+                if (!dst->data || static_cast<long long>(dst->size) != info.back().size) {
+                    set_error("gpu_execute_into: destination holds %zu elements, result has %lld",
+                              static_cast<size_t>(dst->size), info.back().size);
+                    return MXB_E_ARG;
+                }
+                return execute_streamed(ctx, order, index, info, plan, chunks, dst->data);
+            }
+            Tensor* t = new_host_tensor(info.back().dims);
+            if (!t) {
+                set_error("gpu_execute: host allocation of the result failed");
+                return MXB_E_NOMEM;
+            }
+            const int rc = execute_streamed(ctx, order, index, info, plan, chunks, t->data);
+            if (rc != MXB_OK) {
+                free(t->data);
+                free(t->shape);
+                free(t->strides);
+                free(t);
+                return rc;
+            }
+            *result = t;
+            return MXB_OK;
+        }
+    }
 
     std::unordered_map<const Node*, const float*> dev_of;
     std::unordered_map<const Node*, long long> size_of;
@@ -857,6 +1124,8 @@ GpuCtx* gpu_ctx_create_on(int device) {
     }
     bool ok = cuda_ok(cudaFree(nullptr), "context init") &&
               cuda_ok(cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking), "stream create") &&
+              cuda_ok(cudaStreamCreateWithFlags(&g->h2d, cudaStreamNonBlocking), "stream create") &&
+              cuda_ok(cudaStreamCreateWithFlags(&g->d2h, cudaStreamNonBlocking), "stream create") &&
               cuda_ok(cudaMalloc(&g->d_err, sizeof(int)), "error word alloc") &&
               cuda_ok(cudaMemset(g->d_err, 0, sizeof(int)), "error word clear") &&
               cuda_ok(cudaEventCreate(&g->ev0), "event create") && cuda_ok(cudaEventCreate(&g->ev1), "event create");
@@ -883,6 +1152,9 @@ void gpu_ctx_destroy(GpuCtx* g) {
         if (g->d_err) cudaFree(g->d_err);
         if (g->ev0) cudaEventDestroy(g->ev0);
         if (g->ev1) cudaEventDestroy(g->ev1);
+        for (cudaEvent_t e : g->sync_events) cudaEventDestroy(e);
+        if (g->h2d) cudaStreamDestroy(g->h2d);
+        if (g->d2h) cudaStreamDestroy(g->d2h);
         if (g->stream) cudaStreamDestroy(g->stream);
     }
     delete g;
