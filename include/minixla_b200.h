@@ -131,6 +131,21 @@ MXB_API Tensor* gpu_run_fused(const Node* fused, const char* ptx);
 
 /* Context on a given CUDA device (one process per GPU).  NULL on failure. */
 MXB_API GpuCtx* gpu_ctx_create_on(int device);
+/* One context driving GPUs 0..ngpu-1 from this thread (gpu_ctx_create does
+ * the same when $MINIXLA_NGPU > 1).  gpu_execute then splits the rows of
+ * every row-wise node over the GPUs: leaves read whole (B operands, bias
+ * rows) are uploaded once and replicated by peer copies over NVLink, row
+ * leaves are uploaded shard by shard, each GPU computes its rows, and result
+ * rows go from each GPU straight into the host tensor; an NCCL all-gather
+ * runs only when a later node reads an intermediate whole.  Graphs that are
+ * not row-wise run on GPU 0.  All other entry points use GPU 0.  NULL on
+ * failure. */
+MXB_API GpuCtx* gpu_ctx_create_multi(int ngpu);
+/* Number of GPUs a context drives (1 unless made by gpu_ctx_create_multi). */
+MXB_API int     gpu_ctx_ngpu(const GpuCtx* ctx);
+/* The row split a multi-GPU context uses: part p of `parts` gets rows
+ * [r0, r1) of M, the first M % parts parts one row more.  0 or MXB_E_ARG. */
+MXB_API int     mxb_shard_rows(long long M, int parts, int part, long long* r0, long long* r1);
 /* Sets / reads the precision used by gpu_execute, gpu_time_kernel_ms and
  * gpu_run_fused.  The initial mode comes from $MINIXLA_PRECISION ("tf32" or
  * "3xtf32"), else 3xTF32.  Returns 0, or -1 for an unknown mode. */

@@ -65,6 +65,7 @@ struct FusedParams {
     int tiles_m, tiles_n, num_tiles, num_kb;
     int group_m;
     int seg_kb;                     // k-blocks per accumulation segment (num_kb: one segment)
+    long long row_base;             // global index of row 0 of this launch (modulo-rule operands)
     unsigned long long timeout_ns;
     int* err;
     EpStepDev steps[MXB_MAX_EPILOGUE];
@@ -163,7 +164,7 @@ __device__ __forceinline__ void apply_epilogue(float (&v)[32], int row, int col,
             if (!row_ok) continue;
             const unsigned long long size = static_cast<unsigned long long>(p.steps[s].ld_or_size);
             const unsigned long long base =
-                static_cast<unsigned long long>(row) * static_cast<unsigned long long>(p.N) + col;
+                static_cast<unsigned long long>(row + p.row_base) * static_cast<unsigned long long>(p.N) + col;
 #pragma unroll
             for (int i = 0; i < 32; ++i)
                 if (col + i < p.N) v[i] += __ldg(ptr + (base + i) % size);
@@ -749,6 +750,7 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.num_kb = (g.K + kBK - 1) / kBK;
     p.group_m = 16;
     p.seg_kb = SEG ? kSegKb : p.num_kb;
+    p.row_base = g.row_base;
     p.timeout_ns = g.timeout_ns;
     p.err = g.err;
     for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
@@ -821,6 +823,7 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.num_kb = (g.K + kBK - 1) / kBK;
     p.group_m = 8;
     p.seg_kb = p.num_kb;
+    p.row_base = g.row_base;
     p.timeout_ns = g.timeout_ns;
     p.err = g.err;
     for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];

@@ -28,6 +28,7 @@ struct GemmLaunch {
     const float* B_small;
     float* out; long long ldo;
     int M, N, K;
+    long long row_base;                // global index of row 0 (rows of a larger matrix)
     const EpStepDev* steps; int n_steps;
     int precision;                     // GPU_PRECISION_TF32 / GPU_PRECISION_3XTF32
     int* err;                          // device error word
