@@ -52,6 +52,8 @@ def parse():
     p.add_argument("--workload", choices=["weak", "config5"], default="weak")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    p.add_argument("--sweep", action="store_true",
+                   help="time every BASELINE shape (kernel only, operands resident); one JSON line per shape")
     p.add_argument("--shape", type=int, default=0,
                    help="per-GPU M = N = K override (profiling on a smaller case); 0 = 8192")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -455,9 +457,125 @@ def ours_arm(args, rank, local_rank, world):
     return 0
 
 
+SWEEP_SHAPES = [  # (M, N, K, C distribution) -- BASELINE configs 1-3 and config 5 on one GPU
+    (128, 128, 128, "uniform"),
+    (512, 512, 512, "normal"), (1024, 1024, 1024, "normal"), (2048, 2048, 2048, "normal"),
+    (4096, 4096, 4096, "normal"), (8192, 8192, 8192, "normal"),
+    (1000, 1000, 1000, "uniform"), (257, 4097, 129, "uniform"), (8191, 127, 3000, "uniform"),
+    (1, 4096, 4096, "uniform"), (32768, 8192, 8192, "normal"),
+]
+
+
+def run_sweep(args):
+    """Kernel-only time of relu(A.B + C) for every BASELINE shape, both
+    precision modes, operands resident (min and median of CUDA-event-timed
+    launches after warm-up), plus the 3-layer MLP DAG of config 4 through the
+    device API (one launch per fused node)."""
+    import numpy as np
+    import torch
+
+    from minixla_b200 import datagen
+    from minixla_b200 import lib as mlib
+
+    lib = mlib.load()
+    ctx = lib.gpu_ctx_create_on(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.Stream(dev)
+    peak, _ = measured_tf32_peak()
+
+    def pad4(x):
+        # TMA needs 16-byte row pitches: pad the columns as gpu_execute does.
+        cols = x.shape[1]
+        if cols % 4 == 0:
+            return x, cols
+        p = torch.zeros((x.shape[0], (cols + 3) // 4 * 4), device=dev)
+        p[:, :cols] = x
+        return p, p.shape[1]
+
+    def time_launches(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return min(ts), statistics.median(ts)
+
+    for M, N, K, cdist in SWEEP_SHAPES:
+        A = torch.from_numpy(datagen.uniform((M, K), 0)).to(dev)
+        B = torch.from_numpy(datagen.uniform((K, N), 1)).to(dev)
+        Cm = torch.from_numpy(datagen.normal((M, N), 2) if cdist == "normal" else datagen.uniform((M, N), 2)).to(dev)
+        out = torch.empty((M, N), device=dev)
+        Ap, lda = pad4(A)
+        Bp, ldb = pad4(B)
+        steps = (mlib.EpStepDev * 2)()
+        steps[0] = mlib.EpStepDev(mlib.MXB_EP_ADD_FULL, 0, Cm.data_ptr(), N, 0.0, 0)
+        steps[1] = mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0)
+        flops = 2.0 * M * N * K
+        algo_bytes = 4.0 * (M * K + K * N + 2 * M * N)
+        for prec_name, prec in (("tf32", mlib.GPU_PRECISION_TF32), ("3xtf32", mlib.GPU_PRECISION_3XTF32)):
+            def fn():
+                rc = lib.mxb_fused_gemm(ctx, Ap.data_ptr(), lda, Bp.data_ptr(), ldb, out.data_ptr(), N, M, N, K,
+                                        steps, 2, prec, stream.cuda_stream)
+                assert rc == 0, mlib.last_error()
+            reps = 20 if flops < 1e12 else 5
+            tmin, tmed = time_launches(fn, reps)
+            pk = peak if prec == mlib.GPU_PRECISION_TF32 else peak / 3
+            print(json.dumps({"sweep": "fused relu(A.B+C)", "M": M, "N": N, "K": K, "precision": prec_name,
+                              "ms_min": tmin, "ms_median": tmed, "tflops": flops / (tmin * 1e-3) / 1e12,
+                              "frac_tensor_peak": flops / (tmin * 1e-3) / 1e12 / pk,
+                              "gbs": algo_bytes / (tmin * 1e-3) / 1e9}), flush=True)
+        del A, B, Cm, out, Ap, Bp
+        torch.cuda.empty_cache()
+
+    # config 4: 3-layer MLP, one launch per fused node (+ the bare matmul)
+    Mx, D, H = 4096, 1024, 4096
+    X = torch.from_numpy(datagen.uniform((Mx, D), 70)).to(dev)
+    W1 = torch.from_numpy(datagen.normal((D, H), 71, 0.0, 1.0 / np.sqrt(D))).to(dev)
+    W2 = torch.from_numpy(datagen.normal((H, H), 72, 0.0, 1.0 / np.sqrt(H))).to(dev)
+    W2p = torch.from_numpy(datagen.normal((H, H), 73, 0.0, 1.0 / np.sqrt(H))).to(dev)
+    W3 = torch.from_numpy(datagen.normal((H, D), 74, 0.0, 1.0 / np.sqrt(H))).to(dev)
+    b1, b2, b3 = (torch.from_numpy(datagen.normal((n,), s, 0.0, 0.1)).to(dev) for n, s in ((H, 75), (H, 76), (D, 77)))
+    h = torch.empty((Mx, H), device=dev)
+    hw = torch.empty((Mx, H), device=dev)
+    y = torch.empty((Mx, H), device=dev)
+    o = torch.empty((Mx, D), device=dev)
+
+    def st(*items):
+        arr = (mlib.EpStepDev * max(1, len(items)))()
+        for i, it in enumerate(items):
+            arr[i] = it
+        return arr, len(items)
+
+    s1 = st(mlib.EpStepDev(mlib.MXB_EP_ADD_ROW, 0, b1.data_ptr(), H, 0.0, 0), mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0))
+    s2 = st(mlib.EpStepDev(mlib.MXB_EP_ADD_ROW, 0, b2.data_ptr(), H, 0.0, 0), mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0),
+            mlib.EpStepDev(mlib.MXB_EP_ADD_FULL, 0, hw.data_ptr(), H, 0.0, 0))
+    s3 = st(mlib.EpStepDev(mlib.MXB_EP_ADD_ROW, 0, b3.data_ptr(), D, 0.0, 0))
+    for prec_name, prec in (("tf32", mlib.GPU_PRECISION_TF32), ("3xtf32", mlib.GPU_PRECISION_3XTF32)):
+        def mlp():
+            for a, lda, b, n, k, outp, (arr, ns) in (
+                    (X, D, W1, H, D, h, s1), (h, H, W2p, H, H, hw, st()), (h, H, W2, H, H, y, s2), (y, H, W3, D, H, o, s3)):
+                rc = lib.mxb_fused_gemm(ctx, a.data_ptr(), lda, b.data_ptr(), n, outp.data_ptr(), n, Mx, n, k, arr, ns,
+                                        prec, stream.cuda_stream)
+                assert rc == 0, mlib.last_error()
+        tmin, tmed = time_launches(mlp, 10)
+        flops = 2.0 * Mx * (D * H + 2 * H * H + H * D)
+        print(json.dumps({"sweep": "3-layer MLP DAG (4 GEMM launches)", "M": Mx, "D": D, "H": H, "precision": prec_name,
+                          "ms_min": tmin, "ms_median": tmed, "tflops": flops / (tmin * 1e-3) / 1e12}), flush=True)
+    lib.gpu_ctx_destroy(ctx)
+    return 0
+
+
 def main():
     args = parse()
     rank, local_rank, world = env_rank()
+    if args.sweep:
+        return run_sweep(args)
     if args.impl == "reference":
         return reference_arm(args, rank, world)
     return ours_arm(args, rank, local_rank, world)
