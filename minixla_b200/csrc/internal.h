@@ -36,6 +36,19 @@ struct GemmLaunch {
     int num_sms;
 };
 
+// Skinny GEMM (skinny_gemm.cu): few output rows, CUDA-core fp32, split over
+// column blocks x K ranges; workspace holds splits * M * N floats.
+constexpr int kSkinnyMaxRows = 16;
+struct SkinnyPlan {
+    int col_blocks = 1;
+    int splits = 1;
+    int k_per_split = 1;
+};
+SkinnyPlan plan_skinny(int M, int N, int K, int num_sms);
+cudaError_t launch_skinny_gemm(const float* A, long long lda, const float* B, long long ldb, float* out, long long ldo,
+                               int M, int N, int K, long long row_base, const EpStepDev* steps, int n_steps,
+                               float* workspace, const SkinnyPlan& plan, int num_sms, cudaStream_t stream);
+
 // Kernel launchers (fused_gemm.cu, elementwise.cu).  Return cudaError_t.
 cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream);
 cudaError_t launch_split_tf32(const float* x, long long rows, long long cols, long long ld_in,

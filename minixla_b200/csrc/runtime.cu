@@ -426,6 +426,20 @@ static bool tma_operand(GpuCtx* ctx, const float* src, long long rows, long long
 static int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
                        long long ldo, int M, int N, int K, const EpStepDev* steps, int n_steps, int precision,
                        cudaStream_t stream, const float* B_small_pre = nullptr, long long row_base = 0) {
+    if (M <= kSkinnyMaxRows) {
+        // Few rows: HBM-bound on B, CUDA-core fp32 split over columns and K.
+        const SkinnyPlan pl = plan_skinny(M, N, K, ctx->num_sms);
+        float* ws = static_cast<float*>(
+            ctx->pool->alloc(static_cast<size_t>(pl.splits) * M * N * sizeof(float), stream));
+        if (!ws) return MXB_E_NOMEM;
+        const int rc = cuda_ok(launch_skinny_gemm(A, lda, B, ldb, out, ldo, M, N, K, row_base, steps, n_steps, ws, pl,
+                                                  ctx->num_sms, stream),
+                               "skinny GEMM launch")
+                           ? MXB_OK
+                           : MXB_E_CUDA;
+        ctx->pool->release(ws, stream);
+        return rc;
+    }
     GemmLaunch g{};
     g.row_base = row_base;
     g.A = A;

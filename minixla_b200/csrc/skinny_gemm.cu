@@ -1,0 +1,163 @@
+// Skinny fused GEMM for few output rows (M <= 16): out = epi(A[M,K] @ B[K,N]).
+//
+// With one to a few rows the work is reading B (4*K*N bytes); a 128-row
+// tensor-core tile would idle most of the MMA and cover too few SMs.  This
+// path is HBM-bound CUDA-core fp32:
+//   1. partial kernel: grid = column blocks x K splits, sized to ~4 CTAs per
+//      SM.  Each CTA stages its rows of A for its k-range in shared memory;
+//      each thread owns four consecutive columns, reads one float4 of each B
+//      row (a warp reads 512 contiguous bytes per row) and accumulates
+//      M x 4 sums in registers.  Partial sums go to pooled workspace
+//      [splits][M][N].
+//   2. reduce kernel: sums the splits in a fixed order (deterministic), then
+//      applies the node's epilogue steps in order and stores once.
+// fp32 multiply-adds: at least as accurate as either precision mode.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "internal.h"
+
+namespace mxb {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kColsPerCta = kThreads * 4;
+constexpr int kMaxSmemFloats = 12 * 1024;  // 48 KiB of staged A
+
+template <int MR>
+__global__ void __launch_bounds__(kThreads)
+    skinny_partial_kernel(const float* __restrict__ A, long long lda, const float* __restrict__ B, long long ldb,
+                          float* __restrict__ partial, int M, int N, int K, int k_per_split) {
+    extern __shared__ float sA[];  // [M][k_per_split]
+    const int k0 = blockIdx.y * k_per_split;
+    const int k1 = min(K, k0 + k_per_split);
+    const int kl = k1 - k0;
+    for (int i = threadIdx.x; i < M * kl; i += kThreads) {
+        const int m = i / kl, kk = i - m * kl;
+        sA[m * k_per_split + kk] = A[static_cast<long long>(m) * lda + k0 + kk];
+    }
+    __syncthreads();
+    const int col = (blockIdx.x * kThreads + threadIdx.x) * 4;
+    if (col >= N) return;
+    float acc[MR][4];
+#pragma unroll
+    for (int m = 0; m < MR; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.0f;
+    const bool vec = col + 3 < N && (ldb & 3) == 0 && (reinterpret_cast<uintptr_t>(B) & 15) == 0;
+    const float* bp = B + static_cast<long long>(k0) * ldb + col;
+#pragma unroll 4
+    for (int k = 0; k < kl; ++k, bp += ldb) {
+        float4 b;
+        if (vec) {
+            b = __ldcs(reinterpret_cast<const float4*>(bp));
+        } else {
+            b.x = bp[0];
+            b.y = col + 1 < N ? bp[1] : 0.0f;
+            b.z = col + 2 < N ? bp[2] : 0.0f;
+            b.w = col + 3 < N ? bp[3] : 0.0f;
+        }
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+            if (m < M) {
+                const float a = sA[m * k_per_split + k];
+                acc[m][0] = fmaf(a, b.x, acc[m][0]);
+                acc[m][1] = fmaf(a, b.y, acc[m][1]);
+                acc[m][2] = fmaf(a, b.z, acc[m][2]);
+                acc[m][3] = fmaf(a, b.w, acc[m][3]);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+        if (m >= M) break;
+        float* dst = partial + (static_cast<long long>(blockIdx.y) * M + m) * N + col;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            if (col + c < N) dst[c] = acc[m][c];
+    }
+}
+
+struct SkinnyEpilogue {
+    int n_steps;
+    EpStepDev steps[MXB_MAX_EPILOGUE];
+};
+
+__global__ void __launch_bounds__(kThreads)
+    skinny_reduce_kernel(const float* __restrict__ partial, int splits, float* __restrict__ out, long long ldo, int M,
+                         int N, long long row_base, const __grid_constant__ SkinnyEpilogue epi) {
+    const long long total = static_cast<long long>(M) * N;
+    for (long long idx = blockIdx.x * static_cast<long long>(kThreads) + threadIdx.x; idx < total;
+         idx += static_cast<long long>(gridDim.x) * kThreads) {
+        const int m = static_cast<int>(idx / N), n = static_cast<int>(idx - static_cast<long long>(m) * N);
+        float x = 0.0f;
+        for (int s = 0; s < splits; ++s) x += partial[(static_cast<long long>(s) * M + m) * N + n];
+        for (int i = 0; i < epi.n_steps; ++i) {
+            const EpStepDev& st = epi.steps[i];
+            if (st.kind == MXB_EP_ADD_FULL) {
+                x += st.ptr[static_cast<long long>(m) * st.ld_or_size + n];
+            } else if (st.kind == MXB_EP_ADD_ROW) {
+                x += st.ptr[n];
+            } else if (st.kind == MXB_EP_ADD_MOD) {
+                const unsigned long long flat =
+                    static_cast<unsigned long long>(m + row_base) * static_cast<unsigned long long>(N) + n;
+                x += st.ptr[flat % static_cast<unsigned long long>(st.ld_or_size)];
+            } else if (st.kind == MXB_EP_RELU) {
+                x = x > 0.0f ? x : 0.0f;
+            } else if (st.kind == MXB_EP_SCALE) {
+                x = x * st.scale;
+            }
+        }
+        out[static_cast<long long>(m) * ldo + n] = x;
+    }
+}
+
+template <int MR>
+cudaError_t launch_partial(const SkinnyPlan& pl, const float* A, long long lda, const float* B, long long ldb,
+                           float* partial, int M, int N, int K, cudaStream_t stream) {
+    const dim3 grid(pl.col_blocks, pl.splits);
+    const size_t smem = static_cast<size_t>(M) * pl.k_per_split * sizeof(float);
+    skinny_partial_kernel<MR><<<grid, kThreads, smem, stream>>>(A, lda, B, ldb, partial, M, N, K, pl.k_per_split);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+SkinnyPlan plan_skinny(int M, int N, int K, int num_sms) {
+    SkinnyPlan p;
+    p.col_blocks = (N + kColsPerCta - 1) / kColsPerCta;
+    int splits = (4 * num_sms + p.col_blocks - 1) / p.col_blocks;
+    splits = std::max(1, std::min(splits, (K + 31) / 32));
+    int kps = (K + splits - 1) / splits;
+    const int kps_cap = std::max(32, kMaxSmemFloats / std::max(1, M));
+    if (kps > kps_cap) kps = kps_cap;
+    p.k_per_split = kps;
+    p.splits = (K + kps - 1) / kps;
+    return p;
+}
+
+cudaError_t launch_skinny_gemm(const float* A, long long lda, const float* B, long long ldb, float* out, long long ldo,
+                               int M, int N, int K, long long row_base, const EpStepDev* steps, int n_steps,
+                               float* workspace, const SkinnyPlan& pl, int num_sms, cudaStream_t stream) {
+    if (M < 1 || M > kSkinnyMaxRows) return cudaErrorInvalidValue;
+    cudaError_t e;
+    if (M == 1) e = launch_partial<1>(pl, A, lda, B, ldb, workspace, M, N, K, stream);
+    else if (M == 2) e = launch_partial<2>(pl, A, lda, B, ldb, workspace, M, N, K, stream);
+    else if (M <= 4) e = launch_partial<4>(pl, A, lda, B, ldb, workspace, M, N, K, stream);
+    else if (M <= 8) e = launch_partial<8>(pl, A, lda, B, ldb, workspace, M, N, K, stream);
+    else e = launch_partial<16>(pl, A, lda, B, ldb, workspace, M, N, K, stream);
+    note_launch();
+    if (e != cudaSuccess) return e;
+    SkinnyEpilogue epi{};
+    epi.n_steps = n_steps;
+    for (int i = 0; i < n_steps; ++i) epi.steps[i] = steps[i];
+    const long long total = static_cast<long long>(M) * N;
+    long long blocks = (total + kThreads - 1) / kThreads;
+    if (blocks > 8ll * num_sms) blocks = 8ll * num_sms;
+    skinny_reduce_kernel<<<static_cast<int>(blocks), kThreads, 0, stream>>>(workspace, pl.splits, out, ldo, M, N, row_base,
+                                                                          epi);
+    note_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace mxb

@@ -369,6 +369,24 @@ def test_row_streamed_executor_matches_one_stream(lib, gpu_ctx, precision, monke
     assert np.array_equal(out, streamed)
 
 
+@pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
+@pytest.mark.parametrize("M", [1, 3, 8, 16])
+def test_skinny_rows_path(lib, gpu_ctx, M, precision, host_threads):
+    """Few output rows run on the split-K CUDA-core path (fp32): every
+    epilogue kind, ragged N, against the oracle at the 3xTF32 tolerance."""
+    N, K = 1000, 777
+    A, B, C = _relu_abc(M, N, K, c_normal=True)
+    bias = datagen.normal((N,), 8, 0.0, 0.5)
+    odd = datagen.uniform((13,), 9)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A), hg.input_node(B),
+                         [(OP_ADD, hg.input_node(C)), (OP_ADD, hg.input_node(odd)), (OP_RELU, None),
+                          (OP_ADD, hg.input_node(bias))])
+    got = run_execute(lib, gpu_ctx, root, precision)
+    want = bindings.fused_oracle(A, B, [("add", C), ("add", odd), ("relu",), ("add", bias)], threads=host_threads)
+    check(got, want, X3, f"skinny M={M}")
+
+
 # ---------------------------------------------------------------- device-pointer API
 
 
