@@ -9,8 +9,11 @@
 //      row (a warp reads 512 contiguous bytes per row) and accumulates
 //      M x 4 sums in registers.  Partial sums go to pooled workspace
 //      [splits][M][N].
-//   2. reduce kernel: sums the splits in a fixed order (deterministic), then
-//      applies the node's epilogue steps in order and stores once.
+//   2. reduce kernel: each CTA takes 32 consecutive outputs; warp g sums a
+//      fixed group of splits for them (coalesced 128-byte rows), the eight
+//      group sums are added in a fixed order (deterministic for a given
+//      split plan), then the node's epilogue steps are applied in order and
+//      each output is stored once.
 // fp32 multiply-adds: at least as accurate as either precision mode.
 #include <cuda_runtime.h>
 
@@ -46,7 +49,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int m = 0; m < MR; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.0f;
     const bool vec = col + 3 < N && (ldb & 3) == 0 && (reinterpret_cast<uintptr_t>(B) & 15) == 0;
     const float* bp = B + static_cast<long long>(k0) * ldb + col;
-#pragma unroll 4
+#pragma unroll 8
     for (int k = 0; k < kl; ++k, bp += ldb) {
         float4 b;
         if (vec) {
@@ -83,32 +86,53 @@ struct SkinnyEpilogue {
     EpStepDev steps[MXB_MAX_EPILOGUE];
 };
 
+constexpr int kReduceGroups = kThreads / 32;
+
 __global__ void __launch_bounds__(kThreads)
     skinny_reduce_kernel(const float* __restrict__ partial, int splits, float* __restrict__ out, long long ldo, int M,
                          int N, long long row_base, const __grid_constant__ SkinnyEpilogue epi) {
+    __shared__ float group_sum[kReduceGroups][32];
     const long long total = static_cast<long long>(M) * N;
-    for (long long idx = blockIdx.x * static_cast<long long>(kThreads) + threadIdx.x; idx < total;
-         idx += static_cast<long long>(gridDim.x) * kThreads) {
-        const int m = static_cast<int>(idx / N), n = static_cast<int>(idx - static_cast<long long>(m) * N);
+    const int lane = threadIdx.x & 31;
+    const int g = threadIdx.x >> 5;
+    const int per = (splits + kReduceGroups - 1) / kReduceGroups;
+    const int s0 = g * per, s1 = min(splits, s0 + per);
+    for (long long base = blockIdx.x * 32ll; base < total; base += static_cast<long long>(gridDim.x) * 32) {
+        const long long idx = base + lane;
         float x = 0.0f;
-        for (int s = 0; s < splits; ++s) x += partial[(static_cast<long long>(s) * M + m) * N + n];
-        for (int i = 0; i < epi.n_steps; ++i) {
-            const EpStepDev& st = epi.steps[i];
-            if (st.kind == MXB_EP_ADD_FULL) {
-                x += st.ptr[static_cast<long long>(m) * st.ld_or_size + n];
-            } else if (st.kind == MXB_EP_ADD_ROW) {
-                x += st.ptr[n];
-            } else if (st.kind == MXB_EP_ADD_MOD) {
-                const unsigned long long flat =
-                    static_cast<unsigned long long>(m + row_base) * static_cast<unsigned long long>(N) + n;
-                x += st.ptr[flat % static_cast<unsigned long long>(st.ld_or_size)];
-            } else if (st.kind == MXB_EP_RELU) {
-                x = x > 0.0f ? x : 0.0f;
-            } else if (st.kind == MXB_EP_SCALE) {
-                x = x * st.scale;
-            }
+        if (idx < total) {
+            const int m = static_cast<int>(idx / N), n = static_cast<int>(idx - static_cast<long long>(m) * N);
+            const float* p = partial + (static_cast<long long>(s0) * M + m) * N + n;
+            const long long stride = static_cast<long long>(M) * N;
+#pragma unroll 4
+            for (int s = s0; s < s1; ++s, p += stride) x += *p;
         }
-        out[static_cast<long long>(m) * ldo + n] = x;
+        group_sum[g][lane] = x;
+        __syncthreads();
+        if (g == 0 && idx < total) {
+            const int m = static_cast<int>(idx / N), n = static_cast<int>(idx - static_cast<long long>(m) * N);
+            float v = group_sum[0][lane];
+#pragma unroll
+            for (int q = 1; q < kReduceGroups; ++q) v += group_sum[q][lane];
+            for (int i = 0; i < epi.n_steps; ++i) {
+                const EpStepDev& st = epi.steps[i];
+                if (st.kind == MXB_EP_ADD_FULL) {
+                    v += st.ptr[static_cast<long long>(m) * st.ld_or_size + n];
+                } else if (st.kind == MXB_EP_ADD_ROW) {
+                    v += st.ptr[n];
+                } else if (st.kind == MXB_EP_ADD_MOD) {
+                    const unsigned long long flat =
+                        static_cast<unsigned long long>(m + row_base) * static_cast<unsigned long long>(N) + n;
+                    v += st.ptr[flat % static_cast<unsigned long long>(st.ld_or_size)];
+                } else if (st.kind == MXB_EP_RELU) {
+                    v = v > 0.0f ? v : 0.0f;
+                } else if (st.kind == MXB_EP_SCALE) {
+                    v = v * st.scale;
+                }
+            }
+            out[static_cast<long long>(m) * ldo + n] = v;
+        }
+        __syncthreads();
     }
 }
 
@@ -126,8 +150,9 @@ cudaError_t launch_partial(const SkinnyPlan& pl, const float* A, long long lda, 
 SkinnyPlan plan_skinny(int M, int N, int K, int num_sms) {
     SkinnyPlan p;
     p.col_blocks = (N + kColsPerCta - 1) / kColsPerCta;
-    int splits = (4 * num_sms + p.col_blocks - 1) / p.col_blocks;
-    splits = std::max(1, std::min(splits, (K + 31) / 32));
+    // About two CTAs per SM, each streaming at least 64 rows of B.
+    int splits = (2 * num_sms + p.col_blocks - 1) / p.col_blocks;
+    splits = std::max(1, std::min(splits, (K + 63) / 64));
     int kps = (K + splits - 1) / splits;
     const int kps_cap = std::max(32, kMaxSmemFloats / std::max(1, M));
     if (kps > kps_cap) kps = kps_cap;
@@ -152,7 +177,7 @@ cudaError_t launch_skinny_gemm(const float* A, long long lda, const float* B, lo
     epi.n_steps = n_steps;
     for (int i = 0; i < n_steps; ++i) epi.steps[i] = steps[i];
     const long long total = static_cast<long long>(M) * N;
-    long long blocks = (total + kThreads - 1) / kThreads;
+    long long blocks = (total + 31) / 32;
     if (blocks > 8ll * num_sms) blocks = 8ll * num_sms;
     skinny_reduce_kernel<<<static_cast<int>(blocks), kThreads, 0, stream>>>(workspace, pl.splits, out, ldo, M, N, row_base,
                                                                           epi);
