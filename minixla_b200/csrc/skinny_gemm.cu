@@ -49,17 +49,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int m = 0; m < MR; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.0f;
     const bool vec = col + 3 < N && (ldb & 3) == 0 && (reinterpret_cast<uintptr_t>(B) & 15) == 0;
     const float* bp = B + static_cast<long long>(k0) * ldb + col;
-#pragma unroll 8
-    for (int k = 0; k < kl; ++k, bp += ldb) {
-        float4 b;
-        if (vec) {
-            b = __ldcs(reinterpret_cast<const float4*>(bp));
-        } else {
-            b.x = bp[0];
-            b.y = col + 1 < N ? bp[1] : 0.0f;
-            b.z = col + 2 < N ? bp[2] : 0.0f;
-            b.w = col + 3 < N ? bp[3] : 0.0f;
-        }
+    auto fma_row = [&](const float4& b, int k) {
 #pragma unroll
         for (int m = 0; m < MR; ++m) {
             if (m < M) {
@@ -69,6 +59,28 @@ __global__ void __launch_bounds__(kThreads)
                 acc[m][2] = fmaf(a, b.z, acc[m][2]);
                 acc[m][3] = fmaf(a, b.w, acc[m][3]);
             }
+        }
+    };
+    int k = 0;
+    if (vec) {
+        // Eight independent row loads in flight per thread, then their FMAs in k order.
+        for (; k + 8 <= kl; k += 8) {
+            float4 b[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) b[u] = __ldcs(reinterpret_cast<const float4*>(bp + static_cast<long long>(u) * ldb));
+            bp += 8 * ldb;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) fma_row(b[u], k + u);
+        }
+        for (; k < kl; ++k, bp += ldb) fma_row(__ldcs(reinterpret_cast<const float4*>(bp)), k);
+    } else {
+        for (; k < kl; ++k, bp += ldb) {
+            float4 b;
+            b.x = bp[0];
+            b.y = col + 1 < N ? bp[1] : 0.0f;
+            b.z = col + 2 < N ? bp[2] : 0.0f;
+            b.w = col + 3 < N ? bp[3] : 0.0f;
+            fma_row(b, k);
         }
     }
 #pragma unroll
@@ -150,9 +162,9 @@ cudaError_t launch_partial(const SkinnyPlan& pl, const float* A, long long lda, 
 SkinnyPlan plan_skinny(int M, int N, int K, int num_sms) {
     SkinnyPlan p;
     p.col_blocks = (N + kColsPerCta - 1) / kColsPerCta;
-    // About two CTAs per SM, each streaming at least 64 rows of B.
-    int splits = (2 * num_sms + p.col_blocks - 1) / p.col_blocks;
-    splits = std::max(1, std::min(splits, (K + 63) / 64));
+    // About four CTAs per SM, each streaming at least 32 rows of B.
+    int splits = (4 * num_sms + p.col_blocks - 1) / p.col_blocks;
+    splits = std::max(1, std::min(splits, (K + 31) / 32));
     int kps = (K + splits - 1) / splits;
     const int kps_cap = std::max(32, kMaxSmemFloats / std::max(1, M));
     if (kps > kps_cap) kps = kps_cap;
