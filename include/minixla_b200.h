@@ -146,6 +146,16 @@ MXB_API int     gpu_ctx_ngpu(const GpuCtx* ctx);
 /* The row split a multi-GPU context uses: part p of `parts` gets rows
  * [r0, r1) of M, the first M % parts parts one row more.  0 or MXB_E_ARG. */
 MXB_API int     mxb_shard_rows(long long M, int parts, int part, long long* r0, long long* r1);
+/* Keeps a host tensor (typically a weight) in device memory: it is uploaded
+ * now, to every GPU of the context, and every later gpu_execute /
+ * gpu_execute_into on this context reads that copy instead of uploading the
+ * leaf again.  The caller must not change the tensor's data while it is
+ * resident (release it and keep it again after a change); a tensor whose
+ * data pointer or size changed since is uploaded as usual.  Resident copies
+ * are freed by gpu_ctx_release_resident or gpu_ctx_destroy.  0 or MXB_E_*. */
+MXB_API int     gpu_ctx_keep_resident(GpuCtx* ctx, const Tensor* t);
+/* Frees the resident copy of `t`, or of every resident tensor when t is NULL. */
+MXB_API int     gpu_ctx_release_resident(GpuCtx* ctx, const Tensor* t);
 /* Sets / reads the precision used by gpu_execute, gpu_time_kernel_ms and
  * gpu_run_fused.  The initial mode comes from $MINIXLA_PRECISION ("tf32" or
  * "3xtf32"), else 3xTF32.  Returns 0, or -1 for an unknown mode. */

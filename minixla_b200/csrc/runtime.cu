@@ -230,6 +230,12 @@ struct GpuCtx {
     std::vector<cudaEvent_t> sync_events;  // reusable ordering events (no timing)
     std::vector<GpuCtx*> peers;            // devices 1..n-1 of a multi-GPU context
     std::vector<ncclComm_t> comms;         // one per device, made on the first all-gather
+    struct Resident {
+        const float* data;                 // host data pointer when kept
+        size_t size;                       // element count when kept
+        std::vector<float*> dev;           // one copy per device (this context, then its peers)
+    };
+    std::unordered_map<const Tensor*, Resident> resident;  // gpu_ctx_keep_resident
 };
 
 namespace mxb {
@@ -242,7 +248,20 @@ struct Info {
     long long size = 0;           // element count
     int last_use = -1;            // index of the last consumer in topo order
     float* dev = nullptr;         // device buffer (compact, row-major)
+    bool borrowed = false;        // dev is a resident copy, not this call's to release
 };
+
+// Device copy of a resident leaf on device `d` of `ctx` (0 = ctx itself,
+// then its peers), or nullptr when the tensor is not resident or its data
+// pointer / size changed since it was kept.
+static float* resident_copy(const GpuCtx* ctx, const Node* n, size_t d) {
+    if (n->op != OP_INPUT || !n->output) return nullptr;
+    auto it = ctx->resident.find(n->output);
+    if (it == ctx->resident.end()) return nullptr;
+    const GpuCtx::Resident& r = it->second;
+    if (r.data != n->output->data || r.size != n->output->size || d >= r.dev.size()) return nullptr;
+    return r.dev[d];
+}
 
 // Post-order DFS over inputs: every node after all of its inputs
 // (graph.c:171-190 defines the same order; this copy does not touch the
@@ -316,18 +335,23 @@ static bool infer_shapes(const std::vector<const Node*>& order,
                 }
                 const Info& a = info[index.at(n->inputs[0])];
                 const Info& b = info[index.at(n->inputs[1])];
-                if (a.dims.size() != 2 || b.dims.size() != 2) {
-                    set_error("gpu_execute: only 2-D matmul operands run on the GPU (got rank %zu x %zu)",
-                              a.dims.size(), b.dims.size());
+                // eval_fused's rule (graph.c:67-77): same rank >= 2, equal batch
+                // dimensions, inner dimensions agree; batches run one after another.
+                const size_t r = a.dims.size();
+                if (r < 2 || b.dims.size() != r || a.dims[r - 1] != b.dims[r - 2]) {
+                    set_error("gpu_execute: incompatible matmul operand shapes (ranks %zu and %zu)", r,
+                              b.dims.size());
                     return false;
                 }
-                if (a.dims[1] != b.dims[0]) {
-                    set_error("gpu_execute: incompatible matmul operand shapes [%d,%d] x [%d,%d]", a.dims[0],
-                              a.dims[1], b.dims[0], b.dims[1]);
-                    return false;
+                for (size_t d = 0; d + 2 < r; ++d) {
+                    if (a.dims[d] != b.dims[d]) {
+                        set_error("gpu_execute: matmul batch dimension %zu mismatch", d);
+                        return false;
+                    }
                 }
-                f.dims = {a.dims[0], b.dims[1]};
-                f.size = static_cast<long long>(a.dims[0]) * b.dims[1];
+                f.dims = a.dims;
+                f.dims[r - 1] = b.dims[r - 1];
+                f.size = product(f.dims);
                 if (n->op == OP_FUSED) {
                     if (n->n_epilogue > MXB_MAX_EPILOGUE) {
                         set_error("gpu_execute: %d epilogue steps exceed the limit of %d", n->n_epilogue,
@@ -480,13 +504,16 @@ static int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* 
 }
 
 // Builds the device epilogue of an OP_FUSED node from its EpSteps
-// (graph.h:17-18): ADD operands become FULL (same element count as the
-// output: flat index i*N+j of the compact operand), ROW ([N]: index j) or
-// MOD (any other size, eval_fused's modulo rule, graph.c:100-105); RELU maps
-// to RELU; other step ops are skipped, as eval_fused skips them.
-static int build_epilogue(const Node* n, int N, long long MN,
+// (graph.h:17-18) for batch `bt` of `batch`.  eval_fused adds
+// op[(bt*M*N + i*N + j) % size] (graph.c:100-105): an operand holding every
+// batch (batch*M*N elements) is FULL at this batch's offset; one holding one
+// M x N block is FULL for every batch; a [N] row is ROW; any other size
+// keeps the modulo rule (MOD, rows counted from bt*M through row_base).
+// RELU maps to RELU; other step ops are skipped, as eval_fused skips them.
+static int build_epilogue(const Node* n, int M, int N, long long batch, long long bt,
                           const std::unordered_map<const Node*, const float*>& dev_of,
                           const std::unordered_map<const Node*, long long>& size_of, EpStepDev* out) {
+    const long long MN = static_cast<long long>(M) * N;
     int k = 0;
     for (int e = 0; e < n->n_epilogue; ++e) {
         const EpStep& s = n->epilogue[e];
@@ -494,7 +521,11 @@ static int build_epilogue(const Node* n, int N, long long MN,
         if (s.op == OP_ADD) {
             const long long sz = size_of.at(s.operand);
             d.ptr = dev_of.at(s.operand);
-            if (sz == MN) {
+            if (sz == batch * MN) {
+                d.kind = MXB_EP_ADD_FULL;
+                d.ptr += bt * MN;
+                d.ld_or_size = N;
+            } else if (sz == MN) {
                 d.kind = MXB_EP_ADD_FULL;
                 d.ld_or_size = N;
             } else if (sz == N) {
@@ -514,20 +545,24 @@ static int build_epilogue(const Node* n, int N, long long MN,
     return k;
 }
 
-// Runs one matmul-anchored node on device buffers.
+// Runs one matmul-anchored node on device buffers: `batch` products of
+// A[M,K] @ B[K,N] stored back to back (batch = 1 for 2-D nodes).
 static int run_gemm_node(GpuCtx* ctx, const Node* n, const float* dA, int M, int K, const float* dB, int N,
                          float* dOut, const std::unordered_map<const Node*, const float*>& dev_of,
                          const std::unordered_map<const Node*, long long>& size_of, int precision,
-                         cudaStream_t stream) {
-    EpStepDev steps[MXB_MAX_EPILOGUE];
-    const int n_steps =
-        n->op == OP_FUSED ? build_epilogue(n, N, static_cast<long long>(M) * N, dev_of, size_of, steps) : 0;
+                         cudaStream_t stream, long long batch = 1) {
     Operand a, b;
     int rc = MXB_OK;
-    if (!tma_operand(ctx, dA, M, K, a, stream) || !tma_operand(ctx, dB, K, N, b, stream)) {
+    // Pitch padding treats the batches as one tall matrix (rows are contiguous).
+    if (!tma_operand(ctx, dA, batch * M, K, a, stream) || !tma_operand(ctx, dB, batch * K, N, b, stream)) {
         rc = MXB_E_NOMEM;
-    } else {
-        rc = launch_gemm(ctx, a.ptr, a.ld, b.ptr, b.ld, dOut, N, M, N, K, steps, n_steps, precision, stream);
+    }
+    for (long long bt = 0; bt < batch && rc == MXB_OK; ++bt) {
+        EpStepDev steps[MXB_MAX_EPILOGUE];
+        const int n_steps = n->op == OP_FUSED ? build_epilogue(n, M, N, batch, bt, dev_of, size_of, steps) : 0;
+        rc = launch_gemm(ctx, a.ptr + bt * M * a.ld, a.ld, b.ptr + bt * K * b.ld, b.ld,
+                         dOut + bt * static_cast<long long>(M) * N, N, M, N, K, steps, n_steps, precision, stream,
+                         nullptr, bt * M);
     }
     ctx->pool->release(a.owned, stream);
     ctx->pool->release(b.owned, stream);
@@ -687,14 +722,21 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
         return true;
     };
 
+    std::vector<char> chunked = plan.chunked;
     for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
+        if (float* res = resident_copy(ctx, order[i], 0)) {
+            info[i].dev = res;
+            info[i].borrowed = true;
+            chunked[i] = 0;
+            continue;
+        }
         info[i].dev = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(info[i].size) * 4, cs));
         if (!info[i].dev) rc = MXB_E_NOMEM;
     }
     // Uploads may touch pooled blocks only after the compute stream's earlier work on them.
     if (rc == MXB_OK && !order_after(hs, cs)) rc = MXB_E_CUDA;
     for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
-        if (order[i]->op == OP_INPUT && !plan.chunked[i] &&
+        if (order[i]->op == OP_INPUT && !chunked[i] && !info[i].borrowed &&
             !cuda_ok(cudaMemcpyAsync(info[i].dev, order[i]->output->data, static_cast<size_t>(info[i].size) * 4,
                                      cudaMemcpyHostToDevice, hs),
                      "input upload"))
@@ -720,7 +762,7 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
         const long long r0 = static_cast<long long>(c) * rows_per;
         const long long r1 = std::min<long long>(M, r0 + rows_per);
         for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
-            if (!plan.chunked[i]) continue;
+            if (!chunked[i]) continue;
             const long long cols = info[i].size / M;
             if (!cuda_ok(cudaMemcpyAsync(info[i].dev + r0 * cols, order[i]->output->data + r0 * cols,
                                          static_cast<size_t>((r1 - r0) * cols) * 4, cudaMemcpyHostToDevice, hs),
@@ -793,7 +835,7 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
     order_after(cs, ds);
     order_after(cs, hs);
     for (size_t i = 0; i < n; ++i) {
-        ctx->pool->release(info[i].dev, cs);
+        if (!info[i].borrowed) ctx->pool->release(info[i].dev, cs);
         ctx->pool->release(b_small[i], cs);
         info[i].dev = nullptr;
     }
@@ -931,15 +973,23 @@ static int execute_sharded(GpuCtx* ctx0, const std::vector<const Node*>& order,
     std::vector<long long> r0(P), r1(P);
     for (int d = 0; d < P; ++d) shard_range(M, P, d, r0[d], r1[d]);
     std::vector<std::vector<float*>> ptr(P, std::vector<float*>(n, nullptr));
+    // Resident leaves are whole on every device already.
+    std::vector<char> full = plan.full, borrowed(n, 0);
+    for (size_t i = 0; i < n; ++i) {
+        if (!resident_copy(ctx0, order[i], 0) || !resident_copy(ctx0, order[i], P - 1)) continue;
+        borrowed[i] = full[i] = 1;
+        for (int d = 0; d < P; ++d) ptr[d][i] = resident_copy(ctx0, order[i], d);
+    }
     auto cols_of = [&](size_t i) { return info[i].dims.size() == 2 ? static_cast<long long>(info[i].dims[1]) : 0ll; };
     // Rows [r0, r1) of node i on device d.
-    auto rows = [&](int d, size_t i) { return plan.full[i] ? ptr[d][i] + r0[d] * cols_of(i) : ptr[d][i]; };
+    auto rows = [&](int d, size_t i) { return full[i] ? ptr[d][i] + r0[d] * cols_of(i) : ptr[d][i]; };
     int rc = MXB_OK;
 
     for (int d = 0; d < P && rc == MXB_OK; ++d) {
         DeviceScope scope(ctxs[d]->device);
         for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
-            const long long elems = plan.full[i] ? info[i].size : (r1[d] - r0[d]) * cols_of(i);
+            if (borrowed[i]) continue;
+            const long long elems = full[i] ? info[i].size : (r1[d] - r0[d]) * cols_of(i);
             if (elems <= 0) continue;
             ptr[d][i] = static_cast<float*>(ctxs[d]->pool->alloc(static_cast<size_t>(elems) * 4, ctxs[d]->stream));
             if (!ptr[d][i]) rc = MXB_E_NOMEM;
@@ -948,9 +998,9 @@ static int execute_sharded(GpuCtx* ctx0, const std::vector<const Node*>& order,
     // Leaves: row shards straight from the host; whole leaves once to device 0, then peer copies.
     size_t ev_k = 0;
     for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
-        if (order[i]->op != OP_INPUT) continue;
+        if (order[i]->op != OP_INPUT || borrowed[i]) continue;
         const float* host = order[i]->output->data;
-        if (!plan.full[i]) {
+        if (!full[i]) {
             for (int d = 0; d < P && rc == MXB_OK; ++d) {
                 if (!ptr[d][i]) continue;
                 DeviceScope scope(ctxs[d]->device);
@@ -1077,7 +1127,8 @@ static int execute_sharded(GpuCtx* ctx0, const std::vector<const Node*>& order,
         DeviceScope scope(ctxs[d]->device);
         const int done = finish(ctxs[d]);
         if (rc == MXB_OK) rc = done;
-        for (size_t i = 0; i < n; ++i) ctxs[d]->pool->release(ptr[d][i], ctxs[d]->stream);
+        for (size_t i = 0; i < n; ++i)
+            if (!borrowed[i]) ctxs[d]->pool->release(ptr[d][i], ctxs[d]->stream);
     }
     return rc;
 }
@@ -1162,7 +1213,12 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
     for (size_t i = 0; i < order.size() && rc == MXB_OK; ++i) {
         const Node* n = order[i];
         Info& f = info[i];
-        f.dev = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(f.size) * 4, stream));
+        if (float* res = resident_copy(ctx, n, 0)) {
+            f.dev = res;
+            f.borrowed = true;
+        } else {
+            f.dev = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(f.size) * 4, stream));
+        }
         if (!f.dev) {
             rc = MXB_E_NOMEM;
             break;
@@ -1171,17 +1227,19 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
         size_of[n] = f.size;
         switch (n->op) {
             case OP_INPUT:
-                if (!cuda_ok(cudaMemcpyAsync(f.dev, n->output->data, static_cast<size_t>(f.size) * 4,
-                                             cudaMemcpyHostToDevice, stream),
-                             "input upload"))
+                if (!f.borrowed && !cuda_ok(cudaMemcpyAsync(f.dev, n->output->data, static_cast<size_t>(f.size) * 4,
+                                                            cudaMemcpyHostToDevice, stream),
+                                            "input upload"))
                     rc = MXB_E_CUDA;
                 break;
             case OP_FUSED:
             case OP_MATMUL: {
                 const Info& a = info[index.at(n->inputs[0])];
                 const Info& b = info[index.at(n->inputs[1])];
-                rc = run_gemm_node(ctx, n, a.dev, a.dims[0], a.dims[1], b.dev, b.dims[1], f.dev, dev_of, size_of,
-                                   ctx->precision, stream);
+                const size_t r = a.dims.size();
+                const long long batch = a.size / (static_cast<long long>(a.dims[r - 2]) * a.dims[r - 1]);
+                rc = run_gemm_node(ctx, n, a.dev, a.dims[r - 2], a.dims[r - 1], b.dev, b.dims[r - 1], f.dev, dev_of,
+                                   size_of, ctx->precision, stream, batch);
                 break;
             }
             case OP_ADD: {
@@ -1205,7 +1263,7 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
         for (int a = 0; a < n->n_inputs; ++a) {
             Info& in = info[index.at(n->inputs[a])];
             if (in.last_use == static_cast<int>(i) && in.dev) {
-                ctx->pool->release(in.dev, stream);
+                if (!in.borrowed) ctx->pool->release(in.dev, stream);
                 in.dev = nullptr;
             }
         }
@@ -1245,7 +1303,7 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
         }
     }
     for (Info& f : info) {
-        if (f.dev) ctx->pool->release(f.dev, stream);
+        if (f.dev && !f.borrowed) ctx->pool->release(f.dev, stream);
         f.dev = nullptr;
     }
     if (rc != MXB_OK) cudaStreamSynchronize(stream);
@@ -1504,6 +1562,63 @@ GpuCtx* gpu_ctx_create(void) {
 
 int gpu_ctx_ngpu(const GpuCtx* ctx) { return ctx ? 1 + static_cast<int>(ctx->peers.size()) : 0; }
 
+static void free_resident(GpuCtx* ctx, GpuCtx::Resident& r) {
+    for (size_t d = 0; d < r.dev.size(); ++d) {
+        GpuCtx* c = d == 0 ? ctx : ctx->peers[d - 1];
+        mxb::DeviceScope scope(c->device);
+        cudaStreamSynchronize(c->stream);
+        if (r.dev[d]) cudaFree(r.dev[d]);
+    }
+    r.dev.clear();
+}
+
+int gpu_ctx_keep_resident(GpuCtx* ctx, const Tensor* t) {
+    if (!ctx || !t || !t->data || t->size == 0) {
+        set_error("gpu_ctx_keep_resident: NULL context or empty tensor");
+        return MXB_E_ARG;
+    }
+    gpu_ctx_release_resident(ctx, t);
+    GpuCtx::Resident r{t->data, t->size, {}};
+    const size_t bytes = t->size * sizeof(float);
+    const size_t ndev = 1 + ctx->peers.size();
+    for (size_t d = 0; d < ndev; ++d) {
+        GpuCtx* c = d == 0 ? ctx : ctx->peers[d - 1];
+        mxb::DeviceScope scope(c->device);
+        float* p = nullptr;
+        if (cudaMalloc(&p, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            c->pool->trim();
+            if (cudaMalloc(&p, bytes) != cudaSuccess) {
+                cudaGetLastError();
+                set_error("gpu_ctx_keep_resident: device allocation of %zu bytes failed", bytes);
+                free_resident(ctx, r);
+                return MXB_E_NOMEM;
+            }
+        }
+        r.dev.push_back(p);
+        if (!cuda_ok(cudaMemcpy(p, t->data, bytes, cudaMemcpyHostToDevice), "resident upload")) {
+            free_resident(ctx, r);
+            return MXB_E_CUDA;
+        }
+    }
+    ctx->resident[t] = std::move(r);
+    return MXB_OK;
+}
+
+int gpu_ctx_release_resident(GpuCtx* ctx, const Tensor* t) {
+    if (!ctx) return MXB_E_ARG;
+    if (!t) {
+        for (auto& kv : ctx->resident) free_resident(ctx, kv.second);
+        ctx->resident.clear();
+        return MXB_OK;
+    }
+    auto it = ctx->resident.find(t);
+    if (it == ctx->resident.end()) return MXB_OK;
+    free_resident(ctx, it->second);
+    ctx->resident.erase(it);
+    return MXB_OK;
+}
+
 int mxb_shard_rows(long long M, int parts, int part, long long* r0, long long* r1) {
     if (M < 0 || parts < 1 || part < 0 || part >= parts || !r0 || !r1) return MXB_E_ARG;
     mxb::shard_range(M, parts, part, *r0, *r1);
@@ -1512,6 +1627,7 @@ int mxb_shard_rows(long long M, int parts, int part, long long* r0, long long* r
 
 void gpu_ctx_destroy(GpuCtx* g) {
     if (!g) return;
+    gpu_ctx_release_resident(g, nullptr);
     if (!g->comms.empty() && mxb::nccl().ok) {
         for (ncclComm_t c : g->comms)
             if (c) mxb::nccl().comm_destroy(c);

@@ -27,6 +27,8 @@ PROTOTYPES = {
     "gpu_ctx_create_on": (C.c_void_p, [C.c_int]),
     "gpu_ctx_create_multi": (C.c_void_p, [C.c_int]),
     "gpu_ctx_ngpu": (C.c_int, [C.c_void_p]),
+    "gpu_ctx_keep_resident": (C.c_int, [C.c_void_p, C.POINTER(Tensor)]),
+    "gpu_ctx_release_resident": (C.c_int, [C.c_void_p, C.POINTER(Tensor)]),
     "mxb_shard_rows": (C.c_int, [C.c_longlong, C.c_int, C.c_int, C.POINTER(C.c_longlong), C.POINTER(C.c_longlong)]),
     "gpu_ctx_destroy": (None, [C.c_void_p]),
     "gpu_execute": (C.POINTER(Tensor), [C.POINTER(Node), C.c_void_p]),

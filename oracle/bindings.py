@@ -86,6 +86,35 @@ def fused_oracle(A: np.ndarray, B: np.ndarray, steps=(), rows=None, f64: bool = 
     return out
 
 
+def fused_oracle_batched(A: np.ndarray, B: np.ndarray, steps=(), f64: bool = False,
+                         threads: int | None = None) -> np.ndarray:
+    """Batched eval_fused (graph.c:80-113): A [..., M, K], B [..., K, N].
+    Batch bt evaluates the rows bt*M .. bt*M+M-1 of A viewed as one tall
+    matrix against its own B; the global row index also drives the ADD
+    operands' modulo rule, exactly as eval_fused's flat index
+    (bt*M*N + i*N + j) % size does."""
+    A = np.ascontiguousarray(A, dtype=np.float32)
+    B = np.ascontiguousarray(B, dtype=np.float32)
+    *batch, M, K = A.shape
+    N = B.shape[-1]
+    nb = int(np.prod(batch)) if batch else 1
+    A2 = A.reshape(nb * M, K)
+    B3 = B.reshape(nb, K, N)
+    out = np.empty((nb * M, N), dtype=np.float64 if f64 else np.float32)
+    arr, keep = _steps(list(steps))
+    for bt in range(nb):
+        rows = np.arange(bt * M, (bt + 1) * M, dtype=np.int64)
+        part = np.empty((M, N), dtype=out.dtype)
+        Bb = np.ascontiguousarray(B3[bt])
+        rc = oracle_lib().oracle_fused_rows(A2.ctypes.data, Bb.ctypes.data, part.ctypes.data, nb * M, N, K,
+                                            rows.ctypes.data, M, arr, len(steps), int(f64),
+                                            threads or os.cpu_count() or 1)
+        if rc != 0:
+            raise RuntimeError("oracle_fused_rows failed")
+        out[bt * M:(bt + 1) * M] = part
+    return out.reshape(*batch, M, N)
+
+
 def add_oracle(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     a = np.ascontiguousarray(a, dtype=np.float32)
     b = np.ascontiguousarray(b, dtype=np.float32)

@@ -153,6 +153,19 @@ def case_mlp_small(M=64, D=32, H=64):
     return "mlp_small", {"X": X, "W1": W1, "W2": W2, "W2p": W2p, "W3": W3, "b1": b1, "b2": b2, "b3": b3}, build
 
 
+def case_batched():
+    """Rank-3 fused node: eval_fused runs batches (graph.c:80-113); ADD
+    operands holding every batch, one M x N block, a [N] row, and an odd size
+    read by the modulo rule over the flat batched index."""
+    bt, M, N, K = 3, 37, 29, 21
+    A, B = _u((bt, M, K), 90), _u((bt, K, N), 91)
+    C, blk = _n((bt, M, N), 92), _u((M, N), 93)
+    bias, odd = _n((N,), 94, 0.0, 0.5), _u((11,), 95)
+    return "batched_rank3", {"A": A, "B": B, "C": C, "blk": blk, "bias": bias, "odd": odd}, \
+        lambda g, t: g.fused(t["A"], t["B"], [("add", t["C"]), ("relu", None), ("add", t["blk"]),
+                                              ("add", t["bias"]), ("add", t["odd"])])
+
+
 def all_cases():
     return [
         case_tests_fused_exec(), case_tests_bias(), case_tests_diamond(),
@@ -160,6 +173,7 @@ def all_cases():
         case_ragged(1, 257, 129, "1x257x129"), case_ragged(129, 127, 33, "129x127x33"),
         case_ragged(257, 264, 129, "257x264x129"), case_ragged(7, 4097, 5, "7x4097x5"),
         case_bias_chain(), case_mod_operand(), case_bare_and_standalone(), case_mlp_small(),
+        case_batched(),
     ]
 
 

@@ -10,16 +10,16 @@ from __future__ import annotations
 import numpy as np
 
 from minixla_b200.abi import OP_ADD, OP_RELU, HostGraph
-from oracle.bindings import add_oracle, fused_oracle, relu_oracle
+from oracle.bindings import add_oracle, fused_oracle, fused_oracle_batched, relu_oracle
 
 
 class OracleBuilder:
     def fused(self, a, b, steps):
         st = [("add", op) if kind == "add" else ("relu",) for kind, op in steps]
-        return fused_oracle(a, b, st)
+        return fused_oracle(a, b, st) if a.ndim == 2 else fused_oracle_batched(a, b, st)
 
     def matmul(self, a, b):
-        return fused_oracle(a, b, [])
+        return fused_oracle(a, b, []) if a.ndim == 2 else fused_oracle_batched(a, b, [])
 
     def add(self, a, b):
         return add_oracle(a, b)

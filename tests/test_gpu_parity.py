@@ -387,6 +387,36 @@ def test_skinny_rows_path(lib, gpu_ctx, M, precision, host_threads):
     check(got, want, X3, f"skinny M={M}")
 
 
+def test_resident_weights(lib, gpu_ctx):
+    """gpu_ctx_keep_resident: the kept copy is read instead of the host data
+    (so a change to the host data is not seen until release + keep), results
+    match the uploading path, a moved data pointer falls back to uploading,
+    and release restores plain behaviour.  Covers the streamed executor
+    (M >= 256) and the one-stream executor (M < 256)."""
+    import ctypes as C
+
+    for M in (512, 64):
+        N, K = 384, 256
+        A, B, Cm = _relu_abc(M, N, K, c_normal=True)
+        hg = HostGraph()
+        bnode = hg.input_node(B)
+        root = hg.fused_node(hg.input_node(A), bnode, [(OP_ADD, hg.input_node(Cm)), (OP_RELU, None)])
+        plain = run_execute(lib, gpu_ctx, root, X3)
+        bt = bnode.contents.output
+        assert lib.gpu_ctx_keep_resident(gpu_ctx, bt) == 0
+        assert np.array_equal(run_execute(lib, gpu_ctx, root, X3), plain)
+        B[:] = 0.0  # host data changes in place: the resident copy is still read
+        assert np.array_equal(run_execute(lib, gpu_ctx, root, X3), plain)
+        assert lib.gpu_ctx_keep_resident(gpu_ctx, bt) == 0  # keep again: picks up the change
+        zero = run_execute(lib, gpu_ctx, root, X3)
+        np.testing.assert_array_equal(zero, np.maximum(Cm, 0))
+        B2 = np.ascontiguousarray(_relu_abc(M, N, K, c_normal=True)[1])
+        bt.contents.data = C.cast(C.c_void_p(B2.ctypes.data), C.POINTER(C.c_float))  # moved data: uploaded
+        np.testing.assert_array_equal(run_execute(lib, gpu_ctx, root, X3), plain)
+        assert lib.gpu_ctx_release_resident(gpu_ctx, None) == 0
+        np.testing.assert_array_equal(run_execute(lib, gpu_ctx, root, X3), plain)
+
+
 # ---------------------------------------------------------------- device-pointer API
 
 

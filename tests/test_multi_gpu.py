@@ -109,3 +109,18 @@ def test_graph_that_does_not_shard_runs_on_gpu0(lib, multi_ctx):
     got = _run(lib, multi_ctx, root, X3)
     want = fused_oracle(X, fused_oracle(P, Q, [("relu",)]), [])
     assert rel_frobenius(got, want) <= 2 * TOL[X3]
+
+
+@needs2
+def test_sharded_with_resident_weight(lib, multi_ctx, gpu_ctx):
+    M, N, K = 2048, 512, 384
+    A, B, C = datagen.uniform((M, K), 30), datagen.uniform((K, N), 31), datagen.normal((M, N), 32)
+    hg = HostGraph()
+    bnode = hg.input_node(B)
+    root = hg.fused_node(hg.input_node(A), bnode, [(OP_ADD, hg.input_node(C)), (OP_RELU, None)])
+    plain = _run(lib, multi_ctx, root, X3)
+    assert lib.gpu_ctx_keep_resident(multi_ctx, bnode.contents.output) == 0
+    kept = _run(lib, multi_ctx, root, X3)
+    assert lib.gpu_ctx_release_resident(multi_ctx, None) == 0
+    assert np.array_equal(plain, kept)
+    assert rel_frobenius(kept, fused_oracle(A, B, [("add", C), ("relu",)])) <= TOL[X3]
