@@ -224,6 +224,7 @@ struct GpuCtx {
     cudaStream_t stream = nullptr;   // kernels
     cudaStream_t h2d = nullptr;      // host-to-device copies of the row-streamed executor
     cudaStream_t d2h = nullptr;      // device-to-host copies of the row-streamed executor
+    std::vector<cudaStream_t> side;  // extra compute streams for independent DAG nodes (made on first use)
     int* d_err = nullptr;
     mxb::DevicePool* pool = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -687,6 +688,8 @@ static RowStreamPlan plan_row_stream(const std::vector<const Node*>& order,
     plan.M = M;
     return plan;
 }
+
+constexpr int kSideStreams = 3;
 
 static cudaEvent_t sync_event(GpuCtx* ctx, size_t k) {
     while (ctx->sync_events.size() <= k) {
@@ -1207,17 +1210,68 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
         }
     }
 
+    // Independent nodes run on different streams (up to 1 + kSideStreams): a
+    // computed node continues the stream of an input whose chain it extends,
+    // else it takes the stream whose last node is oldest.  Inputs made on
+    // another stream are waited on by event, and a buffer goes back to the
+    // pool only after every consumer's stream has passed it.
+    const size_t n_nodes = order.size();
+    if (ctx->side.empty()) {
+        for (int k = 0; k < kSideStreams; ++k) {
+            cudaStream_t st = nullptr;
+            if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
+                cudaGetLastError();
+                break;
+            }
+            ctx->side.push_back(st);
+        }
+    }
+    std::vector<cudaStream_t> streams{stream};
+    streams.insert(streams.end(), ctx->side.begin(), ctx->side.end());
+    const int n_streams = static_cast<int>(streams.size());
+    std::vector<int> stream_of(n_nodes, 0), last_on(n_streams, -1);
+    std::vector<cudaEvent_t> done(n_nodes, nullptr);
+    std::vector<std::vector<int>> inputs_of(n_nodes), consumers(n_nodes);
+    for (size_t i = 0; i < n_nodes; ++i) {
+        for (int a = 0; a < order[i]->n_inputs; ++a) {
+            const int j = index.at(order[i]->inputs[a]);
+            if (std::find(inputs_of[i].begin(), inputs_of[i].end(), j) != inputs_of[i].end()) continue;
+            inputs_of[i].push_back(j);
+            consumers[j].push_back(static_cast<int>(i));
+        }
+    }
+    size_t next_event = 0;
+
     std::unordered_map<const Node*, const float*> dev_of;
     std::unordered_map<const Node*, long long> size_of;
     int rc = MXB_OK;
-    for (size_t i = 0; i < order.size() && rc == MXB_OK; ++i) {
+    for (size_t i = 0; i < n_nodes && rc == MXB_OK; ++i) {
         const Node* n = order[i];
         Info& f = info[i];
+        int sidx = -1;
+        if (n->op == OP_INPUT) {
+            sidx = 0;
+        } else {
+            for (int j : inputs_of[i])
+                if (order[j]->op != OP_INPUT && last_on[stream_of[j]] == j) {
+                    sidx = stream_of[j];
+                    break;
+                }
+            if (sidx < 0) {
+                sidx = 0;
+                for (int k = 1; k < n_streams; ++k)
+                    if (last_on[k] < last_on[sidx]) sidx = k;
+            }
+        }
+        stream_of[i] = sidx;
+        const cudaStream_t st = streams[sidx];
+        for (int j : inputs_of[i])
+            if (stream_of[j] != sidx && done[j]) cudaStreamWaitEvent(st, done[j], 0);
         if (float* res = resident_copy(ctx, n, 0)) {
             f.dev = res;
             f.borrowed = true;
         } else {
-            f.dev = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(f.size) * 4, stream));
+            f.dev = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(f.size) * 4, st));
         }
         if (!f.dev) {
             rc = MXB_E_NOMEM;
@@ -1228,7 +1282,7 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
         switch (n->op) {
             case OP_INPUT:
                 if (!f.borrowed && !cuda_ok(cudaMemcpyAsync(f.dev, n->output->data, static_cast<size_t>(f.size) * 4,
-                                                            cudaMemcpyHostToDevice, stream),
+                                                            cudaMemcpyHostToDevice, st),
                                             "input upload"))
                     rc = MXB_E_CUDA;
                 break;
@@ -1239,19 +1293,19 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
                 const size_t r = a.dims.size();
                 const long long batch = a.size / (static_cast<long long>(a.dims[r - 2]) * a.dims[r - 1]);
                 rc = run_gemm_node(ctx, n, a.dev, a.dims[r - 2], a.dims[r - 1], b.dev, b.dims[r - 1], f.dev, dev_of,
-                                   size_of, ctx->precision, stream, batch);
+                                   size_of, ctx->precision, st, batch);
                 break;
             }
             case OP_ADD: {
                 const Info& a = info[index.at(n->inputs[0])];
                 const Info& b = info[index.at(n->inputs[1])];
-                if (!cuda_ok(launch_add(a.dev, a.size, b.dev, b.size, f.dev, ctx->num_sms, stream), "add launch"))
+                if (!cuda_ok(launch_add(a.dev, a.size, b.dev, b.size, f.dev, ctx->num_sms, st), "add launch"))
                     rc = MXB_E_CUDA;
                 break;
             }
             case OP_RELU: {
                 const Info& a = info[index.at(n->inputs[0])];
-                if (!cuda_ok(launch_relu(a.dev, a.size, f.dev, ctx->num_sms, stream), "relu launch"))
+                if (!cuda_ok(launch_relu(a.dev, a.size, f.dev, ctx->num_sms, st), "relu launch"))
                     rc = MXB_E_CUDA;
                 break;
             }
@@ -1259,15 +1313,29 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
                 rc = MXB_E_UNSUPPORTED;
         }
         if (rc != MXB_OK) break;
-        // Last-use release (gpu_exec.c:520-528), stream-ordered into the pool.
-        for (int a = 0; a < n->n_inputs; ++a) {
-            Info& in = info[index.at(n->inputs[a])];
-            if (in.last_use == static_cast<int>(i) && in.dev) {
-                if (!in.borrowed) ctx->pool->release(in.dev, stream);
-                in.dev = nullptr;
+        done[i] = sync_event(ctx, next_event++);
+        if (!done[i] || cudaEventRecord(done[i], st) != cudaSuccess) {
+            set_error("gpu_execute: event record failed");
+            rc = MXB_E_CUDA;
+            break;
+        }
+        last_on[sidx] = static_cast<int>(i);
+        // Last-use release (gpu_exec.c:520-528), stream-ordered into the pool
+        // after every consumer of the buffer.
+        for (int j : inputs_of[i]) {
+            Info& in = info[j];
+            if (in.last_use != static_cast<int>(i) || !in.dev) continue;
+            if (!in.borrowed) {
+                for (int c : consumers[j])
+                    if (stream_of[c] != sidx && done[c]) cudaStreamWaitEvent(st, done[c], 0);
+                ctx->pool->release(in.dev, st);
             }
+            in.dev = nullptr;
         }
     }
+    // Everything joins the main stream before the result is read.
+    for (int k = 1; k < n_streams; ++k)
+        if (last_on[k] >= 0) cudaStreamWaitEvent(stream, done[last_on[k]], 0);
 
     Info& r = info.back();  // the root is last in post-order
     if (rc == MXB_OK) rc = finish(ctx);
@@ -1641,6 +1709,7 @@ void gpu_ctx_destroy(GpuCtx* g) {
         if (g->ev0) cudaEventDestroy(g->ev0);
         if (g->ev1) cudaEventDestroy(g->ev1);
         for (cudaEvent_t e : g->sync_events) cudaEventDestroy(e);
+        for (cudaStream_t st : g->side) cudaStreamDestroy(st);
         if (g->h2d) cudaStreamDestroy(g->h2d);
         if (g->d2h) cudaStreamDestroy(g->d2h);
         if (g->stream) cudaStreamDestroy(g->stream);

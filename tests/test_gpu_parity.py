@@ -387,6 +387,34 @@ def test_skinny_rows_path(lib, gpu_ctx, M, precision, host_threads):
     check(got, want, X3, f"skinny M={M}")
 
 
+@pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
+def test_wide_dag_on_several_streams(lib, gpu_ctx, precision):
+    """Six independent branches from one input (spread over the executor's
+    streams), joined by standalone adds and a final fused node: exercises
+    the cross-stream waits and the release-after-all-consumers rule."""
+    M, K, N = 96, 200, 136
+    X = datagen.uniform((M, K), 40)
+    Ws = [datagen.normal((K, N), 41 + i, 0.0, 1.0 / np.sqrt(K)) for i in range(6)]
+    bs = [datagen.normal((N,), 51 + i, 0.0, 0.1) for i in range(6)]
+    V = datagen.normal((N, N), 60, 0.0, 1.0 / np.sqrt(N))
+    hg = HostGraph()
+    x = hg.input_node(X)
+    hs = [hg.fused_node(x, hg.input_node(W), [(OP_ADD, hg.input_node(b)), (OP_RELU, None)]) for W, b in zip(Ws, bs)]
+    acc = hs[0]
+    for h in hs[1:]:
+        acc = hg.g_add(acc, h)
+    root = hg.fused_node(acc, hg.input_node(V), [(OP_ADD, hs[2]), (OP_RELU, None)])
+    got = run_execute(lib, gpu_ctx, root, precision)
+    h_ref = [bindings.fused_oracle(X, W, [("add", b), ("relu",)]) for W, b in zip(Ws, bs)]
+    a_ref = h_ref[0]
+    for h in h_ref[1:]:
+        a_ref = bindings.add_oracle(a_ref, h)
+    want = bindings.fused_oracle(a_ref, V, [("add", h_ref[2]), ("relu",)])
+    check(got, want, precision, "wide DAG", depth=2)
+    again = run_execute(lib, gpu_ctx, root, precision)
+    assert np.array_equal(got, again)
+
+
 def test_resident_weights(lib, gpu_ctx):
     """gpu_ctx_keep_resident: the kept copy is read instead of the host data
     (so a change to the host data is not seen until release + keep), results
