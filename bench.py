@@ -7,7 +7,9 @@ One step = one fused relu(A.B + C) over one batch of rows, fp32 in and out.
 Workload: every GPU owns an 8192-row shard of A and C with the full 8192 x 8192
 B (weak scaling: the single-GPU case is the 8192^3 headline shape; at 4 GPUs
 the job is the 32768 x 8192 x 8192 row-sharded shape).  Output rows stay on
-their GPU; no collective runs on the data path.  `--workload config5` runs the
+their GPU; no collective runs on the data path (at N > 1 an NCCL all-gather of
+the output rows is timed after the kernel steps and reported apart, as
+`allgather`).  `--workload config5` runs the
 fixed 32768 x 8192 x 8192 job split over N GPUs instead (strong scaling).
 
 ours:      `value` = whole-job TFLOP/s with inputs resident in HBM, K launches of
@@ -253,6 +255,50 @@ def measured_tf32_peak():
         return 1590.0 / 2.0, "fallback bf16 burst 1590 TFLOP/s / 2"
 
 
+SPEC_TF32_TFLOPS = 1125.0  # B200 nominal dense TF32 (half the 2.25 PFLOP/s dense bf16 figure)
+
+
+def time_allgather(out_d, world, m_total, stream, warmup, steps, max_over_ranks):
+    """NCCL all-gather of every rank's [M, N] output rows into [m_total, N] on
+    the bench stream: mean CUDA-event time per gather, max over ranks.  Every
+    rank runs the same number of gathers."""
+    import torch
+    import torch.distributed as dist
+
+    M, N = out_d.shape
+    full = torch.empty((m_total, N), device=out_d.device, dtype=out_d.dtype)
+    equal = M * world == m_total
+    with torch.cuda.stream(stream):
+        if equal:
+            def gather():
+                dist.all_gather_into_tensor(full, out_d)
+        else:
+            sizes = [torch.zeros(1, device=out_d.device, dtype=torch.int64) for _ in range(world)]
+            dist.all_gather(sizes, torch.tensor([M], device=out_d.device, dtype=torch.int64))
+            parts = list(torch.split(full, [int(s.item()) for s in sizes]))
+
+            def gather():
+                dist.all_gather([p for p in parts], out_d)
+        for _ in range(max(1, warmup)):
+            gather()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            gather()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    total_bytes = 4.0 * m_total * N
+    recv = total_bytes - 4.0 * M * N
+    del full
+    return {"ms_per_step": ms, "bytes_gathered": int(total_bytes), "bytes_received_per_gpu": int(recv),
+            "algbw_GBs": total_bytes / (ms * 1e-3) / 1e9,
+            "busbw_GBs": total_bytes * (world - 1) / world / (ms * 1e-3) / 1e9,
+            "collective": "torch.distributed all_gather_into_tensor (NCCL)", "in_value": False}
+
+
 def traffic_from_profile(precision: str, m: int):
     f = ROOT / "profiles" / f"fused_gemm_{precision}_{ROWS_PER_GPU}.json"
     try:
@@ -360,6 +406,14 @@ def ours_arm(args, rank, local_rank, world):
     flops_job = 2.0 * m_total * N * K
     value = flops_job * args.steps / (total_ms * 1e-3) / 1e12
 
+    # All-gather of the output rows over NVLink (N > 1): timed separately, as
+    # the row-sharded job only needs it when a consumer wants the full tensor.
+    allgather = None
+    if world > 1:
+        allgather = time_allgather(out_d, world, m_total, stream, args.warmup, args.steps, max_over_ranks)
+        allgather["kernel_plus_allgather_tflops"] = flops_job / (
+            (total_ms / args.steps + allgather["ms_per_step"]) * 1e-3) / 1e12
+
     # spot check of this rank's result against the oracle on a few rows
     from oracle.bindings import fused_oracle
 
@@ -462,7 +516,13 @@ def ours_arm(args, rank, local_rank, world):
             "e2e": e2e,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak, "traffic": traffic_from_profile(args.precision, M),
-                         "peak_source": peak_src, "kernel_ms": per_launch_ms},
+                         "peak_source": peak_src, "kernel_ms": per_launch_ms,
+                         "frac_of_spec": achieved / (SPEC_TF32_TFLOPS / (3.0 if prec == mlib.GPU_PRECISION_3XTF32
+                                                                         else 1.0)),
+                         "spec_peak": "1125 TFLOP/s dense TF32 (B200 nominal)",
+                         "frac_of_cublas_tf32": (achieved / cublas) if cublas and prec == mlib.GPU_PRECISION_TF32
+                         else None},
+            "allgather": allgather,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "cublas_tf32_matmul_tflops_same_shape_same_steps": cublas,
