@@ -645,6 +645,26 @@ def run_sweep(args):
         flops = 2.0 * Mx * (D * H + 2 * H * H + H * D)
         print(json.dumps({"sweep": "3-layer MLP DAG (4 GEMM launches)", "M": Mx, "D": D, "H": H, "precision": prec_name,
                           "ms_min": tmin, "ms_median": tmed, "tflops": flops / (tmin * 1e-3) / 1e12}), flush=True)
+
+        # The same DAG with h W2' fused into F2 (mxb_fused_gemm2): three launches.
+        s2p = st(mlib.EpStepDev(mlib.MXB_EP_ADD_ROW, 0, b2.data_ptr(), H, 0.0, 0),
+                 mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0),
+                 mlib.EpStepDev(mlib.MXB_EP_ADD_PRODUCT, 0, None, 0, 0.0, 0))
+
+        def mlp_fused():
+            rc = lib.mxb_fused_gemm(ctx, X.data_ptr(), D, W1.data_ptr(), H, h.data_ptr(), H, Mx, H, D, s1[0], s1[1],
+                                    prec, stream.cuda_stream)
+            assert rc == 0, mlib.last_error()
+            rc = lib.mxb_fused_gemm2(ctx, h.data_ptr(), H, W2.data_ptr(), H, h.data_ptr(), H, W2p.data_ptr(), H, H,
+                                     y.data_ptr(), H, Mx, H, H, s2p[0], s2p[1], prec, stream.cuda_stream)
+            assert rc == 0, mlib.last_error()
+            rc = lib.mxb_fused_gemm(ctx, y.data_ptr(), H, W3.data_ptr(), D, o.data_ptr(), D, Mx, D, H, s3[0], s3[1],
+                                    prec, stream.cuda_stream)
+            assert rc == 0, mlib.last_error()
+        tmin, tmed = time_launches(mlp_fused, 10)
+        print(json.dumps({"sweep": "3-layer MLP DAG, h W2' fused into F2 (3 launches)", "M": Mx, "D": D, "H": H,
+                          "precision": prec_name, "ms_min": tmin, "ms_median": tmed,
+                          "tflops": flops / (tmin * 1e-3) / 1e12}), flush=True)
     lib.gpu_ctx_destroy(ctx)
     return 0
 

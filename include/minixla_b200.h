@@ -176,7 +176,8 @@ enum {
     MXB_EP_ADD_ROW  = 1,  /* x += operand[j]             ([N] bias row)                */
     MXB_EP_ADD_MOD  = 2,  /* x += operand[(i*N + j) % size]  (eval_fused's rule)       */
     MXB_EP_RELU     = 3,  /* x = x > 0 ? x : 0                                         */
-    MXB_EP_SCALE    = 4   /* x *= scale                                                */
+    MXB_EP_SCALE    = 4,  /* x *= scale                                                */
+    MXB_EP_ADD_PRODUCT = 5 /* x += (A2 @ B2)[i,j]  (mxb_fused_gemm2's second product)   */
 };
 #define MXB_MAX_EPILOGUE 16   /* the reference fuses at most 16 steps (optimizer.c:104-107) */
 
@@ -211,6 +212,29 @@ MXB_API int gpu_execute_into(Node* root, GpuCtx* ctx, Tensor* out);
 MXB_API int mxb_fused_gemm(GpuCtx* ctx,
                    const float* A, long long lda,
                    const float* B, long long ldb,
+                   float* out, long long ldo,
+                   int M, int N, int K,
+                   const mxb_ep_step* steps, int n_steps,
+                   int precision, void* stream);
+
+/* out[M,N] = epi(A[M,K] @ B[K,N]) where one MXB_EP_ADD_PRODUCT step adds a
+ * second product A2[M,K2] @ B2[K2,N] at its place in the chain.  No
+ * counterpart in the reference: there optimize() leaves a bare OP_MATMUL
+ * feeding a fused node's ADD step as a node of its own (optimizer.c:94-132)
+ * and eval_fused adds its stored result (graph.c:98-105); gpu_execute uses
+ * this fusion for such a matmul when the fused node is its only consumer and
+ * both share the left operand.  In TF32 mode with A2 == A (same pointer,
+ * pitch and K2 == K, M > 16) both products accumulate side by side in TMEM in
+ * one kernel that stages A once, and the second never goes to HBM; otherwise
+ * the second product runs first into pooled workspace.  Values are the same
+ * either way.  A2 and B2
+ * follow mxb_fused_gemm's layout rules (lda2, ldb2 % 4 == 0); exactly one
+ * ADD_PRODUCT step. */
+MXB_API int mxb_fused_gemm2(GpuCtx* ctx,
+                   const float* A, long long lda,
+                   const float* B, long long ldb,
+                   const float* A2, long long lda2,
+                   const float* B2, long long ldb2, int K2,
                    float* out, long long ldo,
                    int M, int N, int K,
                    const mxb_ep_step* steps, int n_steps,

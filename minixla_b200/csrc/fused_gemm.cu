@@ -111,13 +111,20 @@ __device__ __forceinline__ void raise_error(const FusedParams& p, volatile int* 
 // Applies the node's epilogue steps, in order, to 32 consecutive outputs of
 // one row (cols col..col+31), exactly as eval_fused does per cell
 // (graph.c:98-109): ADD adds the operand element, RELU is x > 0 ? x : 0.
+// `prod` (pair kernel, DUAL) holds this chunk of the second product, added
+// at the MXB_EP_ADD_PRODUCT step.
 __device__ __forceinline__ void apply_epilogue(float (&v)[32], int row, int col, bool row_ok,
-                                               const FusedParams& p) {
+                                               const FusedParams& p, const float* prod = nullptr) {
     const bool full_cols = col + 32 <= p.N;
     for (int s = 0; s < p.n_steps; ++s) {
         const int kind = p.steps[s].kind;
         const float* ptr = p.steps[s].ptr;
-        if (kind == MXB_EP_RELU) {
+        if (kind == MXB_EP_ADD_PRODUCT) {
+            if (prod) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += prod[i];
+            }
+        } else if (kind == MXB_EP_RELU) {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = v[i] > 0.0f ? v[i] : 0.0f;
         } else if (kind == MXB_EP_SCALE) {
@@ -449,38 +456,52 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------------ CTA-pair kernel (TF32)
 //
-// Pair tile 256 x 256 on a 2-CTA cluster (the two SMs of a TPC).  CTA r owns
+// Pair tile 256 x BN on a 2-CTA cluster (the two SMs of a TPC).  CTA r owns
 // output rows m0 + 128 r .. +128; per k-block it stages its 128 rows of A and
-// B columns n0 + 128 r .. +128 (half of the tile's B).  The leader (rank 0)
-// issues tcgen05.mma.cta_group::2 (M=256, N=256, K=8), which reads the A and
-// B halves from both CTAs' shared memory and leaves each CTA's 128 x 256
+// B columns n0 + (BN/2) r .. +BN/2 (half of the tile's B).  The leader (rank
+// 0) issues tcgen05.mma.cta_group::2 (M=256, N=BN, K=8), which reads the A
+// and B halves from both CTAs' shared memory and leaves each CTA's 128 x BN
 // accumulator in that CTA's TMEM.  Per SM that halves the B bytes staged and
-// read per MMA, so a stage is 32 KiB and six stages fit.
+// read per MMA: with BN = 256 a stage is 32 KiB and six stages fit.
+//
+// DUAL: the node's epilogue holds one step that adds a second product
+// A @ B2 with the same A (a bare matmul on the same left operand whose only
+// consumer is this node: config 4's relu(h W2 + b2) + h W2').  Each k-block
+// stages A once with the B and B2 halves; the MMA warp issues A.B into
+// accumulator 0 and A.B2 into accumulator 1 next to it in TMEM; the epilogue
+// reads both and adds the second where the step stands.  The second product
+// never goes to HBM and A is read once for both.  With BN = 128 a stage holds
+// the same 32 KiB as the BN = 256 single product (A 16 KiB + two 8 KiB B
+// halves), and the two accumulators of both TMEM buffers fill the 512
+// columns, so the epilogue still overlaps the next tile's k-loop.
 //
 // Barriers: full[s] lives in the leader and counts both CTAs' TMA bytes (the
 // peer's loads signal it through its cluster address); empty[s] and tfull[a]
 // live in both CTAs and receive the leader's multicast commits; tempty[a]
 // lives in the leader and takes one arrival per epilogue warp of either CTA.
 
-constexpr int kPairBN = 256;
-
-template <int STAGES>
+template <int STAGES, int BN, bool DUAL>
 struct PairCfg {
     static constexpr int kABytes = 128 * kBK * 4;                // 16 KiB: this CTA's A rows
-    static constexpr int kBBytes = (kPairBN / 2) * kBK * 4;      // 16 KiB: this CTA's B columns
-    static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kTmemCols = 2 * kPairBN;
+    static constexpr int kBBytes = (BN / 2) * kBK * 4;           // this CTA's B columns (per product)
+    static constexpr int kStageBytes = kABytes + (DUAL ? 2 : 1) * kBBytes;
+    static constexpr int kAccCols = (DUAL ? 2 : 1) * BN;         // TMEM columns of one tile's accumulators
+    static constexpr int kTmemCols = 2 * kAccCols;
     static constexpr int kBarOffset = STAGES * kStageBytes;
     static constexpr int kNumBars = 2 * STAGES + 5;
     static constexpr int kSmemBytes = 1024 + kBarOffset + kNumBars * 8 + 16;
+    static_assert(BN == 128 || BN == 256, "pair tile width");
+    static_assert(kStageBytes % 1024 == 0, "stages must keep 1 KiB swizzle alignment");
+    static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-template <int STAGES>
+template <int STAGES, int BN, bool DUAL>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     fused_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                            const __grid_constant__ FusedParams p) {
-    using C = PairCfg<STAGES>;
+    using C = PairCfg<STAGES, BN, DUAL>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -515,6 +536,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if (DUAL) {
+            tma_prefetch_desc(&tmA2);
+            tma_prefetch_desc(&tmB2);
+        }
     }
     if (warp == 1) {
         tmem_alloc_pair(smem_addr(tmem_slot), C::kTmemCols);
@@ -537,7 +562,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 int mb, nb;
                 tile_coords(t, p, mb, nb);
                 const int m0 = mb * 256 + static_cast<int>(rank) * 128;
-                const int n0 = nb * kPairBN + static_cast<int>(rank) * (kPairBN / 2);
+                const int n0 = nb * BN + static_cast<int>(rank) * (BN / 2);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (*abort_flag) { ok = false; break; }
                     if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1u, p.timeout_ns)) {
@@ -551,8 +576,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     const int k0 = kb * kBK;
                     tma_load_2d_pair(smem_addr(st), &tmA, fb, k0, m0);
 #pragma unroll
-                    for (int j = 0; j < kPairBN / 64; ++j)
+                    for (int j = 0; j < BN / 64; ++j)
                         tma_load_2d_pair(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb, n0 + 32 * j, k0);
+                    if (DUAL) {
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j)
+                            tma_load_2d_pair(smem_addr(st + C::kABytes + C::kBBytes + j * kBoxBytes), &tmB2, fb,
+                                             n0 + 32 * j, k0);
+                    }
                     ++issued;
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
                 }
@@ -570,7 +601,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (leader only)
         if (lane == 0 && rank == 0) {
-            constexpr uint32_t idesc = idesc_tf32(256, kPairBN);
+            constexpr uint32_t idesc = idesc_tf32(256, BN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
@@ -583,7 +614,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kPairBN);
+                const uint32_t d_tile = tmem_base + static_cast<uint32_t>(acc * C::kAccCols);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (!mbar_wait_cluster(full_bar(stage), phase, p.timeout_ns)) {
                         raise_error(p, abort_flag, kErrMma);
@@ -597,7 +628,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     for (int kk = 0; kk < kBK / 8; ++kk) {
                         const uint64_t da = smem_desc(a_addr + kk * 32, 16, 1024, kLayoutSW128);
                         const uint64_t db = smem_desc(b_addr + kk * 1024, kBoxBytes, 512, kLayoutSW128Base32B);
-                        mma_tf32_pair(d_tmem, da, db, idesc, (kb | kk) != 0 ? 1u : 0u);
+                        const uint32_t accumulate = (kb | kk) != 0 ? 1u : 0u;
+                        mma_tf32_pair(d_tile, da, db, idesc, accumulate);
+                        if (DUAL) {
+                            const uint64_t db2 =
+                                smem_desc(b_addr + C::kBBytes + kk * 1024, kBoxBytes, 512, kLayoutSW128Base32B);
+                            mma_tf32_pair(d_tile + BN, da, db2, idesc, accumulate);
+                        }
                     }
                     mma_commit_pair(empty_bar(stage), 0x3);
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -630,15 +667,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tile_coords(t, p, mb, nb);
             const int row = mb * 256 + row_in_tile;
             const bool row_ok = row < p.M;
-            const int col0 = nb * kPairBN;
+            const int col0 = nb * BN;
             int chunks = (p.N - col0 + 31) / 32;
-            if (chunks > kPairBN / 32) chunks = kPairBN / 32;
+            if (chunks > BN / 32) chunks = BN / 32;
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                                   static_cast<uint32_t>(acc * kPairBN);
+                                   static_cast<uint32_t>(acc * C::kAccCols);
             for (int c = 0; c < chunks; ++c) {
                 uint32_t r[32];
+                float w[32];
                 tmem_ld_32x32b_x32(taddr + 32 * c, r);
-                tmem_ld_wait();
+                if (DUAL) {
+                    uint32_t r2[32];
+                    tmem_ld_32x32b_x32(taddr + BN + 32 * c, r2);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) w[i] = __uint_as_float(r2[i]);
+                } else {
+                    tmem_ld_wait();
+                }
                 if (c == chunks - 1) {
                     // This warp is done with the accumulator: tell the leader's MMA warp.
                     tc_fence_before();
@@ -649,7 +695,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
                 const int col = col0 + 32 * c;
-                apply_epilogue(v, row, col, row_ok, p);
+                if (DUAL)
+                    apply_epilogue(v, row, col, row_ok, p, w);
+                else
+                    apply_epilogue(v, row, col, row_ok, p);
                 if (row_ok) store_row_chunk(v, row, col, p);
             }
             acc ^= 1;
@@ -761,10 +810,10 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-template <int STAGES>
+template <int STAGES, int BN, bool DUAL>
 cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
-    using C = PairCfg<STAGES>;
-    auto kernel = fused_gemm_pair_kernel<STAGES>;
+    using C = PairCfg<STAGES, BN, DUAL>;
+    auto kernel = fused_gemm_pair_kernel<STAGES, BN, DUAL>;
     static std::mutex mu;
     static uint64_t configured = 0;
     static int max_clusters[64] = {0};
@@ -806,9 +855,19 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
 
     constexpr CUtensorMapSwizzle kSwA = CU_TENSOR_MAP_SWIZZLE_128B;
     constexpr CUtensorMapSwizzle kSwB = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-    CUtensorMap mA, mB;
+    CUtensorMap mA, mB, mA2, mB2;
     if (!make_map(&mA, g.A, g.M, g.K, g.lda, kBK, 128, kSwA) || !make_map(&mB, g.B, g.K, g.N, g.ldb, 32, kBK, kSwB))
         return cudaErrorInvalidValue;
+    if (DUAL) {
+        // The second product shares A (same rows, K and pitch); only B2 has a map of its own.
+        if (g.A2 != g.A || g.K2 != g.K || g.lda2 != g.lda || !g.B2 ||
+            !make_map(&mB2, g.B2, g.K, g.N, g.ldb2, 32, kBK, kSwB))
+            return cudaErrorInvalidValue;
+        mA2 = mA;
+    } else {
+        mA2 = mA;
+        mB2 = mB;
+    }
 
     FusedParams p{};
     p.out = g.out;
@@ -818,7 +877,7 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.K = g.K;
     p.n_steps = g.n_steps;
     p.tiles_m = (g.M + 255) / 256;
-    p.tiles_n = (g.N + kPairBN - 1) / kPairBN;
+    p.tiles_n = (g.N + BN - 1) / BN;
     p.num_tiles = p.tiles_m * p.tiles_n;
     p.num_kb = (g.K + kBK - 1) / kBK;
     p.group_m = 8;
@@ -829,7 +888,7 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
     for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
 
     const int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;
-    kernel<<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(mA, mB, p);
+    kernel<<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p);
     note_launch();
     return cudaGetLastError();
 }
@@ -849,8 +908,13 @@ bool use_pair_kernel(const GemmLaunch& g) {
 }  // namespace
 
 cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
+    if (g.A2) {
+        // Two products of one A in one kernel (TF32 only; callers run other cases as two launches).
+        if (g.precision != GPU_PRECISION_TF32) return cudaErrorInvalidValue;
+        return run_pair_variant<6, 128, true>(g, stream);
+    }
     if (g.precision == GPU_PRECISION_3XTF32) return run_variant<128, 3, true, true>(g, stream);
-    if (use_pair_kernel(g)) return run_pair_variant<6>(g, stream);
+    if (use_pair_kernel(g)) return run_pair_variant<6, 256, false>(g, stream);
     // One TF32 product on one CTA.  Narrow or small problems use 128-wide tiles so more SMs get work.
     const long long tiles_m = (g.M + kBM - 1) / kBM;
     const long long tiles256 = tiles_m * ((g.N + 255) / 256);

@@ -26,6 +26,9 @@ struct GemmLaunch {
     const float* B; long long ldb;     // K x N, ldb % 4 == 0
     const float* A_small;              // 3xTF32 only: x - rne_tf32(x), same pitches
     const float* B_small;
+    const float* A2; long long lda2;   // optional second product A2[M,K2] @ B2[K2,N], added at the
+    const float* B2; long long ldb2;   // MXB_EP_ADD_PRODUCT step (TF32 only); A2 == nullptr: none
+    int K2;
     float* out; long long ldo;
     int M, N, K;
     long long row_base;                // global index of row 0 (rows of a larger matrix)

@@ -412,6 +412,57 @@ static bool infer_shapes(const std::vector<const Node*>& order,
     return true;
 }
 
+// ---------------------------------------------------------------- product fusion
+
+// MINIXLA_DUAL_GEMM=0 runs every second product as its own launch (the two
+// forms give the same values; tests compare them).
+static bool dual_kernel_enabled() {
+    const char* v = getenv("MINIXLA_DUAL_GEMM");
+    return !(v && v[0] == '0');
+}
+//
+// optimize() never fuses a bare matmul (optimizer.c:94-132), so a matmul that
+// feeds a fused node's ADD step stays a node of its own and eval_fused adds
+// its stored result (graph.c:98-105) -- config 4's F2 = relu(h W2 + b2) +
+// h W2'.  When that fused node is the matmul's only reader and both products
+// share the left operand, they run in one kernel (TF32 pair kernel, DUAL): A
+// is staged once for both and the matmul's value never goes to HBM.
+// Conditions: TF32, the matmul is 2-D, not the root, read once (by one ADD
+// step), has the fused node's A node as its A, and is shaped like the fused
+// node's 2-D output with more than 16 rows; the row pitches are multiples of
+// 4 (no padding copies).
+// Returns, per node, the index of the matmul it absorbs (-1 for none).
+static std::vector<int> plan_products(const std::vector<const Node*>& order,
+                                      const std::unordered_map<const Node*, int>& index,
+                                      const std::vector<Info>& info, int precision) {
+    const size_t n = order.size();
+    std::vector<int> absorb(n, -1);
+    if (precision != GPU_PRECISION_TF32 || !dual_kernel_enabled()) return absorb;
+    std::vector<int> refs(n, 0);
+    for (size_t i = 0; i < n; ++i)
+        for (int a = 0; a < order[i]->n_inputs; ++a) refs[index.at(order[i]->inputs[a])]++;
+    auto two_d = [&](int k) { return info[k].dims.size() == 2; };
+    for (size_t i = 0; i < n; ++i) {
+        const Node* f = order[i];
+        if (f->op != OP_FUSED || !two_d(static_cast<int>(i)) || info[i].dims[0] <= kSkinnyMaxRows) continue;
+        const int fa = index.at(f->inputs[0]), fb = index.at(f->inputs[1]);
+        if (info[fa].dims[1] % 4 || info[fb].dims[1] % 4) continue;
+        for (int e = 0; e < f->n_epilogue && absorb[i] < 0; ++e) {
+            if (f->epilogue[e].op != OP_ADD) continue;
+            const int j = index.at(f->epilogue[e].operand);
+            const Node* m = order[j];
+            if (m->op != OP_MATMUL || j == static_cast<int>(n) - 1 || refs[j] != 1 || !two_d(j) ||
+                info[j].dims != info[i].dims)
+                continue;
+            if (m->inputs[0] != f->inputs[0]) continue;
+            const int mb = index.at(m->inputs[1]);
+            if (!two_d(mb) || info[mb].dims[1] % 4) continue;
+            absorb[i] = j;
+        }
+    }
+    return absorb;
+}
+
 // ---------------------------------------------------------------- GEMM dispatch
 
 // Device operand of a fused GEMM, with its row pitch; `owned` buffers are
@@ -448,9 +499,44 @@ static bool tma_operand(GpuCtx* ctx, const float* src, long long rows, long long
 
 // Launches epi(A @ B) with already-validated, TMA-ready operands.  For
 // 3xTF32 the low parts of A and B (x - rne_tf32(x)) go to pooled workspace first.
+// A second product A[M,K] @ B[K,N] that a fused node's MXB_EP_ADD_PRODUCT
+// step adds (a bare matmul absorbed into its only consumer).
+struct Product {
+    const float* A;
+    long long lda;
+    const float* B;
+    long long ldb;
+    int K;
+};
+
 static int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
                        long long ldo, int M, int N, int K, const EpStepDev* steps, int n_steps, int precision,
-                       cudaStream_t stream, const float* B_small_pre = nullptr, long long row_base = 0) {
+                       cudaStream_t stream, const float* B_small_pre = nullptr, long long row_base = 0,
+                       const Product* prod = nullptr) {
+    if (prod && !(precision == GPU_PRECISION_TF32 && M > kSkinnyMaxRows && dual_kernel_enabled() && prod->A == A &&
+                  prod->lda == lda && prod->K == K)) {
+        // Two launches: the second product into pooled workspace, then the
+        // node reading it as a full add at the same step.
+        float* ws = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(M) * N * sizeof(float), stream));
+        if (!ws) return MXB_E_NOMEM;
+        int rc = launch_gemm(ctx, prod->A, prod->lda, prod->B, prod->ldb, ws, N, M, N, prod->K, nullptr, 0, precision,
+                             stream);
+        if (rc == MXB_OK) {
+            EpStepDev st2[MXB_MAX_EPILOGUE];
+            for (int i = 0; i < n_steps; ++i) {
+                st2[i] = steps[i];
+                if (st2[i].kind == MXB_EP_ADD_PRODUCT) {
+                    st2[i].kind = MXB_EP_ADD_FULL;
+                    st2[i].ptr = ws;
+                    st2[i].ld_or_size = N;
+                }
+            }
+            rc = launch_gemm(ctx, A, lda, B, ldb, out, ldo, M, N, K, st2, n_steps, precision, stream, B_small_pre,
+                             row_base);
+        }
+        ctx->pool->release(ws, stream);
+        return rc;
+    }
     if (M <= kSkinnyMaxRows) {
         // Few rows: HBM-bound on B, CUDA-core fp32 split over columns and K.
         const SkinnyPlan pl = plan_skinny(M, N, K, ctx->num_sms);
@@ -479,6 +565,13 @@ static int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* 
     g.steps = steps;
     g.n_steps = n_steps;
     g.precision = precision;
+    if (prod) {
+        g.A2 = prod->A;
+        g.lda2 = prod->lda;
+        g.B2 = prod->B;
+        g.ldb2 = prod->ldb;
+        g.K2 = prod->K;
+    }
     g.err = ctx->d_err;
     g.timeout_ns = ctx->timeout_ns;
     g.num_sms = ctx->num_sms;
@@ -513,13 +606,16 @@ static int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* 
 // RELU maps to RELU; other step ops are skipped, as eval_fused skips them.
 static int build_epilogue(const Node* n, int M, int N, long long batch, long long bt,
                           const std::unordered_map<const Node*, const float*>& dev_of,
-                          const std::unordered_map<const Node*, long long>& size_of, EpStepDev* out) {
+                          const std::unordered_map<const Node*, long long>& size_of, EpStepDev* out,
+                          const Node* absorbed = nullptr) {
     const long long MN = static_cast<long long>(M) * N;
     int k = 0;
     for (int e = 0; e < n->n_epilogue; ++e) {
         const EpStep& s = n->epilogue[e];
         EpStepDev d{};
-        if (s.op == OP_ADD) {
+        if (s.op == OP_ADD && absorbed && s.operand == absorbed) {
+            d.kind = MXB_EP_ADD_PRODUCT;  // the absorbed matmul, computed in the same kernel
+        } else if (s.op == OP_ADD) {
             const long long sz = size_of.at(s.operand);
             d.ptr = dev_of.at(s.operand);
             if (sz == batch * MN) {
@@ -551,7 +647,8 @@ static int build_epilogue(const Node* n, int M, int N, long long batch, long lon
 static int run_gemm_node(GpuCtx* ctx, const Node* n, const float* dA, int M, int K, const float* dB, int N,
                          float* dOut, const std::unordered_map<const Node*, const float*>& dev_of,
                          const std::unordered_map<const Node*, long long>& size_of, int precision,
-                         cudaStream_t stream, long long batch = 1) {
+                         cudaStream_t stream, long long batch = 1, const Node* absorbed = nullptr,
+                         const Product* prod = nullptr) {
     Operand a, b;
     int rc = MXB_OK;
     // Pitch padding treats the batches as one tall matrix (rows are contiguous).
@@ -560,10 +657,11 @@ static int run_gemm_node(GpuCtx* ctx, const Node* n, const float* dA, int M, int
     }
     for (long long bt = 0; bt < batch && rc == MXB_OK; ++bt) {
         EpStepDev steps[MXB_MAX_EPILOGUE];
-        const int n_steps = n->op == OP_FUSED ? build_epilogue(n, M, N, batch, bt, dev_of, size_of, steps) : 0;
+        const int n_steps =
+            n->op == OP_FUSED ? build_epilogue(n, M, N, batch, bt, dev_of, size_of, steps, absorbed) : 0;
         rc = launch_gemm(ctx, a.ptr + bt * M * a.ld, a.ld, b.ptr + bt * K * b.ld, b.ld,
                          dOut + bt * static_cast<long long>(M) * N, N, M, N, K, steps, n_steps, precision, stream,
-                         nullptr, bt * M);
+                         nullptr, bt * M, prod);
     }
     ctx->pool->release(a.owned, stream);
     ctx->pool->release(b.owned, stream);
@@ -726,7 +824,12 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
     };
 
     std::vector<char> chunked = plan.chunked;
+    const std::vector<int> absorb = plan_products(order, index, info, ctx->precision);
+    std::vector<char> absorbed(n, 0);
+    for (size_t i = 0; i < n; ++i)
+        if (absorb[i] >= 0) absorbed[absorb[i]] = 1;
     for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
+        if (absorbed[i]) continue;  // computed inside its consumer's kernel, chunk by chunk
         if (float* res = resident_copy(ctx, order[i], 0)) {
             info[i].dev = res;
             info[i].borrowed = true;
@@ -749,7 +852,8 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
     // 3xTF32: the low part of every B operand, once for all chunks.
     for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
         const Node* nd = order[i];
-        if (ctx->precision != GPU_PRECISION_3XTF32 || (nd->op != OP_FUSED && nd->op != OP_MATMUL)) continue;
+        if (ctx->precision != GPU_PRECISION_3XTF32 || (nd->op != OP_FUSED && nd->op != OP_MATMUL) || absorbed[i])
+            continue;
         const Info& b = info[index.at(nd->inputs[1])];
         b_small[i] = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(b.size) * 4, cs));
         if (!b_small[i]) {
@@ -777,6 +881,7 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
             const Node* nd = order[i];
             const Info& f = info[i];
             const long long cols = f.dims.size() == 2 ? f.dims[1] : 0;
+            if (absorbed[i]) continue;
             if (nd->op == OP_FUSED || nd->op == OP_MATMUL) {
                 const Info& a = info[index.at(nd->inputs[0])];
                 const Info& b = info[index.at(nd->inputs[1])];
@@ -786,7 +891,9 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
                 for (int e = 0; nd->op == OP_FUSED && e < nd->n_epilogue; ++e) {
                     const EpStep& st = nd->epilogue[e];
                     EpStepDev d{};
-                    if (st.op == OP_ADD) {
+                    if (st.op == OP_ADD && absorb[i] >= 0 && st.operand == order[absorb[i]]) {
+                        d.kind = MXB_EP_ADD_PRODUCT;
+                    } else if (st.op == OP_ADD) {
                         const Info& o = info[index.at(st.operand)];
                         d.kind = o.size == f.size ? MXB_EP_ADD_FULL
                                                   : (o.size == N ? MXB_EP_ADD_ROW : MXB_EP_ADD_MOD);
@@ -799,8 +906,16 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
                     }
                     steps[n_steps++] = d;
                 }
+                Product prod{};
+                if (absorb[i] >= 0) {
+                    const Node* m = order[absorb[i]];
+                    const Info& a2 = info[index.at(m->inputs[0])];
+                    const Info& b2 = info[index.at(m->inputs[1])];
+                    const int K2 = a2.dims[1];
+                    prod = Product{a2.dev + r0 * K2, K2, b2.dev, N, K2};
+                }
                 rc = launch_gemm(ctx, a.dev + r0 * K, K, b.dev, N, f.dev + r0 * N, N, static_cast<int>(r1 - r0), N, K,
-                                 steps, n_steps, ctx->precision, cs, b_small[i], r0);
+                                 steps, n_steps, ctx->precision, cs, b_small[i], r0, absorb[i] >= 0 ? &prod : nullptr);
             } else if (nd->op == OP_ADD) {
                 const Info& a = info[index.at(nd->inputs[0])];
                 const Info& b = info[index.at(nd->inputs[1])];
@@ -1232,14 +1347,32 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
     std::vector<int> stream_of(n_nodes, 0), last_on(n_streams, -1);
     std::vector<cudaEvent_t> done(n_nodes, nullptr);
     std::vector<std::vector<int>> inputs_of(n_nodes), consumers(n_nodes);
+    // A matmul absorbed into its consumer is never materialised: its inputs
+    // become inputs of the consumer and live until the consumer has run.
+    const std::vector<int> absorb = plan_products(order, index, info, ctx->precision);
+    std::vector<char> absorbed(n_nodes, 0);
+    for (size_t i = 0; i < n_nodes; ++i)
+        if (absorb[i] >= 0) absorbed[absorb[i]] = 1;
     for (size_t i = 0; i < n_nodes; ++i) {
-        for (int a = 0; a < order[i]->n_inputs; ++a) {
-            const int j = index.at(order[i]->inputs[a]);
-            if (std::find(inputs_of[i].begin(), inputs_of[i].end(), j) != inputs_of[i].end()) continue;
+        if (absorbed[i]) continue;
+        auto add_input = [&](const Node* in) {
+            const int j = index.at(in);
+            if (std::find(inputs_of[i].begin(), inputs_of[i].end(), j) != inputs_of[i].end()) return;
             inputs_of[i].push_back(j);
             consumers[j].push_back(static_cast<int>(i));
+        };
+        for (int a = 0; a < order[i]->n_inputs; ++a) {
+            const Node* in = order[i]->inputs[a];
+            if (absorb[i] >= 0 && in == order[absorb[i]]) {
+                for (int b = 0; b < in->n_inputs; ++b) add_input(in->inputs[b]);
+            } else {
+                add_input(in);
+            }
         }
     }
+    for (size_t i = 0; i < n_nodes; ++i) info[i].last_use = -1;
+    for (size_t i = 0; i < n_nodes; ++i)
+        for (int j : inputs_of[i]) info[j].last_use = std::max(info[j].last_use, static_cast<int>(i));
     size_t next_event = 0;
 
     std::unordered_map<const Node*, const float*> dev_of;
@@ -1248,6 +1381,7 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
     for (size_t i = 0; i < n_nodes && rc == MXB_OK; ++i) {
         const Node* n = order[i];
         Info& f = info[i];
+        if (absorbed[i]) continue;  // computed inside its consumer's kernel
         int sidx = -1;
         if (n->op == OP_INPUT) {
             sidx = 0;
@@ -1292,8 +1426,17 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
                 const Info& b = info[index.at(n->inputs[1])];
                 const size_t r = a.dims.size();
                 const long long batch = a.size / (static_cast<long long>(a.dims[r - 2]) * a.dims[r - 1]);
-                rc = run_gemm_node(ctx, n, a.dev, a.dims[r - 2], a.dims[r - 1], b.dev, b.dims[r - 1], f.dev, dev_of,
-                                   size_of, ctx->precision, st, batch);
+                if (absorb[i] >= 0) {
+                    const Node* m = order[absorb[i]];
+                    const Info& a2 = info[index.at(m->inputs[0])];
+                    const Info& b2 = info[index.at(m->inputs[1])];
+                    const Product prod{a2.dev, a2.dims[1], b2.dev, b2.dims[1], a2.dims[1]};
+                    rc = run_gemm_node(ctx, n, a.dev, a.dims[0], a.dims[1], b.dev, b.dims[1], f.dev, dev_of, size_of,
+                                       ctx->precision, st, 1, m, &prod);
+                } else {
+                    rc = run_gemm_node(ctx, n, a.dev, a.dims[r - 2], a.dims[r - 1], b.dev, b.dims[r - 1], f.dev,
+                                       dev_of, size_of, ctx->precision, st, batch);
+                }
                 break;
             }
             case OP_ADD: {
@@ -1794,6 +1937,45 @@ int mxb_fused_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, l
     mxb::DeviceScope scope(ctx->device);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
     return mxb::launch_gemm(ctx, A, lda, B, ldb, out, ldo, M, N, K, dev_steps, n_steps, precision, st);
+}
+
+int mxb_fused_gemm2(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, const float* A2,
+                    long long lda2, const float* B2, long long ldb2, int K2, float* out, long long ldo, int M, int N,
+                    int K, const mxb_ep_step* steps, int n_steps, int precision, void* stream) {
+    if (!ctx || !A || !B || !A2 || !B2 || !out || M < 1 || N < 1 || K < 1 || K2 < 1 || lda < K || ldb < N ||
+        lda2 < K2 || ldb2 < N || ldo < N || n_steps < 1 || n_steps > MXB_MAX_EPILOGUE || !steps ||
+        !mxb::valid_precision(precision)) {
+        set_error("mxb_fused_gemm2: invalid arguments");
+        return MXB_E_ARG;
+    }
+    if (lda % 4 || ldb % 4 || lda2 % 4 || ldb2 % 4 || (reinterpret_cast<uintptr_t>(A) & 15) ||
+        (reinterpret_cast<uintptr_t>(B) & 15) || (reinterpret_cast<uintptr_t>(A2) & 15) ||
+        (reinterpret_cast<uintptr_t>(B2) & 15)) {
+        set_error("mxb_fused_gemm2: A, B, A2 and B2 need 16-byte aligned bases and row pitches (multiples of 4)");
+        return MXB_E_ARG;
+    }
+    mxb::EpStepDev dev_steps[MXB_MAX_EPILOGUE];
+    int n_prod = 0;
+    for (int i = 0; i < n_steps; ++i) {
+        const mxb_ep_step& s = steps[i];
+        const bool is_add = s.kind == MXB_EP_ADD_FULL || s.kind == MXB_EP_ADD_ROW || s.kind == MXB_EP_ADD_MOD;
+        if (s.kind < MXB_EP_ADD_FULL || s.kind > MXB_EP_ADD_PRODUCT || (is_add && !s.operand) ||
+            (s.kind == MXB_EP_ADD_FULL && s.ld_or_size < N) || (s.kind == MXB_EP_ADD_MOD && s.ld_or_size < 1)) {
+            set_error("mxb_fused_gemm2: invalid epilogue step %d", i);
+            return MXB_E_ARG;
+        }
+        n_prod += s.kind == MXB_EP_ADD_PRODUCT;
+        memcpy(&dev_steps[i], &s, sizeof(s));
+    }
+    if (n_prod != 1) {
+        set_error("mxb_fused_gemm2: exactly one MXB_EP_ADD_PRODUCT step required (got %d)", n_prod);
+        return MXB_E_ARG;
+    }
+    mxb::DeviceScope scope(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    const mxb::Product prod{A2, lda2, B2, ldb2, K2};
+    return mxb::launch_gemm(ctx, A, lda, B, ldb, out, ldo, M, N, K, dev_steps, n_steps, precision, st, nullptr, 0,
+                            &prod);
 }
 
 int mxb_add(GpuCtx* ctx, const float* a, long long n, const float* b, long long b_size, float* out, void* stream) {

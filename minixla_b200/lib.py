@@ -17,7 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libminixla_b200.so"
 GPU_PRECISION_TF32 = 1
 GPU_PRECISION_3XTF32 = 3
 
-MXB_EP_ADD_FULL, MXB_EP_ADD_ROW, MXB_EP_ADD_MOD, MXB_EP_RELU, MXB_EP_SCALE = range(5)
+MXB_EP_ADD_FULL, MXB_EP_ADD_ROW, MXB_EP_ADD_MOD, MXB_EP_RELU, MXB_EP_SCALE, MXB_EP_ADD_PRODUCT = range(6)
 MXB_OK, MXB_E_ARG, MXB_E_CUDA, MXB_E_NOMEM, MXB_E_TIMEOUT, MXB_E_UNSUPPORTED = 0, -1, -2, -3, -4, -5
 MXB_MAX_EPILOGUE = 16
 
@@ -44,6 +44,12 @@ PROTOTYPES = {
         C.c_int,
         [C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong,
          C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p],
+    ),
+    "mxb_fused_gemm2": (
+        C.c_int,
+        [C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong, C.c_void_p,
+         C.c_longlong, C.c_int, C.c_void_p, C.c_longlong, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int,
+         C.c_void_p],
     ),
     "mxb_fused_gemm_noalloc": (
         C.c_int,

@@ -445,6 +445,109 @@ def test_resident_weights(lib, gpu_ctx):
         np.testing.assert_array_equal(run_execute(lib, gpu_ctx, root, X3), plain)
 
 
+# ---------------------------------------------------------------- bare matmul fused into its consumer
+
+
+@pytest.mark.parametrize("M", [8, 200, 1000, 4096])
+def test_product_fusion_in_graphs(lib, gpu_ctx, M, monkeypatch, host_threads):
+    """Config 4's pattern, y = relu(h W2 + b2) + h W2' with h W2' a bare
+    matmul read only by y: in TF32 mode both products run in one kernel.
+    The result matches the two-launch form (MINIXLA_DUAL_GEMM=0) bit for bit
+    and the oracle within the TF32 tolerance; M = 8 keeps the two-launch
+    form, M = 200 runs on the one-stream executor, larger M row-streamed."""
+    D, H = 96, 256
+    X = datagen.uniform((M, D), 80)
+    W1 = datagen.normal((D, H), 81, 0.0, 1.0 / np.sqrt(D))
+    W2 = datagen.normal((H, H), 82, 0.0, 1.0 / np.sqrt(H))
+    W2p = datagen.normal((H, H), 83, 0.0, 1.0 / np.sqrt(H))
+    b1 = datagen.normal((H,), 84, 0.0, 0.1)
+    b2 = datagen.normal((H,), 85, 0.0, 0.1)
+    hg = HostGraph()
+    x = hg.input_node(X)
+    h = hg.fused_node(x, hg.input_node(W1), [(OP_ADD, hg.input_node(b1)), (OP_RELU, None)])
+    hw = hg.g_matmul(h, hg.input_node(W2p))
+    root = hg.fused_node(h, hg.input_node(W2), [(OP_ADD, hg.input_node(b2)), (OP_RELU, None), (OP_ADD, hw)])
+    fused = run_execute(lib, gpu_ctx, root, TF32)
+    monkeypatch.setenv("MINIXLA_DUAL_GEMM", "0")
+    two = run_execute(lib, gpu_ctx, root, TF32)
+    monkeypatch.delenv("MINIXLA_DUAL_GEMM")
+    assert np.array_equal(fused, two)
+    h_ref = bindings.fused_oracle(X, W1, [("add", b1), ("relu",)], threads=host_threads)
+    hw_ref = bindings.fused_oracle(h_ref, W2p, [], threads=host_threads)
+    want = bindings.fused_oracle(h_ref, W2, [("add", b2), ("relu",), ("add", hw_ref)], threads=host_threads)
+    check(fused, want, TF32, f"product fusion M={M}", depth=2)
+
+
+@pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
+@pytest.mark.parametrize("mnkk", [(256, 256, 32, 64), (300, 520, 100, 36), (1000, 1000, 1000, 1000),
+                                  (2048, 2048, 2048, 1024), (12, 260, 128, 96), (4096, 4096, 4096, 4096)])
+@pytest.mark.parametrize("shared", [True, False], ids=["shared_A", "own_A2"])
+def test_fused_gemm2_device_api(lib, gpu_ctx, mnkk, precision, shared, host_threads):
+    """mxb_fused_gemm2: epi(A B) with a second product A2 B2 added at its
+    step, against the oracle (the second product evaluated separately, as
+    eval_fused adds a stored matmul).  shared_A passes A itself as A2 (the
+    one-kernel form in TF32 mode); own_A2 a separate matrix (two launches)."""
+    import torch
+
+    M, N, K, K2 = mnkk
+    if shared:
+        K2 = K
+    elif M * N * K > 2048 ** 3:
+        pytest.skip("the two-launch form is covered at the smaller shapes")
+    A = datagen.uniform((M, K), 90)
+    B = datagen.uniform((K, N), 91)
+    A2 = A if shared else datagen.uniform((M, K2), 92)
+    B2 = datagen.uniform((K2, N), 93)
+    bias = datagen.normal((N,), 94, 0.0, 0.5)
+    dA, dB, dA2, dB2, dbias = (torch.from_numpy(x).cuda() for x in (A, B, A2, B2, bias))
+    if shared:
+        dA2 = dA
+    out = torch.empty((M, N), device="cuda")
+    steps = (mlib.EpStepDev * 3)()
+    steps[0] = mlib.EpStepDev(mlib.MXB_EP_ADD_ROW, 0, dbias.data_ptr(), N, 0.0, 0)
+    steps[1] = mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0)
+    steps[2] = mlib.EpStepDev(mlib.MXB_EP_ADD_PRODUCT, 0, None, 0, 0.0, 0)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.mxb_fused_gemm2(gpu_ctx, dA.data_ptr(), K, dB.data_ptr(), N, dA2.data_ptr(), K2, dB2.data_ptr(), N, K2,
+                             out.data_ptr(), N, M, N, K, steps, 3, precision, stream)
+    assert rc == 0, mlib.last_error()
+    torch.cuda.synchronize()
+    assert lib.mxb_check_device_error(gpu_ctx) == 0
+    rows = None if M * N * K <= 2048 ** 3 else _sample_rows(M, 256)
+    p_ref = bindings.fused_oracle(A2, B2, [], rows=rows, threads=host_threads)
+    if rows is not None:  # the add operand is indexed by global row: place the sampled rows
+        full = np.zeros((M, N), np.float32)
+        full[rows] = p_ref
+        p_ref = full
+    want = bindings.fused_oracle(A, B, [("add", bias), ("relu",), ("add", p_ref)], rows=rows, threads=host_threads)
+    got = out.cpu().numpy()
+    check(got if rows is None else got[rows], want, precision, f"gemm2 {mnkk}", depth=2)
+
+
+def test_fused_gemm2_rejects_bad_arguments(lib, gpu_ctx):
+    import torch
+
+    M, N, K = 256, 256, 64
+    t = torch.zeros((M, max(N, K) + 4), device="cuda")
+    out = torch.empty((M, N), device="cuda")
+    p = t.data_ptr()
+    relu = mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0)
+    prod = mlib.EpStepDev(mlib.MXB_EP_ADD_PRODUCT, 0, None, 0, 0.0, 0)
+
+    def call(steps, lda2=K, a2=p):
+        arr = (mlib.EpStepDev * len(steps))(*steps)
+        return lib.mxb_fused_gemm2(gpu_ctx, p, K, p, N, a2, lda2, p, N, K, out.data_ptr(), N, M, N, K, arr,
+                                   len(steps), TF32, None)
+
+    assert call([relu]) == mlib.MXB_E_ARG                 # no ADD_PRODUCT step
+    assert call([prod, relu, prod]) == mlib.MXB_E_ARG     # two
+    assert call([prod], lda2=K + 2) == mlib.MXB_E_ARG     # row pitch not a multiple of 4
+    assert call([prod], a2=p + 4) == mlib.MXB_E_ARG       # base not 16-byte aligned
+    steps = (mlib.EpStepDev * 1)(prod)
+    assert lib.mxb_fused_gemm(gpu_ctx, p, K, p, N, out.data_ptr(), N, M, N, K, steps, 1, TF32,
+                              None) == mlib.MXB_E_ARG  # mxb_fused_gemm has no second product
+
+
 # ---------------------------------------------------------------- device-pointer API
 
 
