@@ -322,12 +322,14 @@ def test_full_size_checksums(lib, gpu_ctx, precision):
     assert rel_frobenius(got.sum(1), row_want) < tol
 
 
+@pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
 @pytest.mark.parametrize("variant", ["pair", "single"])
 @pytest.mark.parametrize("mnk", [(256, 256, 32), (300, 520, 100), (1000, 1000, 1000), (257, 4097, 129),
-                                 (8191, 127, 3000), (2048, 2048, 2048), (4096, 300, 1024)])
-def test_tf32_kernel_variants(lib, gpu_ctx, mnk, variant, monkeypatch, host_threads):
-    """Both TF32 kernels (CTA pair, single CTA) on tile-edge shapes, with a
-    full-matrix add, a bias row and relu in the epilogue."""
+                                 (8191, 127, 3000), (2048, 2048, 2048), (4096, 300, 1024), (640, 384, 4100)])
+def test_kernel_variants(lib, gpu_ctx, mnk, variant, precision, monkeypatch, host_threads):
+    """Both kernels of each mode (CTA pair, single CTA) on tile-edge shapes,
+    with a full-matrix add, a bias row and relu in the epilogue.  K = 4100
+    ends on a partial k-block and a partial 3xTF32 segment."""
     monkeypatch.setenv("MINIXLA_GEMM_VARIANT", variant)
     M, N, K = mnk
     A, B, C = _relu_abc(M, N, K, c_normal=True)
@@ -335,10 +337,10 @@ def test_tf32_kernel_variants(lib, gpu_ctx, mnk, variant, monkeypatch, host_thre
     hg = HostGraph()
     root = hg.fused_node(hg.input_node(A), hg.input_node(B),
                          [(OP_ADD, hg.input_node(C)), (OP_RELU, None), (OP_ADD, hg.input_node(bias))])
-    got = run_execute(lib, gpu_ctx, root, TF32)
+    got = run_execute(lib, gpu_ctx, root, precision)
     rows = None if M * N * K <= 2048 ** 3 else _sample_rows(M, 256)
     want = bindings.fused_oracle(A, B, [("add", C), ("relu",), ("add", bias)], rows=rows, threads=host_threads)
-    check(got if rows is None else got[rows], want, TF32, f"{variant} {mnk}")
+    check(got if rows is None else got[rows], want, precision, f"{variant} {mnk}")
 
 
 @pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
