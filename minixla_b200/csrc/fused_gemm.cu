@@ -197,6 +197,17 @@ __device__ __forceinline__ void store_row_chunk(const float (&v)[W], int row, in
     }
 }
 
+// Pulls this thread's rows of every full-matrix ADD operand, columns
+// col .. col + ncols, into L2 ahead of the epilogue's loads.
+__device__ __forceinline__ void prefetch_full_operands(int row, int col, int ncols, const FusedParams& p) {
+    for (int s = 0; s < p.n_steps; ++s) {
+        if (p.steps[s].kind != MXB_EP_ADD_FULL) continue;
+        const float* src = p.steps[s].ptr + static_cast<long long>(row) * p.steps[s].ld_or_size + col;
+        for (int c = 0; c < ncols; c += 32)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(src + c)));
+    }
+}
+
 template <int BN, int STAGES, bool SPLIT3, bool SEG>
 __global__ void __launch_bounds__(kThreads, 1)
     fused_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -465,7 +476,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 // 0) issues tcgen05.mma.cta_group::2 (M=256, N=BN, K=8), which reads the A
 // and B halves from both CTAs' shared memory and leaves each CTA's 128 x BN
 // accumulator in that CTA's TMEM.  Per SM that halves the B bytes staged and
-// read per MMA: with BN = 256 a stage is 32 KiB and six stages fit.
+// read per MMA: with BN = 256 a stage is 32 KiB and six stages fit.  With
+// BN = 512 the leader issues two N = 256 MMAs per k step, each into its own
+// 256 accumulator columns; CTA r stages, for MMA h, B columns
+// nb*512 + 256 h + 128 r .. +128, so accumulator column c is output column
+// nb*512 + c.  A stage is 48 KiB (four fit) and the 512 columns leave one
+// TMEM buffer: the epilogue drains it before the next tile starts.
 //
 // DUAL: the node's epilogue holds one step that adds a second product
 // A @ B2 with the same A (a bare matmul on the same left operand whose only
@@ -483,28 +499,37 @@ __global__ void __launch_bounds__(kThreads, 1)
 // live in both CTAs and receive the leader's multicast commits; tempty[a]
 // lives in the leader and takes one arrival per epilogue warp of either CTA.
 
-template <int STAGES, int BN, bool DUAL>
+template <int STAGES, int BN, bool DUAL, int EPI = 4>
 struct PairCfg {
+    static_assert(EPI == 4 || EPI == 8, "epilogue warps: one or two per TMEM lane quadrant");
+    static constexpr int kThreadsPerCta = 64 + 32 * EPI;         // TMA warp, MMA warp, epilogue warps
     static constexpr int kABytes = 128 * kBK * 4;                // 16 KiB: this CTA's A rows
     static constexpr int kBBytes = (BN / 2) * kBK * 4;           // this CTA's B columns (per product)
     static constexpr int kStageBytes = kABytes + (DUAL ? 2 : 1) * kBBytes;
+    // One MMA covers at most N = 256: wider tiles issue BN / 256 of them per
+    // k step, each on its own 256 accumulator columns.
+    static constexpr int kSubN = BN < 256 ? BN : 256;
+    static constexpr int kSubs = BN / kSubN;
+    static constexpr int kSubBoxes = kSubN / 64;                 // 32-column B boxes per CTA per sub-MMA
     static constexpr int kAccCols = (DUAL ? 2 : 1) * BN;         // TMEM columns of one tile's accumulators
-    static constexpr int kTmemCols = 2 * kAccCols;
+    static constexpr int kBufs = kAccCols <= 256 ? 2 : 1;        // accumulator buffers in TMEM
+    static constexpr int kTmemCols = kBufs * kAccCols;
     static constexpr int kBarOffset = STAGES * kStageBytes;
     static constexpr int kNumBars = 2 * STAGES + 5;
     static constexpr int kSmemBytes = 1024 + kBarOffset + kNumBars * 8 + 16;
-    static_assert(BN == 128 || BN == 256, "pair tile width");
+    static_assert(BN == 128 || BN == 256 || BN == 512, "pair tile width");
+    static_assert(!(DUAL && BN == 512), "two products use 128- or 256-column tiles");
     static_assert(kStageBytes % 1024 == 0, "stages must keep 1 KiB swizzle alignment");
     static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-template <int STAGES, int BN, bool DUAL>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+template <int STAGES, int BN, bool DUAL, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, DUAL, EPI>::kThreadsPerCta, 1)
     fused_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                            const __grid_constant__ FusedParams p) {
-    using C = PairCfg<STAGES, BN, DUAL>;
+    using C = PairCfg<STAGES, BN, DUAL, EPI>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -532,7 +557,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(tfull_bar(a), 1);
-            mbar_init(tempty_bar(a), 8);  // 4 epilogue warps in each of the two CTAs
+            mbar_init(tempty_bar(a), 2 * EPI);  // every epilogue warp of the two CTAs
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -565,7 +590,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 int mb, nb;
                 tile_coords(t, p, mb, nb);
                 const int m0 = mb * 256 + static_cast<int>(rank) * 128;
-                const int n0 = nb * BN + static_cast<int>(rank) * (BN / 2);
+                // CTA r stages, for sub-MMA h, B columns nb*BN + h*kSubN + r*kSubN/2 ..
+                // + kSubN/2, so accumulator column c is output column nb*BN + c.
+                const int n0 = nb * BN + static_cast<int>(rank) * (C::kSubN / 2);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (*abort_flag) { ok = false; break; }
                     if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1u, p.timeout_ns)) {
@@ -580,7 +607,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     tma_load_2d_pair(smem_addr(st), &tmA, fb, k0, m0);
 #pragma unroll
                     for (int j = 0; j < BN / 64; ++j)
-                        tma_load_2d_pair(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb, n0 + 32 * j, k0);
+                        tma_load_2d_pair(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb,
+                                         n0 + (j / C::kSubBoxes) * C::kSubN + 32 * (j % C::kSubBoxes), k0);
                     if (DUAL) {
 #pragma unroll
                         for (int j = 0; j < BN / 64; ++j)
@@ -604,7 +632,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (leader only)
         if (lane == 0 && rank == 0) {
-            constexpr uint32_t idesc = idesc_tf32(256, BN);
+            constexpr uint32_t idesc = idesc_tf32(256, C::kSubN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
@@ -633,6 +661,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         const uint64_t db = smem_desc(b_addr + kk * 1024, kBoxBytes, 512, kLayoutSW128Base32B);
                         const uint32_t accumulate = (kb | kk) != 0 ? 1u : 0u;
                         mma_tf32_pair(d_tile, da, db, idesc, accumulate);
+#pragma unroll
+                        for (int h = 1; h < C::kSubs; ++h) {
+                            const uint64_t dbh = smem_desc(b_addr + h * C::kSubBoxes * kBoxBytes + kk * 1024,
+                                                           kBoxBytes, 512, kLayoutSW128Base32B);
+                            mma_tf32_pair(d_tile + h * C::kSubN, da, dbh, idesc, accumulate);
+                        }
                         if (DUAL) {
                             const uint64_t db2 =
                                 smem_desc(b_addr + C::kBBytes + kk * 1024, kBoxBytes, 512, kLayoutSW128Base32B);
@@ -644,7 +678,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
                 if (!ok) break;
                 mma_commit_pair(tfull_bar(acc), 0x3);
-                acc ^= 1;
+                if (C::kBufs == 2) acc ^= 1;
                 if (acc == 0) acc_phase ^= 1u;
             }
             mma_commit_pair(drain_bar, 0x1);
@@ -652,7 +686,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
     } else {
         // ------------------------------------------------------------ epilogue (both CTAs)
+        // Warp w reads TMEM lane quadrant w % 4; with EPI = 8 the two warps of a
+        // quadrant split the tile's columns in halves.
         const int quad = warp & 3;
+        constexpr int kChunksPerWarp = BN / 32 / (EPI / 4);
+        const int c_first = ((warp - 2) >> 2) * kChunksPerWarp;
         const int row_in_tile = static_cast<int>(rank) * 128 + quad * 32 + lane;
         const uint32_t tempty_leader0 = mapa_shared(tempty_bar(0), 0);
         const uint32_t tempty_leader1 = mapa_shared(tempty_bar(1), 0);
@@ -672,10 +710,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const bool row_ok = row < p.M;
             const int col0 = nb * BN;
             int chunks = (p.N - col0 + 31) / 32;
-            if (chunks > BN / 32) chunks = BN / 32;
+            if (chunks > c_first + kChunksPerWarp) chunks = c_first + kChunksPerWarp;
+            if (row_ok && chunks > c_first) prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p);
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                    static_cast<uint32_t>(acc * C::kAccCols);
-            for (int c = 0; c < chunks; ++c) {
+            if (chunks <= c_first) {
+                // No columns of this tile for this warp: release the accumulator at once.
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+            }
+            for (int c = c_first; c < chunks; ++c) {
                 uint32_t r[32];
                 float w[32];
                 tmem_ld_32x32b_x32(taddr + 32 * c, r);
@@ -704,7 +749,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     apply_epilogue(v, row, col, row_ok, p);
                 if (row_ok) store_row_chunk(v, row, col, p);
             }
-            acc ^= 1;
+            if (C::kBufs == 2) acc ^= 1;
             if (acc == 0) acc_phase ^= 1u;
         }
     }
@@ -1078,10 +1123,10 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-template <int STAGES, int BN, bool DUAL>
+template <int STAGES, int BN, bool DUAL, int EPI = 4>
 cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
-    using C = PairCfg<STAGES, BN, DUAL>;
-    auto kernel = fused_gemm_pair_kernel<STAGES, BN, DUAL>;
+    using C = PairCfg<STAGES, BN, DUAL, EPI>;
+    auto kernel = fused_gemm_pair_kernel<STAGES, BN, DUAL, EPI>;
     static std::mutex mu;
     static uint64_t configured = 0;
     static int max_clusters[64] = {0};
@@ -1102,7 +1147,7 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
             attr.val.clusterDim.y = 1;
             attr.val.clusterDim.z = 1;
             cfg.gridDim = dim3(2 * (g.num_sms / 2), 1, 1);
-            cfg.blockDim = dim3(kThreads, 1, 1);
+            cfg.blockDim = dim3(C::kThreadsPerCta, 1, 1);
             cfg.dynamicSmemBytes = C::kSmemBytes;
             cfg.attrs = &attr;
             cfg.numAttrs = 1;
@@ -1156,7 +1201,7 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
     for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
 
     const int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;
-    kernel<<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p);
+    kernel<<<2 * pairs, C::kThreadsPerCta, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p);
     note_launch();
     return cudaGetLastError();
 }
@@ -1238,14 +1283,32 @@ cudaError_t run_pair3_variant(const GemmLaunch& g, cudaStream_t stream) {
 
 // Which TF32 kernel: the CTA-pair kernel once there are enough 256 x 256
 // tiles to occupy the SMs, else the single-CTA kernel (128 x 256 or 128 x 128
-// tiles spread over more SMs).  MINIXLA_GEMM_VARIANT=pair|single overrides.
+// tiles spread over more SMs).  MINIXLA_GEMM_VARIANT=pair|pair512|single
+// overrides.
 bool use_pair_kernel(const GemmLaunch& g) {
     if (const char* v = getenv("MINIXLA_GEMM_VARIANT")) {
-        if (!strcmp(v, "pair")) return true;
+        if (!strcmp(v, "pair") || !strcmp(v, "pair512")) return true;
         if (!strcmp(v, "single")) return false;
     }
     const long long pair_tiles = static_cast<long long>((g.M + 255) / 256) * ((g.N + 255) / 256);
     return g.M >= 256 && pair_tiles >= g.num_sms / 4;
+}
+
+// TF32 pair kernel with 256 x 512 tiles: per k-block each CTA stages 16 KiB
+// of A and 32 KiB of B for eight 256 x 256 x 8 MMAs -- a quarter fewer bytes
+// per MMA than the 256 x 256 tile, whose 32 KiB feed four.  The 512
+// accumulator columns fill TMEM, so the epilogue no longer overlaps the next
+// tile's k-loop (single buffer); it prefetches its rows of C into L2 first.
+// Measured at 8192^3: 784 vs 712 TFLOP/s, and 693 vs 652 under the power
+// cap.  (Eight epilogue warps instead of four drained no faster.)  Used once
+// the wide tiles alone give every CTA pair a tile.
+bool pair_wide_tiles(const GemmLaunch& g) {
+    if (const char* v = getenv("MINIXLA_GEMM_VARIANT")) {
+        if (!strcmp(v, "pair512")) return true;
+        if (!strcmp(v, "pair")) return false;
+    }
+    const long long wide_tiles = static_cast<long long>((g.M + 255) / 256) * ((g.N + 511) / 512);
+    return wide_tiles >= g.num_sms / 2;
 }
 
 }  // namespace
@@ -1253,12 +1316,19 @@ bool use_pair_kernel(const GemmLaunch& g) {
 cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
     if (g.A2) {
         // Two products of one A in one kernel (TF32 only; callers run other cases as two launches).
+        // 256-column tiles put both accumulators in the 512 TMEM columns (one buffer,
+        // 48 KiB stages); 128-column tiles keep two buffers for problems with few tiles.
         if (g.precision != GPU_PRECISION_TF32) return cudaErrorInvalidValue;
+        const long long tiles256 = static_cast<long long>((g.M + 255) / 256) * ((g.N + 255) / 256);
+        if (tiles256 >= g.num_sms / 2) return run_pair_variant<4, 256, true>(g, stream);
         return run_pair_variant<6, 128, true>(g, stream);
     }
     if (g.precision == GPU_PRECISION_3XTF32)
         return use_pair_kernel(g) ? run_pair3_variant<3>(g, stream) : run_variant<128, 3, true, true>(g, stream);
-    if (use_pair_kernel(g)) return run_pair_variant<6, 256, false>(g, stream);
+    if (use_pair_kernel(g)) {
+        return pair_wide_tiles(g) ? run_pair_variant<4, 512, false>(g, stream)
+                                  : run_pair_variant<6, 256, false>(g, stream);
+    }
     // One TF32 product on one CTA.  Narrow or small problems use 128-wide tiles so more SMs get work.
     const long long tiles_m = (g.M + kBM - 1) / kBM;
     const long long tiles256 = tiles_m * ((g.N + 255) / 256);
