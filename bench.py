@@ -544,6 +544,33 @@ SWEEP_SHAPES = [  # (M, N, K, C distribution) -- BASELINE configs 1-3 and config
 ]
 
 
+CPU_SLICE_FLOPS = 0.3e9  # per reference timing: about 0.3 s of single-threaded execute()
+
+
+def cpu_reference_ms(build, rows_total: int, flops_per_row: float):
+    """Single-threaded wall time of MiniXLA's own execute() (oracle/_ref) for
+    a graph over `rows_total` output rows, from a timed row slice: rows are
+    independent through eval_fused, so the time scales linearly in M.
+    `build(rg, r)` builds the graph of the first r rows with RefGraph and
+    returns its root.  Falls back to the C restatement when the reference
+    library is absent (kind "port")."""
+    from oracle.bindings import RefGraph, ref_available
+
+    r = int(max(1, min(rows_total, CPU_SLICE_FLOPS // max(1.0, flops_per_row))))
+    if not ref_available():
+        return {"cpu_reference_ms": None, "cpu_kind": "unavailable"}
+    rg = RefGraph()
+    try:
+        root = rg.own(rg.optimize(build(rg, r)))
+        t0 = time.perf_counter()
+        rg.execute(root)
+        dt = time.perf_counter() - t0
+    finally:
+        rg.close()
+    return {"cpu_reference_ms": dt * 1e3 * rows_total / r, "cpu_rows_timed": r,
+            "cpu_extrapolated": r < rows_total, "cpu_kind": "reference execute(), 1 thread"}
+
+
 def run_sweep(args):
     """Kernel-only time of relu(A.B + C) for every BASELINE shape, both
     precision modes, operands resident (min and median of CUDA-event-timed
@@ -596,6 +623,14 @@ def run_sweep(args):
         steps[1] = mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0)
         flops = 2.0 * M * N * K
         algo_bytes = 4.0 * (M * K + K * N + 2 * M * N)
+        A_h, B_h, C_h = A.cpu().numpy(), B.cpu().numpy(), Cm.cpu().numpy()
+
+        def build_rows(rg, r, A_h=A_h, B_h=B_h, C_h=C_h):
+            L = rg.lib
+            return L.g_relu(L.g_add(L.g_matmul(rg.input(A_h[:r]), rg.input(B_h)), rg.input(C_h[:r])))
+
+        cpu = cpu_reference_ms(build_rows, M, 2.0 * N * K)
+        del A_h, B_h, C_h
         for prec_name, prec in (("tf32", mlib.GPU_PRECISION_TF32), ("3xtf32", mlib.GPU_PRECISION_3XTF32)):
             def fn():
                 rc = lib.mxb_fused_gemm(ctx, Ap.data_ptr(), lda, Bp.data_ptr(), ldb, out.data_ptr(), N, M, N, K,
@@ -604,10 +639,15 @@ def run_sweep(args):
             reps = 20 if flops < 1e12 else 5
             tmin, tmed = time_launches(fn, reps)
             pk = peak if prec == mlib.GPU_PRECISION_TF32 else peak / 3
-            print(json.dumps({"sweep": "fused relu(A.B+C)", "M": M, "N": N, "K": K, "precision": prec_name,
-                              "ms_min": tmin, "ms_median": tmed, "tflops": flops / (tmin * 1e-3) / 1e12,
-                              "frac_tensor_peak": flops / (tmin * 1e-3) / 1e12 / pk,
-                              "gbs": algo_bytes / (tmin * 1e-3) / 1e9}), flush=True)
+            line = {"sweep": "fused relu(A.B+C)", "M": M, "N": N, "K": K, "precision": prec_name,
+                    "ms_min": tmin, "ms_median": tmed, "tflops": flops / (tmin * 1e-3) / 1e12,
+                    "frac_tensor_peak": flops / (tmin * 1e-3) / 1e12 / pk,
+                    "gbs": algo_bytes / (tmin * 1e-3) / 1e9}
+            if cpu:
+                line.update(cpu)
+                if cpu.get("cpu_reference_ms"):
+                    line["speedup_vs_cpu_reference"] = cpu["cpu_reference_ms"] / tmin
+            print(json.dumps(line), flush=True)
         del A, B, Cm, out, Ap, Bp
         torch.cuda.empty_cache()
 
@@ -623,6 +663,20 @@ def run_sweep(args):
     hw = torch.empty((Mx, H), device=dev)
     y = torch.empty((Mx, H), device=dev)
     o = torch.empty((Mx, D), device=dev)
+
+    host = {k: v.cpu().numpy() for k, v in (("X", X), ("W1", W1), ("W2", W2), ("W2p", W2p), ("W3", W3),
+                                             ("b1", b1), ("b2", b2), ("b3", b3))}
+
+    def build_mlp(rg, r):
+        # h = relu(X W1 + b1); y = relu(h W2 + b2) + h W2'; out = y W3 + b3 (rows of X independent)
+        L = rg.lib
+        w = {k: rg.input(v) for k, v in host.items() if k != "X"}
+        hn = L.g_relu(L.g_add(L.g_matmul(rg.input(host["X"][:r]), w["W1"]), w["b1"]))
+        yn = L.g_add(L.g_relu(L.g_add(L.g_matmul(hn, w["W2"]), w["b2"])), L.g_matmul(hn, w["W2p"]))
+        return L.g_add(L.g_matmul(yn, w["W3"]), w["b3"])
+
+    mlp_cpu = cpu_reference_ms(build_mlp, Mx, 2.0 * (D * H + 2 * H * H + H * D))
+    del host
 
     def st(*items):
         arr = (mlib.EpStepDev * max(1, len(items)))()
@@ -643,8 +697,12 @@ def run_sweep(args):
                 assert rc == 0, mlib.last_error()
         tmin, tmed = time_launches(mlp, 10)
         flops = 2.0 * Mx * (D * H + 2 * H * H + H * D)
-        print(json.dumps({"sweep": "3-layer MLP DAG (4 GEMM launches)", "M": Mx, "D": D, "H": H, "precision": prec_name,
-                          "ms_min": tmin, "ms_median": tmed, "tflops": flops / (tmin * 1e-3) / 1e12}), flush=True)
+        line = {"sweep": "3-layer MLP DAG (4 GEMM launches)", "M": Mx, "D": D, "H": H, "precision": prec_name,
+                "ms_min": tmin, "ms_median": tmed, "tflops": flops / (tmin * 1e-3) / 1e12}
+        line.update(mlp_cpu)
+        if mlp_cpu.get("cpu_reference_ms"):
+            line["speedup_vs_cpu_reference"] = mlp_cpu["cpu_reference_ms"] / tmin
+        print(json.dumps(line), flush=True)
 
         # The same DAG with h W2' fused into F2 (mxb_fused_gemm2): three launches.
         s2p = st(mlib.EpStepDev(mlib.MXB_EP_ADD_ROW, 0, b2.data_ptr(), H, 0.0, 0),

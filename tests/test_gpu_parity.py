@@ -266,6 +266,31 @@ def test_config2_square_sweep(lib, gpu_ctx, S, precision, host_threads):
 
 
 @pytest.mark.parametrize("precision", [X3, TF32], ids=["3xtf32", "tf32"])
+def test_oracle_noise_at_8192(lib, gpu_ctx, precision, host_threads):
+    """At K = 8192 the fp32 oracle's own k-ordered sum carries error of the
+    order of the 3xTF32 budget, so the result is also compared with the
+    float64 restatement of the same loop on the sampled rows: GPU vs fp32
+    oracle, GPU vs float64 and fp32 oracle vs float64 are all reported, and
+    the GPU must meet the tolerance against both references."""
+    S = 8192
+    A, B, C = _relu_abc(S, S, S, c_normal=True)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A), hg.input_node(B), [(OP_ADD, hg.input_node(C)), (OP_RELU, None)])
+    got = run_execute(lib, gpu_ctx, root, precision)
+    rows = _sample_rows(S, 256, seed=3)
+    steps = [("add", C), ("relu",)]
+    f32 = bindings.fused_oracle(A, B, steps, rows=rows, threads=host_threads)
+    f64 = bindings.fused_oracle(A, B, steps, rows=rows, f64=True, threads=host_threads)
+    e_gpu_f32 = rel_frobenius(got[rows], f32)
+    e_gpu_f64 = rel_frobenius(got[rows], f64)
+    e_f32_f64 = rel_frobenius(f32, f64)
+    print(f"\n8192^3 {'tf32' if precision == TF32 else '3xtf32'}: gpu vs fp32 oracle {e_gpu_f32:.3g}, "
+          f"gpu vs float64 {e_gpu_f64:.3g}, fp32 oracle vs float64 {e_f32_f64:.3g}")
+    assert e_gpu_f32 <= TOL[precision] and e_gpu_f64 <= TOL[precision]
+    assert e_f32_f64 < 1e-5
+
+
+@pytest.mark.parametrize("precision", [X3, TF32], ids=["3xtf32", "tf32"])
 @pytest.mark.parametrize("mnk", [(1000, 1000, 1000), (257, 4097, 129), (8191, 127, 3000), (1, 4096, 4096)])
 def test_config3_ragged(lib, gpu_ctx, mnk, precision, host_threads):
     M, N, K = mnk
