@@ -56,6 +56,10 @@ constexpr int kThreads = 192;
 constexpr int kBoxBytes = 32 * 32 * 4;  // one B box: 32 k-rows x 128 bytes
 
 constexpr int kSegKb = 8;           // k-blocks (of 32) per accumulation segment in 3xTF32 mode
+// With at most this many k-blocks the main loop is short (K <= 1024), so the
+// epilogue prefetches its rows of the ADD operands before the accumulator is
+// ready; longer loops prefetch once it is (earlier lines would be evicted).
+constexpr int kShortKb = 32;
 
 struct FusedParams {
     float* out;
@@ -387,6 +391,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (chunks > BN / 32) chunks = BN / 32;
             const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
             bool failed = false;
+            if (row_ok) {
+                // Short k-loops: fetch C while the MMAs run; long ones: just before the drain.
+                if (p.num_kb <= kShortKb) prefetch_full_operands(row, col0, min(BN, p.N - col0), p);
+            }
             if (SEG) {
                 // Sum the K segments in registers (fp32, round to nearest).
                 float total[BN];
@@ -437,6 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
+                if (row_ok && p.num_kb > kShortKb) prefetch_full_operands(row, col0, min(BN, p.N - col0), p);
                 const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * BN);
                 for (int c = 0; c < chunks; ++c) {
                     uint32_t r[32];
@@ -697,13 +706,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
         int acc = 0;
         uint32_t acc_phase = 0;
         for (int t = pair; t < p.num_tiles; t += num_pairs) {
-            const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
-            const bool got = !stop && mbar_wait_cluster(tfull_bar(acc), acc_phase, p.timeout_ns);
-            if (!__all_sync(0xffffffffu, got)) {
-                if (lane == 0 && !stop) raise_error(p, abort_flag, kErrEpilogue);
-                break;
-            }
-            tc_fence_after();
             int mb, nb;
             tile_coords(t, p, mb, nb);
             const int row = mb * 256 + row_in_tile;
@@ -711,7 +713,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             const int col0 = nb * BN;
             int chunks = (p.N - col0 + 31) / 32;
             if (chunks > c_first + kChunksPerWarp) chunks = c_first + kChunksPerWarp;
-            if (row_ok && chunks > c_first) prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p);
+            // C rows into L2: during the k-loop when it is short, else once the accumulator is ready.
+            const bool fetch = row_ok && chunks > c_first;
+            if (fetch && p.num_kb <= kShortKb)
+                prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p);
+            const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
+            const bool got = !stop && mbar_wait_cluster(tfull_bar(acc), acc_phase, p.timeout_ns);
+            if (!__all_sync(0xffffffffu, got)) {
+                if (lane == 0 && !stop) raise_error(p, abort_flag, kErrEpilogue);
+                break;
+            }
+            tc_fence_after();
+            if (fetch && p.num_kb > kShortKb)
+                prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p);
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                    static_cast<uint32_t>(acc * C::kAccCols);
             if (chunks <= c_first) {
@@ -1294,6 +1308,22 @@ bool use_pair_kernel(const GemmLaunch& g) {
     return g.M >= 256 && pair_tiles >= g.num_sms / 4;
 }
 
+// Tile width of the single-CTA kernels (128-row tiles): 256 once those tiles
+// fill the GPU, else the widest of 128 / 64 / 32 that gives at least half
+// the SMs a tile (32 when none does).  MINIXLA_SINGLE_BN forces one.
+int single_cta_width(const GemmLaunch& g) {
+    if (const char* v = getenv("MINIXLA_SINGLE_BN")) {
+        const int w = atoi(v);
+        if (w == 32 || w == 64 || w == 128 || w == 256) return w;
+    }
+    const long long tiles_m = (g.M + kBM - 1) / kBM;
+    auto tiles = [&](int bn) { return tiles_m * ((g.N + bn - 1) / bn); };
+    if (g.N > 128 && tiles(256) >= g.num_sms) return 256;
+    for (int bn : {128, 64})
+        if (tiles(bn) >= g.num_sms / 2) return bn;
+    return 32;
+}
+
 // TF32 pair kernel with 256 x 512 tiles: per k-block each CTA stages 16 KiB
 // of A and 32 KiB of B for eight 256 x 256 x 8 MMAs -- a quarter fewer bytes
 // per MMA than the 256 x 256 tile, whose 32 KiB feed four.  The 512
@@ -1323,18 +1353,27 @@ cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
         if (tiles256 >= g.num_sms / 2) return run_pair_variant<4, 256, true>(g, stream);
         return run_pair_variant<6, 128, true>(g, stream);
     }
-    if (g.precision == GPU_PRECISION_3XTF32)
-        return use_pair_kernel(g) ? run_pair3_variant<3>(g, stream) : run_variant<128, 3, true, true>(g, stream);
+    if (g.precision == GPU_PRECISION_3XTF32) {
+        if (use_pair_kernel(g)) return run_pair3_variant<3>(g, stream);
+        switch (single_cta_width(g)) {
+            case 256:
+            case 128: return run_variant<128, 3, true, true>(g, stream);
+            case 64: return run_variant<64, 4, true, true>(g, stream);
+            default: return run_variant<32, 5, true, true>(g, stream);
+        }
+    }
     if (use_pair_kernel(g)) {
         return pair_wide_tiles(g) ? run_pair_variant<4, 512, false>(g, stream)
                                   : run_pair_variant<6, 256, false>(g, stream);
     }
-    // One TF32 product on one CTA.  Narrow or small problems use 128-wide tiles so more SMs get work.
-    const long long tiles_m = (g.M + kBM - 1) / kBM;
-    const long long tiles256 = tiles_m * ((g.N + 255) / 256);
-    const long long tiles128 = tiles_m * ((g.N + 127) / 128);
-    if (g.N <= 128 || (tiles256 < g.num_sms && tiles128 > tiles256)) return run_variant<128, 6, false, false>(g, stream);
-    return run_variant<256, 4, false, false>(g, stream);
+    // One TF32 product on one CTA.  Narrower tiles for problems with few
+    // tiles, so more SMs share the k-loops and the epilogue.
+    switch (single_cta_width(g)) {
+        case 256: return run_variant<256, 4, false, false>(g, stream);
+        case 128: return run_variant<128, 6, false, false>(g, stream);
+        case 64: return run_variant<64, 8, false, false>(g, stream);
+        default: return run_variant<32, 8, false, false>(g, stream);
+    }
 }
 
 // ------------------------------------------------------------------ bounded-wait probe

@@ -348,16 +348,19 @@ def test_full_size_checksums(lib, gpu_ctx, precision):
 
 
 @pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
-@pytest.mark.parametrize("variant", ["pair", "pair512", "single"])
+@pytest.mark.parametrize("variant", ["pair", "pair512", "single", "single64", "single32"])
 @pytest.mark.parametrize("mnk", [(256, 256, 32), (300, 520, 100), (1000, 1000, 1000), (257, 4097, 129),
                                  (8191, 127, 3000), (2048, 2048, 2048), (4096, 300, 1024), (640, 384, 4100)])
 def test_kernel_variants(lib, gpu_ctx, mnk, variant, precision, monkeypatch, host_threads):
     """Every kernel of each mode (CTA pair with 256- and, in TF32, 512-wide
-    tiles; single CTA) on tile-edge shapes, with a full-matrix add, a bias
+    tiles; single CTA with 128/256-, 64- and 32-wide tiles) on tile-edge shapes, with a full-matrix add, a bias
     row and relu in the epilogue.  K = 4100 ends on a partial k-block and a
     partial 3xTF32 segment."""
     if variant == "pair512" and precision == X3:
         pytest.skip("3xTF32 has one pair tile width")
+    if variant.startswith("single") and variant != "single":
+        monkeypatch.setenv("MINIXLA_SINGLE_BN", variant[len("single"):])
+        variant = "single"
     monkeypatch.setenv("MINIXLA_GEMM_VARIANT", variant)
     M, N, K = mnk
     A, B, C = _relu_abc(M, N, K, c_normal=True)
