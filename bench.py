@@ -574,8 +574,9 @@ def cpu_reference_ms(build, rows_total: int, flops_per_row: float):
 def run_sweep(args):
     """Kernel-only time of relu(A.B + C) for every BASELINE shape, both
     precision modes, operands resident (min and median of CUDA-event-timed
-    launches after warm-up), plus the 3-layer MLP DAG of config 4 through the
-    device API (one launch per fused node)."""
+    launches after warm-up; each behind a ~50 us spin on the stream so the
+    host's launch preparation stays outside the events), plus the 3-layer
+    MLP DAG of config 4 through the device API (one launch per fused node)."""
     import numpy as np
     import torch
 
@@ -604,6 +605,10 @@ def run_sweep(args):
         ts = []
         for _ in range(reps):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            # Keep the stream busy (~50 us) while the call is prepared, so the
+            # events bracket the kernels rather than the host's launch work.
+            with torch.cuda.stream(stream):
+                torch.cuda._sleep(100_000)
             e0.record(stream)
             fn()
             e1.record(stream)

@@ -223,10 +223,11 @@ MXB_API int mxb_fused_gemm(GpuCtx* ctx,
  * feeding a fused node's ADD step as a node of its own (optimizer.c:94-132)
  * and eval_fused adds its stored result (graph.c:98-105); gpu_execute uses
  * this fusion for such a matmul when the fused node is its only consumer and
- * both share the left operand.  In TF32 mode with A2 == A (same pointer,
- * pitch and K2 == K, M > 16) both products accumulate side by side in TMEM in
- * one kernel that stages A once, and the second never goes to HBM; otherwise
- * the second product runs first into pooled workspace.  Values are the same
+ * both share the left operand.  With A2 == A (same pointer, pitch and
+ * K2 == K, M > 16; in 3xTF32 mode also enough 256 x 128 tiles to fill a
+ * quarter of the SMs) both products accumulate side by side in TMEM in one
+ * kernel that stages A once, and the second never goes to HBM; otherwise the
+ * second product runs first into pooled workspace.  Values are the same
  * either way.  A2 and B2
  * follow mxb_fused_gemm's layout rules (lda2, ldb2 % 4 == 0); exactly one
  * ADD_PRODUCT step. */

@@ -791,29 +791,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
 // reads TMEM lane quadrant w % 4 and column half (w - 2) / 4, so each thread
 // keeps 128 running totals.  Per SM this stages the same A bytes as the
 // single-CTA kernel for twice the columns.
+//
+// DUAL: a second product A @ B2 on the same A (the two-product form of the
+// TF32 pair kernel).  The tile is 256 x 128 per product: a stage holds A's
+// big and small parts with 64-column halves of B and B2 (64 KiB again), the
+// leader issues the three MMAs (N=128) for each product, and each segment
+// buffer holds both 128-column accumulators.  Warp w of column half h sums
+// columns 64h .. 64h+63 of both products, so the epilogue finds A.B and
+// A.B2 of the same output columns in one thread.
 
 constexpr int kPair3Threads = 320;  // TMA warp, MMA warp, 8 epilogue warps
 
-template <int STAGES>
+template <int STAGES, bool DUAL>
 struct Pair3Cfg {
+    static constexpr int kBN = DUAL ? 128 : 256;           // output columns of the pair tile
+    static constexpr int kProducts = DUAL ? 2 : 1;
     static constexpr int kABytes = 128 * kBK * 4;          // 16 KiB: this CTA's A rows
-    static constexpr int kBBytes = 128 * kBK * 4;          // 16 KiB: this CTA's 128 B columns
-    static constexpr int kOperandBytes = kABytes + kBBytes;
+    static constexpr int kBBytes = (kBN / 2) * kBK * 4;    // this CTA's B columns, per product
+    static constexpr int kOperandBytes = kABytes + kProducts * kBBytes;
     static constexpr int kStageBytes = 2 * kOperandBytes;  // big parts, then small parts
-    static constexpr int kTmemCols = 512;                  // two 256-column segment accumulators
+    static constexpr int kTmemCols = 512;                  // two segment buffers of 256 columns
     static constexpr int kBarOffset = STAGES * kStageBytes;
     static constexpr int kNumBars = 2 * STAGES + 5;
     static constexpr int kSmemBytes = 1024 + kBarOffset + kNumBars * 8 + 16;
+    static_assert(kProducts * kBN == 256, "a segment buffer is 256 columns");
     static_assert(kStageBytes % 1024 == 0, "stages must keep 1 KiB swizzle alignment");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-template <int STAGES>
+template <int STAGES, bool DUAL>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
     fused_gemm_pair3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmAs, const __grid_constant__ CUtensorMap tmBs,
+                            const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmB2s,
                             const __grid_constant__ FusedParams p) {
-    using C = Pair3Cfg<STAGES>;
+    using C = Pair3Cfg<STAGES, DUAL>;
+    constexpr int BN = C::kBN;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -850,6 +863,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
         tma_prefetch_desc(&tmB);
         tma_prefetch_desc(&tmAs);
         tma_prefetch_desc(&tmBs);
+        if (DUAL) {
+            tma_prefetch_desc(&tmB2);
+            tma_prefetch_desc(&tmB2s);
+        }
     }
     if (warp == 1) {
         tmem_alloc_pair(smem_addr(tmem_slot), C::kTmemCols);
@@ -872,7 +889,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
                 int mb, nb;
                 tile_coords(t, p, mb, nb);
                 const int m0 = mb * 256 + static_cast<int>(rank) * 128;
-                const int n0 = nb * 256 + static_cast<int>(rank) * 128;
+                const int n0 = nb * BN + static_cast<int>(rank) * (BN / 2);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (*abort_flag) { ok = false; break; }
                     if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1u, p.timeout_ns)) {
@@ -881,16 +898,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
                         break;
                     }
                     uint8_t* st = smem + stage * C::kStageBytes;
+                    uint8_t* st2 = st + C::kOperandBytes;
                     if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * C::kStageBytes);
                     const uint32_t fb = mapa_shared(full_bar(stage), 0);
                     const int k0 = kb * kBK;
                     tma_load_2d_pair(smem_addr(st), &tmA, fb, k0, m0);
-                    tma_load_2d_pair(smem_addr(st + C::kOperandBytes), &tmAs, fb, k0, m0);
+                    tma_load_2d_pair(smem_addr(st2), &tmAs, fb, k0, m0);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
+                    for (int j = 0; j < BN / 64; ++j) {
                         tma_load_2d_pair(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb, n0 + 32 * j, k0);
-                        tma_load_2d_pair(smem_addr(st + C::kOperandBytes + C::kABytes + j * kBoxBytes), &tmBs, fb,
-                                         n0 + 32 * j, k0);
+                        tma_load_2d_pair(smem_addr(st2 + C::kABytes + j * kBoxBytes), &tmBs, fb, n0 + 32 * j, k0);
+                        if (DUAL) {
+                            tma_load_2d_pair(smem_addr(st + C::kABytes + C::kBBytes + j * kBoxBytes), &tmB2, fb,
+                                             n0 + 32 * j, k0);
+                            tma_load_2d_pair(smem_addr(st2 + C::kABytes + C::kBBytes + j * kBoxBytes), &tmB2s, fb,
+                                             n0 + 32 * j, k0);
+                        }
                     }
                     ++issued;
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -909,7 +932,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (leader only)
         if (lane == 0 && rank == 0) {
-            constexpr uint32_t idesc = idesc_tf32(256, 256);
+            constexpr uint32_t idesc = idesc_tf32(256, BN);
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
@@ -934,20 +957,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
                         }
                         tc_fence_after();
                         const uint32_t a_addr = smem_addr(smem + stage * C::kStageBytes);
-                        const uint32_t b_addr = a_addr + C::kABytes;
 #pragma unroll
                         for (int kk = 0; kk < kBK / 8; ++kk) {
                             const uint64_t da = smem_desc(a_addr + kk * 32, 16, 1024, kLayoutSW128);
-                            const uint64_t db = smem_desc(b_addr + kk * 1024, kBoxBytes, 512, kLayoutSW128Base32B);
                             const uint64_t das =
                                 smem_desc(a_addr + C::kOperandBytes + kk * 32, 16, 1024, kLayoutSW128);
-                            const uint64_t dbs = smem_desc(b_addr + C::kOperandBytes + kk * 1024, kBoxBytes, 512,
-                                                           kLayoutSW128Base32B);
                             const uint32_t accumulate = (kb != k_begin || kk != 0) ? 1u : 0u;
-                            // Small cross terms first, the dominant big*big product last.
-                            mma_tf32_pair(d_tmem, da, dbs, idesc, accumulate);
-                            mma_tf32_pair(d_tmem, das, db, idesc, 1u);
-                            mma_tf32_pair(d_tmem, da, db, idesc, 1u);
+#pragma unroll
+                            for (int q = 0; q < C::kProducts; ++q) {
+                                const uint32_t b_addr = a_addr + C::kABytes + q * C::kBBytes;
+                                const uint64_t db =
+                                    smem_desc(b_addr + kk * 1024, kBoxBytes, 512, kLayoutSW128Base32B);
+                                const uint64_t dbs = smem_desc(b_addr + C::kOperandBytes + kk * 1024, kBoxBytes,
+                                                               512, kLayoutSW128Base32B);
+                                const uint32_t d = d_tmem + static_cast<uint32_t>(q * BN);
+                                // Small cross terms first, the dominant big*big product last.
+                                mma_tf32_pair(d, da, dbs, idesc, accumulate);
+                                mma_tf32_pair(d, das, db, idesc, 1u);
+                                mma_tf32_pair(d, da, db, idesc, 1u);
+                            }
                         }
                         mma_commit_pair(empty_bar(stage), 0x3);
                         if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -963,13 +991,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
         }
     } else {
         // ------------------------------------------------------------ epilogue (both CTAs, 8 warps)
+        // Each thread sums 128 accumulator columns: columns 128h .. 128h+127
+        // of the single product, or (DUAL) 64h .. 64h+63 of both products.
         const int quad = warp & 3;
         const int half = (warp - 2) >> 2;
         const int row_in_tile = static_cast<int>(rank) * 128 + quad * 32 + lane;
         const uint32_t tempty_leader0 = mapa_shared(tempty_bar(0), 0);
         const uint32_t tempty_leader1 = mapa_shared(tempty_bar(1), 0);
-        const uint32_t lane_base =
-            tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(half * 128);
+        const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+        // TMEM column of this thread's 16-column group g (0..7).
+        auto group_col = [&](int g) -> uint32_t {
+            return DUAL ? static_cast<uint32_t>((g >> 2) * BN + half * 64 + 16 * (g & 3))
+                        : static_cast<uint32_t>(half * 128 + 16 * g);
+        };
         int acc = 0;
         uint32_t acc_phase = 0;
         bool failed = false;
@@ -978,7 +1012,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
             tile_coords(t, p, mb, nb);
             const int row = mb * 256 + row_in_tile;
             const bool row_ok = row < p.M;
-            const int col0 = nb * 256 + half * 128;
+            const int col0 = nb * BN + half * (DUAL ? 64 : 128);  // first output column of this thread
             float total[128];
             for (int k_begin = 0; k_begin < p.num_kb; k_begin += p.seg_kb) {
                 const bool first = k_begin == 0;
@@ -996,32 +1030,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
                 // After the last segment the totals go back into this accumulator,
                 // so the epilogue below runs with the registers free.
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
+                for (int g = 0; g < 8; ++g) {
                     uint32_t r[16];
-                    tmem_ld_32x32b_x16(taddr + 16 * c, r);
+                    tmem_ld_32x32b_x16(taddr + group_col(g), r);
                     tmem_ld_wait();
 #pragma unroll
                     for (int i = 0; i < 16; ++i)
-                        total[16 * c + i] = first ? __uint_as_float(r[i]) : total[16 * c + i] + __uint_as_float(r[i]);
+                        total[16 * g + i] = first ? __uint_as_float(r[i]) : total[16 * g + i] + __uint_as_float(r[i]);
                     if (last) {
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(total[16 * c + i]);
-                        tmem_st_32x32b_x16(taddr + 16 * c, r);
+                        for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(total[16 * g + i]);
+                        tmem_st_32x32b_x16(taddr + group_col(g), r);
                     }
                 }
                 if (last) {
                     tmem_st_wait();
-                    for (int c = 0; c < 4; ++c) {
-                        const int col = col0 + 32 * c;
-                        if (col >= p.N) break;
-                        uint32_t r[32];
-                        tmem_ld_32x32b_x32(taddr + 32 * c, r);
-                        tmem_ld_wait();
-                        float v[32];
+                    if (DUAL) {
+                        // 16 columns of both products at a time.
+                        for (int c = 0; c < 4; ++c) {
+                            const int col = col0 + 16 * c;
+                            if (col >= p.N) break;
+                            uint32_t r[16], r2[16];
+                            tmem_ld_32x32b_x16(taddr + group_col(c), r);
+                            tmem_ld_32x32b_x16(taddr + group_col(4 + c), r2);
+                            tmem_ld_wait();
+                            float v[16], w[16];
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-                        apply_epilogue(v, row, col, row_ok, p);
-                        if (row_ok) store_row_chunk(v, row, col, p);
+                            for (int i = 0; i < 16; ++i) {
+                                v[i] = __uint_as_float(r[i]);
+                                w[i] = __uint_as_float(r2[i]);
+                            }
+                            apply_epilogue<16>(v, row, col, row_ok, p, w);
+                            if (row_ok) store_row_chunk<16>(v, row, col, p);
+                        }
+                    } else {
+                        for (int c = 0; c < 4; ++c) {
+                            const int col = col0 + 32 * c;
+                            if (col >= p.N) break;
+                            uint32_t r[32];
+                            tmem_ld_32x32b_x32(taddr + group_col(2 * c), r);
+                            tmem_ld_wait();
+                            float v[32];
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                            apply_epilogue(v, row, col, row_ok, p);
+                            if (row_ok) store_row_chunk(v, row, col, p);
+                        }
                     }
                 }
                 tc_fence_before();
@@ -1220,10 +1274,10 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-template <int STAGES>
+template <int STAGES, bool DUAL>
 cudaError_t run_pair3_variant(const GemmLaunch& g, cudaStream_t stream) {
-    using C = Pair3Cfg<STAGES>;
-    auto kernel = fused_gemm_pair3_kernel<STAGES>;
+    using C = Pair3Cfg<STAGES, DUAL>;
+    auto kernel = fused_gemm_pair3_kernel<STAGES, DUAL>;
     static std::mutex mu;
     static uint64_t configured = 0;
     static int max_clusters[64] = {0};
@@ -1265,11 +1319,21 @@ cudaError_t run_pair3_variant(const GemmLaunch& g, cudaStream_t stream) {
 
     constexpr CUtensorMapSwizzle kSwA = CU_TENSOR_MAP_SWIZZLE_128B;
     constexpr CUtensorMapSwizzle kSwB = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-    CUtensorMap mA, mB, mAs, mBs;
+    CUtensorMap mA, mB, mAs, mBs, mB2, mB2s;
     if (!make_map(&mA, g.A, g.M, g.K, g.lda, kBK, 128, kSwA) || !make_map(&mB, g.B, g.K, g.N, g.ldb, 32, kBK, kSwB) ||
         !make_map(&mAs, g.A_small, g.M, g.K, g.lda, kBK, 128, kSwA) ||
         !make_map(&mBs, g.B_small, g.K, g.N, g.ldb, 32, kBK, kSwB))
         return cudaErrorInvalidValue;
+    if (DUAL) {
+        // The second product shares A (same rows, K and pitch); B2 and its low part have maps of their own.
+        if (g.A2 != g.A || g.K2 != g.K || g.lda2 != g.lda || !g.B2 || !g.B2_small ||
+            !make_map(&mB2, g.B2, g.K, g.N, g.ldb2, 32, kBK, kSwB) ||
+            !make_map(&mB2s, g.B2_small, g.K, g.N, g.ldb2, 32, kBK, kSwB))
+            return cudaErrorInvalidValue;
+    } else {
+        mB2 = mB;
+        mB2s = mBs;
+    }
 
     FusedParams p{};
     p.out = g.out;
@@ -1279,7 +1343,7 @@ cudaError_t run_pair3_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.K = g.K;
     p.n_steps = g.n_steps;
     p.tiles_m = (g.M + 255) / 256;
-    p.tiles_n = (g.N + 255) / 256;
+    p.tiles_n = (g.N + C::kBN - 1) / C::kBN;
     p.num_tiles = p.tiles_m * p.tiles_n;
     p.num_kb = (g.K + kBK - 1) / kBK;
     p.group_m = 8;
@@ -1290,7 +1354,7 @@ cudaError_t run_pair3_variant(const GemmLaunch& g, cudaStream_t stream) {
     for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
 
     const int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;
-    kernel<<<2 * pairs, kPair3Threads, C::kSmemBytes, stream>>>(mA, mB, mAs, mBs, p);
+    kernel<<<2 * pairs, kPair3Threads, C::kSmemBytes, stream>>>(mA, mB, mAs, mBs, mB2, mB2s, p);
     note_launch();
     return cudaGetLastError();
 }
@@ -1345,8 +1409,9 @@ bool pair_wide_tiles(const GemmLaunch& g) {
 
 cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
     if (g.A2) {
-        // Two products of one A in one kernel (TF32 only; callers run other cases as two launches).
-        // 256-column tiles put both accumulators in the 512 TMEM columns (one buffer,
+        // Two products of one A in one kernel (callers run other cases as two launches).
+        if (g.precision == GPU_PRECISION_3XTF32) return run_pair3_variant<3, true>(g, stream);
+        // TF32: 256-column tiles put both accumulators in the 512 TMEM columns (one buffer,
         // 48 KiB stages); 128-column tiles keep two buffers for problems with few tiles.
         if (g.precision != GPU_PRECISION_TF32) return cudaErrorInvalidValue;
         const long long tiles256 = static_cast<long long>((g.M + 255) / 256) * ((g.N + 255) / 256);
@@ -1354,7 +1419,7 @@ cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
         return run_pair_variant<6, 128, true>(g, stream);
     }
     if (g.precision == GPU_PRECISION_3XTF32) {
-        if (use_pair_kernel(g)) return run_pair3_variant<3>(g, stream);
+        if (use_pair_kernel(g)) return run_pair3_variant<3, false>(g, stream);
         switch (single_cta_width(g)) {
             case 256:
             case 128: return run_variant<128, 3, true, true>(g, stream);
@@ -1393,6 +1458,26 @@ __global__ void wait_timeout_probe_kernel(int* err, unsigned long long timeout_n
 cudaError_t launch_wait_timeout_probe(int* err, unsigned long long timeout_ns, cudaStream_t stream) {
     wait_timeout_probe_kernel<<<1, 32, 0, stream>>>(err, timeout_ns);
     note_launch();
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ timer hold
+//
+// Keeps the stream busy for about `ns` of global time (and at most 2^24
+// polls), so that a start event recorded after it is stamped when the work
+// behind it is already queued: kernel timers then measure the kernels, not
+// the host's time to enqueue them.
+
+namespace {
+__global__ void hold_kernel(unsigned long long ns) {
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 0; it < (1u << 24); ++it)
+        if (global_timer_ns() - t0 >= ns) break;
+}
+}  // namespace
+
+cudaError_t launch_hold(unsigned long long ns, cudaStream_t stream) {
+    hold_kernel<<<1, 1, 0, stream>>>(ns);
     return cudaGetLastError();
 }
 

@@ -27,7 +27,8 @@ struct GemmLaunch {
     const float* A_small;              // 3xTF32 only: x - rne_tf32(x), same pitches
     const float* B_small;
     const float* A2; long long lda2;   // optional second product A2[M,K2] @ B2[K2,N], added at the
-    const float* B2; long long ldb2;   // MXB_EP_ADD_PRODUCT step (TF32 only); A2 == nullptr: none
+    const float* B2; long long ldb2;   // MXB_EP_ADD_PRODUCT step; A2 == nullptr: none
+    const float* B2_small;             // 3xTF32 only: low part of B2
     int K2;
     float* out; long long ldo;
     int M, N, K;
@@ -60,6 +61,7 @@ cudaError_t launch_add(const float* a, long long n, const float* b, long long b_
                        int num_sms, cudaStream_t stream);
 cudaError_t launch_relu(const float* x, long long n, float* out, int num_sms, cudaStream_t stream);
 cudaError_t launch_wait_timeout_probe(int* err, unsigned long long timeout_ns, cudaStream_t stream);
+cudaError_t launch_hold(unsigned long long ns, cudaStream_t stream);
 
 // Process-wide count of kernel launches issued by this library.
 void note_launch(unsigned n = 1);

@@ -425,19 +425,20 @@ static bool dual_kernel_enabled() {
 // feeds a fused node's ADD step stays a node of its own and eval_fused adds
 // its stored result (graph.c:98-105) -- config 4's F2 = relu(h W2 + b2) +
 // h W2'.  When that fused node is the matmul's only reader and both products
-// share the left operand, they run in one kernel (TF32 pair kernel, DUAL): A
-// is staged once for both and the matmul's value never goes to HBM.
-// Conditions: TF32, the matmul is 2-D, not the root, read once (by one ADD
-// step), has the fused node's A node as its A, and is shaped like the fused
-// node's 2-D output with more than 16 rows; the row pitches are multiples of
-// 4 (no padding copies).
+// share the left operand, they run in one kernel (the pair kernels' DUAL
+// forms, TF32 and 3xTF32): A is staged once for both and the matmul's value
+// never goes to HBM.  Conditions: the matmul is 2-D, not the root, read once
+// (by one ADD step), has the fused node's A node as its A, and is shaped like
+// the fused node's 2-D output with more than 16 rows; the row pitches are
+// multiples of 4 (no padding copies).  launch_gemm still runs the two
+// products as two launches where the one-kernel form does not apply.
 // Returns, per node, the index of the matmul it absorbs (-1 for none).
 static std::vector<int> plan_products(const std::vector<const Node*>& order,
                                       const std::unordered_map<const Node*, int>& index,
                                       const std::vector<Info>& info, int precision) {
     const size_t n = order.size();
     std::vector<int> absorb(n, -1);
-    if (precision != GPU_PRECISION_TF32 || !dual_kernel_enabled()) return absorb;
+    if (!dual_kernel_enabled()) return absorb;
     std::vector<int> refs(n, 0);
     for (size_t i = 0; i < n; ++i)
         for (int a = 0; a < order[i]->n_inputs; ++a) refs[index.at(order[i]->inputs[a])]++;
@@ -507,20 +508,31 @@ struct Product {
     const float* B;
     long long ldb;
     int K;
+    const float* B_small = nullptr;  // 3xTF32: low part of B made beforehand (else split here)
 };
+
+// Whether launch_gemm runs a shared-A second product in the same kernel:
+// TF32 always (M > 16); 3xTF32 when the 256 x 128 pair tiles occupy a
+// quarter of the SMs (else two launches, on the single-CTA kernels).
+static bool dual_in_one_kernel(const GpuCtx* ctx, const float* A, long long lda, int M, int N, int K,
+                               const Product& prod, int precision) {
+    if (M <= kSkinnyMaxRows || !dual_kernel_enabled() || prod.A != A || prod.lda != lda || prod.K != K) return false;
+    if (precision == GPU_PRECISION_TF32) return true;
+    const long long tiles = static_cast<long long>((M + 255) / 256) * ((N + 127) / 128);
+    return M >= 256 && tiles >= ctx->num_sms / 4;
+}
 
 static int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
                        long long ldo, int M, int N, int K, const EpStepDev* steps, int n_steps, int precision,
                        cudaStream_t stream, const float* B_small_pre = nullptr, long long row_base = 0,
                        const Product* prod = nullptr) {
-    if (prod && !(precision == GPU_PRECISION_TF32 && M > kSkinnyMaxRows && dual_kernel_enabled() && prod->A == A &&
-                  prod->lda == lda && prod->K == K)) {
+    if (prod && !dual_in_one_kernel(ctx, A, lda, M, N, K, *prod, precision)) {
         // Two launches: the second product into pooled workspace, then the
         // node reading it as a full add at the same step.
         float* ws = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(M) * N * sizeof(float), stream));
         if (!ws) return MXB_E_NOMEM;
         int rc = launch_gemm(ctx, prod->A, prod->lda, prod->B, prod->ldb, ws, N, M, N, prod->K, nullptr, 0, precision,
-                             stream);
+                             stream, prod->B_small);
         if (rc == MXB_OK) {
             EpStepDev st2[MXB_MAX_EPILOGUE];
             for (int i = 0; i < n_steps; ++i) {
@@ -575,21 +587,28 @@ static int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* 
     g.err = ctx->d_err;
     g.timeout_ns = ctx->timeout_ns;
     g.num_sms = ctx->num_sms;
-    float* ws[2] = {nullptr, nullptr};
+    float* ws[3] = {nullptr, nullptr, nullptr};
     int rc = MXB_OK;
     if (precision == GPU_PRECISION_3XTF32) {
         const size_t a_bytes = static_cast<size_t>(M) * lda * 4, b_bytes = static_cast<size_t>(K) * ldb * 4;
+        const bool need_b2 = prod && !prod->B_small;
         ws[0] = static_cast<float*>(ctx->pool->alloc(a_bytes, stream));
         if (ws[0] && !B_small_pre) ws[1] = static_cast<float*>(ctx->pool->alloc(b_bytes, stream));
-        if (!ws[0] || (!B_small_pre && !ws[1])) {
+        if (ws[0] && need_b2)
+            ws[2] = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(K) * prod->ldb * 4, stream));
+        if (!ws[0] || (!B_small_pre && !ws[1]) || (need_b2 && !ws[2])) {
             rc = MXB_E_NOMEM;
         } else if (!cuda_ok(launch_split_tf32(A, M, K, lda, ws[0], lda, ctx->num_sms, stream), "split A") ||
                    (!B_small_pre &&
-                    !cuda_ok(launch_split_tf32(B, K, N, ldb, ws[1], ldb, ctx->num_sms, stream), "split B"))) {
+                    !cuda_ok(launch_split_tf32(B, K, N, ldb, ws[1], ldb, ctx->num_sms, stream), "split B")) ||
+                   (need_b2 && !cuda_ok(launch_split_tf32(prod->B, K, N, prod->ldb, ws[2], prod->ldb, ctx->num_sms,
+                                                          stream),
+                                        "split B2"))) {
             rc = MXB_E_CUDA;
         } else {
             g.A_small = ws[0];
             g.B_small = B_small_pre ? B_small_pre : ws[1];
+            if (prod) g.B2_small = prod->B_small ? prod->B_small : ws[2];
         }
     }
     if (rc == MXB_OK && !cuda_ok(launch_fused_gemm(g, stream), "fused GEMM launch")) rc = MXB_E_CUDA;
@@ -811,7 +830,7 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
     const int rows_per = std::max(128, (M + chunks - 1) / chunks);
     const int n_chunks = (M + rows_per - 1) / rows_per;
     const size_t n = order.size();
-    std::vector<float*> b_small(n, nullptr);
+    std::vector<float*> b_small(n, nullptr), b2_small(n, nullptr);
     size_t next_event = 0;
     int rc = MXB_OK;
     auto order_after = [&](cudaStream_t waiter, cudaStream_t signaller) {
@@ -863,6 +882,18 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
                             "split B")) {
             rc = MXB_E_CUDA;
         }
+        if (rc == MXB_OK && absorb[i] >= 0) {
+            // The absorbed matmul's B: its low part once for all chunks too.
+            const Info& b2 = info[index.at(order[absorb[i]]->inputs[1])];
+            b2_small[i] = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(b2.size) * 4, cs));
+            if (!b2_small[i]) {
+                rc = MXB_E_NOMEM;
+            } else if (!cuda_ok(launch_split_tf32(b2.dev, b2.dims[0], b2.dims[1], b2.dims[1], b2_small[i],
+                                                  b2.dims[1], ctx->num_sms, cs),
+                                "split B2")) {
+                rc = MXB_E_CUDA;
+            }
+        }
     }
     std::vector<cudaEvent_t> computed(n_chunks, nullptr);
     for (int c = 0; c < n_chunks && rc == MXB_OK; ++c) {
@@ -912,7 +943,7 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
                     const Info& a2 = info[index.at(m->inputs[0])];
                     const Info& b2 = info[index.at(m->inputs[1])];
                     const int K2 = a2.dims[1];
-                    prod = Product{a2.dev + r0 * K2, K2, b2.dev, N, K2};
+                    prod = Product{a2.dev + r0 * K2, K2, b2.dev, N, K2, b2_small[i]};
                 }
                 rc = launch_gemm(ctx, a.dev + r0 * K, K, b.dev, N, f.dev + r0 * N, N, static_cast<int>(r1 - r0), N, K,
                                  steps, n_steps, ctx->precision, cs, b_small[i], r0, absorb[i] >= 0 ? &prod : nullptr);
@@ -955,6 +986,7 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
     for (size_t i = 0; i < n; ++i) {
         if (!info[i].borrowed) ctx->pool->release(info[i].dev, cs);
         ctx->pool->release(b_small[i], cs);
+        ctx->pool->release(b2_small[i], cs);
         info[i].dev = nullptr;
     }
     cudaStreamSynchronize(ds);
@@ -1654,6 +1686,13 @@ static double time_fused(Node* root, GpuCtx* ctx, int warmup, int reps, int prec
         }
         double lo = 1e30;
         for (int r = 0; r < reps && rc == MXB_OK; ++r) {
+            // The stream is held busy while the launch is prepared and queued,
+            // so the events bracket the kernels alone (gpu_exec.c:380-398 times
+            // its kernel launch between two events the same way).
+            if (!cuda_ok(launch_hold(50000, ctx->stream), "timer hold launch")) {
+                rc = MXB_E_CUDA;
+                break;
+            }
             cudaEventRecord(ctx->ev0, ctx->stream);
             rc = run_gemm_node(ctx, root, s.dA, s.M, s.K, s.dB, s.N, s.dOut, s.dev_of, s.size_of, precision,
                                ctx->stream);

@@ -481,14 +481,17 @@ def test_resident_weights(lib, gpu_ctx):
 # ---------------------------------------------------------------- bare matmul fused into its consumer
 
 
-@pytest.mark.parametrize("M", [8, 200, 1000, 4096])
-def test_product_fusion_in_graphs(lib, gpu_ctx, M, monkeypatch, host_threads):
+@pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
+@pytest.mark.parametrize("M,H", [(8, 256), (200, 256), (1000, 256), (4096, 256), (1024, 2048)])
+def test_product_fusion_in_graphs(lib, gpu_ctx, M, H, precision, monkeypatch, host_threads):
     """Config 4's pattern, y = relu(h W2 + b2) + h W2' with h W2' a bare
-    matmul read only by y: in TF32 mode both products run in one kernel.
-    The result matches the two-launch form (MINIXLA_DUAL_GEMM=0) bit for bit
-    and the oracle within the TF32 tolerance; M = 8 keeps the two-launch
-    form, M = 200 runs on the one-stream executor, larger M row-streamed."""
-    D, H = 96, 256
+    matmul read only by y: both products run in one kernel (TF32 always,
+    3xTF32 when its 256 x 128 pair tiles fill a quarter of the SMs, here
+    (1024, 2048)).  The result matches the two-launch form
+    (MINIXLA_DUAL_GEMM=0) bit for bit and the oracle within the mode's
+    tolerance; M = 8 keeps the two-launch form, M = 200 runs on the
+    one-stream executor, larger M row-streamed."""
+    D = 96
     X = datagen.uniform((M, D), 80)
     W1 = datagen.normal((D, H), 81, 0.0, 1.0 / np.sqrt(D))
     W2 = datagen.normal((H, H), 82, 0.0, 1.0 / np.sqrt(H))
@@ -500,15 +503,15 @@ def test_product_fusion_in_graphs(lib, gpu_ctx, M, monkeypatch, host_threads):
     h = hg.fused_node(x, hg.input_node(W1), [(OP_ADD, hg.input_node(b1)), (OP_RELU, None)])
     hw = hg.g_matmul(h, hg.input_node(W2p))
     root = hg.fused_node(h, hg.input_node(W2), [(OP_ADD, hg.input_node(b2)), (OP_RELU, None), (OP_ADD, hw)])
-    fused = run_execute(lib, gpu_ctx, root, TF32)
+    fused = run_execute(lib, gpu_ctx, root, precision)
     monkeypatch.setenv("MINIXLA_DUAL_GEMM", "0")
-    two = run_execute(lib, gpu_ctx, root, TF32)
+    two = run_execute(lib, gpu_ctx, root, precision)
     monkeypatch.delenv("MINIXLA_DUAL_GEMM")
     assert np.array_equal(fused, two)
     h_ref = bindings.fused_oracle(X, W1, [("add", b1), ("relu",)], threads=host_threads)
     hw_ref = bindings.fused_oracle(h_ref, W2p, [], threads=host_threads)
     want = bindings.fused_oracle(h_ref, W2, [("add", b2), ("relu",), ("add", hw_ref)], threads=host_threads)
-    check(fused, want, TF32, f"product fusion M={M}", depth=2)
+    check(fused, want, precision, f"product fusion M={M} H={H}", depth=2)
 
 
 @pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
