@@ -396,9 +396,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (p.num_kb <= kShortKb) prefetch_full_operands(row, col0, min(BN, p.N - col0), p);
             }
             if (SEG) {
-                // Sum the K segments in registers (fp32, round to nearest).
+                // Sum the K segments in registers (fp32, round to nearest), 16
+                // columns at a time.  After the last segment the totals go back
+                // into that accumulator and the epilogue reads them from there,
+                // with the registers free.
                 float total[BN];
                 for (int k_begin = 0; k_begin < p.num_kb; k_begin += p.seg_kb) {
+                    const bool first = k_begin == 0;
+                    const bool last = k_begin + p.seg_kb >= p.num_kb;
                     const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
                     const bool got = !stop && mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns);
                     if (!__all_sync(0xffffffffu, got)) {
@@ -409,15 +414,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * BN);
 #pragma unroll
-                    for (int c = 0; c < BN / 32; ++c) {
-                        if (c < chunks) {
+                    for (int g = 0; g < BN / 16; ++g) {
+                        uint32_t r[16];
+                        tmem_ld_32x32b_x16(taddr + 16 * g, r);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            total[16 * g + i] = first ? __uint_as_float(r[i]) : total[16 * g + i] + __uint_as_float(r[i]);
+                        if (last) {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(total[16 * g + i]);
+                            tmem_st_32x32b_x16(taddr + 16 * g, r);
+                        }
+                    }
+                    if (last) {
+                        tmem_st_wait();
+                        for (int c = 0; c < chunks; ++c) {
                             uint32_t r[32];
                             tmem_ld_32x32b_x32(taddr + 32 * c, r);
                             tmem_ld_wait();
+                            float v[32];
 #pragma unroll
-                            for (int i = 0; i < 32; ++i)
-                                total[32 * c + i] = k_begin == 0 ? __uint_as_float(r[i])
-                                                                 : total[32 * c + i] + __uint_as_float(r[i]);
+                            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                            const int col = col0 + 32 * c;
+                            apply_epilogue(v, row, col, row_ok, p);
+                            if (row_ok) store_row_chunk(v, row, col, p);
                         }
                     }
                     tc_fence_before();
@@ -426,17 +447,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (acc == 0) acc_phase ^= 1u;
                 }
                 if (failed) break;
-#pragma unroll
-                for (int c = 0; c < BN / 32; ++c) {
-                    if (c < chunks) {
-                        float v[32];
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] = total[32 * c + i];
-                        const int col = col0 + 32 * c;
-                        apply_epilogue(v, row, col, row_ok, p);
-                        if (row_ok) store_row_chunk(v, row, col, p);
-                    }
-                }
             } else {
                 const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
                 const bool got = !stop && mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns);
