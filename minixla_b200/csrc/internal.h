@@ -44,6 +44,7 @@ struct GemmLaunch {
 // column blocks x K ranges; workspace holds splits * M * N floats.
 constexpr int kSkinnyMaxRows = 16;
 struct SkinnyPlan {
+    bool one_kernel = false;  // cluster kernel: no workspace (splits == 0)
     int col_blocks = 1;
     int splits = 1;
     int k_per_split = 1;

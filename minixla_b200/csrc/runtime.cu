@@ -552,9 +552,11 @@ static int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* 
     if (M <= kSkinnyMaxRows) {
         // Few rows: HBM-bound on B, CUDA-core fp32 split over columns and K.
         const SkinnyPlan pl = plan_skinny(M, N, K, ctx->num_sms);
-        float* ws = static_cast<float*>(
-            ctx->pool->alloc(static_cast<size_t>(pl.splits) * M * N * sizeof(float), stream));
-        if (!ws) return MXB_E_NOMEM;
+        float* ws = nullptr;  // the one-kernel form needs no workspace
+        if (!pl.one_kernel) {
+            ws = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(pl.splits) * M * N * sizeof(float), stream));
+            if (!ws) return MXB_E_NOMEM;
+        }
         const int rc = cuda_ok(launch_skinny_gemm(A, lda, B, ldb, out, ldo, M, N, K, row_base, steps, n_steps, ws, pl,
                                                   ctx->num_sms, stream),
                                "skinny GEMM launch")

@@ -15,11 +15,24 @@
 //      split plan), then the node's epilogue steps are applied in order and
 //      each output is stored once.
 // fp32 multiply-adds: at least as accurate as either precision mode.
+//
+// One-kernel form (whenever A's rows of a K slice fit in shared memory): a
+// cluster of kSplits CTAs shares one 128-column block and splits K between
+// its CTAs, and each CTA's eight warps split its slice again.  Each warp
+// keeps M x 4 sums per thread; the CTA adds its warps' sums in warp order in
+// shared memory, then CTA r of the cluster adds the kSplits CTAs' sums for
+// columns 16r .. 16r+15 through distributed shared memory in rank order,
+// applies the epilogue and stores.  No workspace, no second launch, and the
+// summation order is fixed.
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
 
 #include "internal.h"
+#include "sm100_ptx.cuh"
 
 namespace mxb {
 
@@ -148,6 +161,152 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
+constexpr int kSplits = 8;           // CTAs of a cluster, one K slice each
+constexpr int kClusterCols = 128;    // output columns of a cluster (32 lanes x float4)
+constexpr int kMaxSliceFloats = 16 * 1024;  // A's rows of one K slice staged in shared memory
+
+// Epilogue of one output element (row m, column n), eval_fused's step order.
+__device__ __forceinline__ float skinny_epilogue(float v, int m, int n, int N, long long row_base,
+                                                 const SkinnyEpilogue& epi) {
+    for (int i = 0; i < epi.n_steps; ++i) {
+        const EpStepDev& st = epi.steps[i];
+        if (st.kind == MXB_EP_ADD_FULL) {
+            v += st.ptr[static_cast<long long>(m) * st.ld_or_size + n];
+        } else if (st.kind == MXB_EP_ADD_ROW) {
+            v += st.ptr[n];
+        } else if (st.kind == MXB_EP_ADD_MOD) {
+            const unsigned long long flat =
+                static_cast<unsigned long long>(m + row_base) * static_cast<unsigned long long>(N) + n;
+            v += st.ptr[flat % static_cast<unsigned long long>(st.ld_or_size)];
+        } else if (st.kind == MXB_EP_RELU) {
+            v = v > 0.0f ? v : 0.0f;
+        } else if (st.kind == MXB_EP_SCALE) {
+            v = v * st.scale;
+        }
+    }
+    return v;
+}
+
+template <int MR>
+__global__ void __cluster_dims__(1, kSplits, 1) __launch_bounds__(kThreads, 2)
+    skinny_cluster_kernel(const float* __restrict__ A, long long lda, const float* __restrict__ B, long long ldb,
+                          float* __restrict__ out, long long ldo, int M, int N, int K, long long row_base,
+                          const __grid_constant__ SkinnyEpilogue epi) {
+    extern __shared__ float sm[];
+    const int slice = (K + kSplits - 1) / kSplits;  // rows of K per CTA
+    const int k0 = blockIdx.y * slice;
+    const int k1 = min(K, k0 + slice);
+    const int kl = max(0, k1 - k0);
+    float* sA = sm;                                 // [M][slice]
+    float* part = sm + M * slice;                   // [8 warps][M][128]
+    for (int i = threadIdx.x; i < M * kl; i += kThreads) {
+        const int m = i / kl, kk = i - m * kl;
+        sA[m * slice + kk] = A[static_cast<long long>(m) * lda + k0 + kk];
+    }
+    __syncthreads();
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int col = blockIdx.x * kClusterCols + lane * 4;
+    const int per_warp = (kl + 7) / 8;
+    const int w0 = min(kl, warp * per_warp), w1 = min(kl, w0 + per_warp);
+    float acc[MR][4];
+#pragma unroll
+    for (int m = 0; m < MR; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.0f;
+    auto fma_row = [&](const float4& b, int k) {
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+            if (m < M) {
+                const float a = sA[m * slice + k];
+                acc[m][0] = fmaf(a, b.x, acc[m][0]);
+                acc[m][1] = fmaf(a, b.y, acc[m][1]);
+                acc[m][2] = fmaf(a, b.z, acc[m][2]);
+                acc[m][3] = fmaf(a, b.w, acc[m][3]);
+            }
+        }
+    };
+    if (col < N) {
+        const float* bp = B + static_cast<long long>(k0 + w0) * ldb + col;
+        int k = w0;
+        if (col + 3 < N && (ldb & 3) == 0 && (reinterpret_cast<uintptr_t>(B) & 15) == 0) {
+            // kBatch independent row loads in flight (16 while the sums need
+            // few registers), then their FMAs in k order.
+            constexpr int kBatch = MR <= 8 ? 16 : 8;
+            for (; k + kBatch <= w1; k += kBatch) {
+                float4 b[kBatch];
+#pragma unroll
+                for (int u = 0; u < kBatch; ++u)
+                    b[u] = __ldcs(reinterpret_cast<const float4*>(bp + static_cast<long long>(u) * ldb));
+                bp += kBatch * ldb;
+#pragma unroll
+                for (int u = 0; u < kBatch; ++u) fma_row(b[u], k + u);
+            }
+            for (; k < w1; ++k, bp += ldb) fma_row(__ldcs(reinterpret_cast<const float4*>(bp)), k);
+        } else {
+            for (; k < w1; ++k, bp += ldb) {
+                float4 b;
+                b.x = bp[0];
+                b.y = col + 1 < N ? bp[1] : 0.0f;
+                b.z = col + 2 < N ? bp[2] : 0.0f;
+                b.w = col + 3 < N ? bp[3] : 0.0f;
+                fma_row(b, k);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+        if (m >= M) break;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) part[(warp * M + m) * kClusterCols + lane * 4 + c] = acc[m][c];
+    }
+    __syncthreads();
+    // This CTA's sums: warps added in order, into warp 0's rows.
+    for (int e = threadIdx.x; e < M * kClusterCols; e += kThreads) {
+        float v = part[e];
+        for (int w = 1; w < 8; ++w) v += part[w * M * kClusterCols + e];
+        part[e] = v;
+    }
+    cluster_sync();  // every CTA's sums are visible to the cluster
+    // CTA r: columns 16r .. 16r+15 of the block, summed over the cluster's CTAs in rank order.
+    const uint32_t rank = static_cast<uint32_t>(blockIdx.y % kSplits);
+    constexpr int kColsPerRank = kClusterCols / kSplits;
+    for (int e = threadIdx.x; e < M * kColsPerRank; e += kThreads) {
+        const int m = e / kColsPerRank;
+        const int j = static_cast<int>(rank) * kColsPerRank + (e - m * kColsPerRank);
+        const uint32_t addr = static_cast<uint32_t>(__cvta_generic_to_shared(&part[m * kClusterCols + j]));
+        float v = 0.0f;
+#pragma unroll
+        for (int q = 0; q < kSplits; ++q) v += ld_shared_cluster_f32(mapa_shared(addr, static_cast<uint32_t>(q)));
+        const int n = blockIdx.x * kClusterCols + j;
+        if (n < N) out[static_cast<long long>(m) * ldo + n] = skinny_epilogue(v, m, n, N, row_base, epi);
+    }
+    cluster_sync();  // no CTA leaves while the others may still read its shared memory
+}
+
+template <int MR>
+cudaError_t launch_cluster(const float* A, long long lda, const float* B, long long ldb, float* out, long long ldo,
+                           int M, int N, int K, long long row_base, const SkinnyEpilogue& epi, cudaStream_t stream) {
+    auto kernel = skinny_cluster_kernel<MR>;
+    const int slice = (K + kSplits - 1) / kSplits;
+    const size_t smem = (static_cast<size_t>(M) * slice + 8ull * M * kClusterCols) * sizeof(float);
+    static std::mutex mu;
+    static uint64_t configured = 0;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (dev >= 64 || !(configured & (1ull << dev))) {
+            e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>((kMaxSliceFloats + 8 * 16 * kClusterCols) * sizeof(float)));
+            if (e != cudaSuccess) return e;
+            if (dev < 64) configured |= 1ull << dev;
+        }
+    }
+    const dim3 grid((N + kClusterCols - 1) / kClusterCols, kSplits);
+    kernel<<<grid, kThreads, smem, stream>>>(A, lda, B, ldb, out, ldo, M, N, K, row_base, epi);
+    return cudaGetLastError();
+}
+
 template <int MR>
 cudaError_t launch_partial(const SkinnyPlan& pl, const float* A, long long lda, const float* B, long long ldb,
                            float* partial, int M, int N, int K, cudaStream_t stream) {
@@ -161,6 +320,17 @@ cudaError_t launch_partial(const SkinnyPlan& pl, const float* A, long long lda, 
 
 SkinnyPlan plan_skinny(int M, int N, int K, int num_sms) {
     SkinnyPlan p;
+    // One kernel whenever a K slice of A's rows fits in shared memory (no
+    // workspace then).  Measured against the two-kernel form: (1, 4096,
+    // 4096) 12.3 vs 19.2 us, (16, 4096, 4096) 29.6 vs 35.7, (1, 1000, 780)
+    // 8.1 vs 13.2.  MINIXLA_SKINNY_FORM=split forces the two kernels.
+    const long long slice = (K + kSplits - 1) / kSplits;
+    const char* force = getenv("MINIXLA_SKINNY_FORM");
+    if (static_cast<long long>(M) * slice <= kMaxSliceFloats && !(force && !strcmp(force, "split"))) {
+        p.one_kernel = true;
+        p.splits = 0;
+        return p;
+    }
     p.col_blocks = (N + kColsPerCta - 1) / kColsPerCta;
     // About four CTAs per SM, each streaming at least 32 rows of B.
     int splits = (4 * num_sms + p.col_blocks - 1) / p.col_blocks;
@@ -178,6 +348,18 @@ cudaError_t launch_skinny_gemm(const float* A, long long lda, const float* B, lo
                                float* workspace, const SkinnyPlan& pl, int num_sms, cudaStream_t stream) {
     if (M < 1 || M > kSkinnyMaxRows) return cudaErrorInvalidValue;
     cudaError_t e;
+    if (pl.one_kernel) {
+        SkinnyEpilogue epi{};
+        epi.n_steps = n_steps;
+        for (int i = 0; i < n_steps; ++i) epi.steps[i] = steps[i];
+        if (M == 1) e = launch_cluster<1>(A, lda, B, ldb, out, ldo, M, N, K, row_base, epi, stream);
+        else if (M == 2) e = launch_cluster<2>(A, lda, B, ldb, out, ldo, M, N, K, row_base, epi, stream);
+        else if (M <= 4) e = launch_cluster<4>(A, lda, B, ldb, out, ldo, M, N, K, row_base, epi, stream);
+        else if (M <= 8) e = launch_cluster<8>(A, lda, B, ldb, out, ldo, M, N, K, row_base, epi, stream);
+        else e = launch_cluster<16>(A, lda, B, ldb, out, ldo, M, N, K, row_base, epi, stream);
+        note_launch();
+        return e;
+    }
     if (M == 1) e = launch_partial<1>(pl, A, lda, B, ldb, workspace, M, N, K, stream);
     else if (M == 2) e = launch_partial<2>(pl, A, lda, B, ldb, workspace, M, N, K, stream);
     else if (M <= 4) e = launch_partial<4>(pl, A, lda, B, ldb, workspace, M, N, K, stream);

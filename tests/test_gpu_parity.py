@@ -404,10 +404,17 @@ def test_row_streamed_executor_matches_one_stream(lib, gpu_ctx, precision, monke
 
 @pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
 @pytest.mark.parametrize("M", [1, 3, 8, 16])
-def test_skinny_rows_path(lib, gpu_ctx, M, precision, host_threads):
+@pytest.mark.parametrize("form,NK", [("cluster", (1000, 777)), ("split", (1000, 777)), ("cluster", (2501, 1500)),
+                                     (None, (300, 20000))], ids=["cluster", "split", "cluster_wide", "long_k"])
+def test_skinny_rows_path(lib, gpu_ctx, M, form, NK, precision, monkeypatch, host_threads):
     """Few output rows run on the split-K CUDA-core path (fp32): every
-    epilogue kind, ragged N, against the oracle at the 3xTF32 tolerance."""
-    N, K = 1000, 777
+    epilogue kind, ragged N, against the oracle at the 3xTF32 tolerance.
+    Both forms -- one kernel reducing over a cluster's shared memory, and
+    partial sums + reduce kernel (MINIXLA_SKINNY_FORM=split) -- and K = 20000,
+    whose slices of A do not fit in shared memory (two kernels by itself)."""
+    if form:
+        monkeypatch.setenv("MINIXLA_SKINNY_FORM", form)
+    N, K = NK
     A, B, C = _relu_abc(M, N, K, c_normal=True)
     bias = datagen.normal((N,), 8, 0.0, 0.5)
     odd = datagen.uniform((13,), 9)
