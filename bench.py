@@ -56,6 +56,9 @@ def parse():
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     p.add_argument("--sweep", action="store_true",
                    help="time every BASELINE shape (kernel only, operands resident); one JSON line per shape")
+    p.add_argument("--kernels", action="store_true",
+                   help="HBM-bound kernels alone (standalone add / relu, skinny GEMM) on operands larger than L2: "
+                        "GB/s against the measured copy rate; one JSON line per kernel")
     p.add_argument("--shape", type=int, default=0,
                    help="per-GPU M = N = K override (profiling on a smaller case); 0 = 8192")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -242,6 +245,15 @@ def reference_arm(args, rank, world):
 
 
 # ------------------------------------------------------------------ our arm
+
+
+def measured_hbm_gbs():
+    f = ROOT / "MEASURED_PEAKS.json"
+    try:
+        v = float(json.loads(f.read_text())["hbm_gbs"])
+        return v, f"measured copy {v:.1f} GB/s (MEASURED_PEAKS.json)"
+    except Exception:
+        return 6650.0, "fallback copy 6650 GB/s"
 
 
 def measured_tf32_peak():
@@ -732,11 +744,101 @@ def run_sweep(args):
     return 0
 
 
+def run_kernels(args):
+    """The library's HBM-bound kernels alone, operands larger than L2 (126 MB)
+    and resident: standalone add (same shape: 12 B per element; [N] row
+    broadcast: 8 B), relu (8 B), and the skinny GEMM, whose traffic is B
+    (4*K*N bytes).  Each launch behind a ~50 us spin on the stream so the
+    events bracket the kernel; min and median of 20.  Reported against the
+    measured HBM copy rate."""
+    import torch
+
+    from minixla_b200 import lib as mlib
+
+    lib = mlib.load()
+    ctx = lib.gpu_ctx_create_on(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.Stream(dev)
+    peak, peak_src = measured_hbm_gbs()
+
+    def time_launches(fn, reps=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                torch.cuda._sleep(100_000)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return min(ts), statistics.median(ts)
+
+    def report(name, nbytes, fn, extra=None):
+        tmin, tmed = time_launches(fn)
+        gbs = nbytes / (tmin * 1e-3) / 1e9
+        line = {"kernel": name, "bytes": int(nbytes), "ms_min": tmin, "ms_median": tmed, "gbs": gbs,
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                             "peak_source": peak_src}}
+        line.update(extra or {})
+        print(json.dumps(line), flush=True)
+
+    n = 64 << 20  # 64 Mi floats = 256 MiB per operand
+    g = torch.Generator(device=dev).manual_seed(0)
+    a = torch.rand(n, device=dev, generator=g) - 0.5
+    b = torch.rand(n, device=dev, generator=g) - 0.5
+    out = torch.empty(n, device=dev)
+    row = torch.rand(8192, device=dev, generator=g)
+
+    def add_same():
+        assert lib.mxb_add(ctx, a.data_ptr(), n, b.data_ptr(), n, out.data_ptr(), stream.cuda_stream) == 0
+
+    def add_row():
+        assert lib.mxb_add(ctx, a.data_ptr(), n, row.data_ptr(), row.numel(), out.data_ptr(), stream.cuda_stream) == 0
+
+    def relu():
+        assert lib.mxb_relu(ctx, a.data_ptr(), n, out.data_ptr(), stream.cuda_stream) == 0
+
+    report("add (same shape)", 12.0 * n, add_same, {"elements": n})
+    torch.testing.assert_close(out, a + b)
+    report("add ([8192] row broadcast)", 8.0 * n, add_row, {"elements": n})
+    torch.testing.assert_close(out, a + row.repeat(n // 8192))
+    report("relu", 8.0 * n, relu, {"elements": n})
+    torch.testing.assert_close(out, torch.relu(a))
+    del a, b, out
+
+    # Skinny fused GEMM relu(x.B + c), M rows: the work is streaming B.
+    K = N = 8192
+    B = torch.rand(K, N, device=dev, generator=g) - 0.5
+    for M in (1, 4, 16):
+        x = torch.rand(M, K, device=dev, generator=g) - 0.5
+        c = torch.rand(M, N, device=dev, generator=g) - 0.5
+        y = torch.empty(M, N, device=dev)
+        steps = (mlib.EpStepDev * 2)()
+        steps[0] = mlib.EpStepDev(mlib.MXB_EP_ADD_FULL, 0, c.data_ptr(), N, 0.0, 0)
+        steps[1] = mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0)
+
+        def skinny():
+            assert lib.mxb_fused_gemm(ctx, x.data_ptr(), K, B.data_ptr(), N, y.data_ptr(), N, M, N, K, steps, 2,
+                                      mlib.GPU_PRECISION_TF32, stream.cuda_stream) == 0
+
+        report(f"skinny fused GEMM M={M}", 4.0 * (K * N + M * K + 2 * M * N), skinny, {"M": M, "N": N, "K": K})
+        ref = torch.relu(x.double() @ B.double() + c.double())
+        assert float((y.double() - ref).norm() / ref.norm()) < 1e-5
+    lib.gpu_ctx_destroy(ctx)
+    return 0
+
+
 def main():
     args = parse()
     rank, local_rank, world = env_rank()
     if args.sweep:
         return run_sweep(args)
+    if args.kernels:
+        return run_kernels(args)
     if args.impl == "reference":
         return reference_arm(args, rank, world)
     return ours_arm(args, rank, local_rank, world)

@@ -197,8 +197,8 @@ __global__ void __cluster_dims__(1, kSplits, 1) __launch_bounds__(kThreads, 2)
     const int k0 = blockIdx.y * slice;
     const int k1 = min(K, k0 + slice);
     const int kl = max(0, k1 - k0);
-    float* sA = sm;                                 // [M][slice]
-    float* part = sm + M * slice;                   // [8 warps][M][128]
+    float* sA = sm;                                 // [M][slice] during the k-loop,
+    float* part = sm;                               // then [8 warps][M][128] in the same bytes
     for (int i = threadIdx.x; i < M * kl; i += kThreads) {
         const int m = i / kl, kk = i - m * kl;
         sA[m * slice + kk] = A[static_cast<long long>(m) * lda + k0 + kk];
@@ -252,6 +252,7 @@ __global__ void __cluster_dims__(1, kSplits, 1) __launch_bounds__(kThreads, 2)
             }
         }
     }
+    __syncthreads();  // every warp is done with sA before its bytes hold the sums
 #pragma unroll
     for (int m = 0; m < MR; ++m) {
         if (m >= M) break;
@@ -287,7 +288,7 @@ cudaError_t launch_cluster(const float* A, long long lda, const float* B, long l
                            int M, int N, int K, long long row_base, const SkinnyEpilogue& epi, cudaStream_t stream) {
     auto kernel = skinny_cluster_kernel<MR>;
     const int slice = (K + kSplits - 1) / kSplits;
-    const size_t smem = (static_cast<size_t>(M) * slice + 8ull * M * kClusterCols) * sizeof(float);
+    const size_t smem = std::max<size_t>(static_cast<size_t>(M) * slice, 8ull * M * kClusterCols) * sizeof(float);
     static std::mutex mu;
     static uint64_t configured = 0;
     int dev = 0;
@@ -297,7 +298,7 @@ cudaError_t launch_cluster(const float* A, long long lda, const float* B, long l
         std::lock_guard<std::mutex> lock(mu);
         if (dev >= 64 || !(configured & (1ull << dev))) {
             e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>((kMaxSliceFloats + 8 * 16 * kClusterCols) * sizeof(float)));
+                                     static_cast<int>(std::max(kMaxSliceFloats, 8 * 16 * kClusterCols) * sizeof(float)));
             if (e != cudaSuccess) return e;
             if (dev < 64) configured |= 1ull << dev;
         }
