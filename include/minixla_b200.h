@@ -12,7 +12,10 @@
  * failures return NULL or -1.0 and print one line to stderr; nothing aborts;
  * every device buffer is released on every path; calls are synchronous
  * (the result is on the host when the call returns); a GpuCtx is used from
- * one host thread.
+ * one host thread at a time for graph execution (gpu_execute and friends).
+ * The device-pointer launches (mxb_fused_gemm, mxb_fused_gemm2, mxb_add,
+ * mxb_relu) only touch the context's pool, which is locked, and may come
+ * from several threads.
  */
 #ifndef MINIXLA_B200_H
 #define MINIXLA_B200_H

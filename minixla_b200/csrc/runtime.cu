@@ -78,7 +78,9 @@ static bool cuda_ok(cudaError_t e, const char* what) {
 // stream wait on the event, so reuse is always stream-ordered.  A failed
 // cudaMalloc first returns every cached block to the driver and retries.
 // MINIXLA_FAIL_ALLOC_AT=n makes the n-th pool allocation of the process fail
-// (host-side fault injection for the out-of-memory path).
+// (host-side fault injection for the out-of-memory path).  A mutex guards the
+// lists, so host threads may share a context's pool (the reference API
+// itself is single-threaded; the device-pointer entry points need not be).
 
 static std::atomic<long long> g_alloc_calls{0};
 
@@ -86,12 +88,13 @@ class DevicePool {
   public:
     explicit DevicePool(int device) : device_(device) {}
     ~DevicePool() {
-        trim();
+        trim_locked();
         for (auto& kv : live_) cudaFree(kv.first);
         for (cudaEvent_t e : spare_events_) cudaEventDestroy(e);
     }
 
     void* alloc(size_t bytes, cudaStream_t stream) {
+        std::lock_guard<std::mutex> lock(mu_);
         const long long call = g_alloc_calls.fetch_add(1) + 1;
         if (const char* fail = getenv("MINIXLA_FAIL_ALLOC_AT")) {
             if (atoll(fail) == call) {
@@ -113,7 +116,7 @@ class DevicePool {
         void* p = nullptr;
         if (cudaMalloc(&p, cls) != cudaSuccess) {
             cudaGetLastError();
-            trim();
+            trim_locked();
             if (cudaMalloc(&p, cls) != cudaSuccess) {
                 cudaGetLastError();
                 set_error("device allocation of %zu bytes failed", cls);
@@ -126,6 +129,7 @@ class DevicePool {
 
     void release(void* p, cudaStream_t stream) {
         if (!p) return;
+        std::lock_guard<std::mutex> lock(mu_);
         auto it = live_.find(p);
         if (it == live_.end()) return;
         const size_t cls = it->second;
@@ -140,6 +144,23 @@ class DevicePool {
     }
 
     void trim() {
+        std::lock_guard<std::mutex> lock(mu_);
+        trim_locked();
+    }
+
+    size_t live_bytes() {
+        std::lock_guard<std::mutex> lock(mu_);
+        size_t s = 0;
+        for (auto& kv : live_) s += kv.second;
+        return s;
+    }
+    size_t cached_bytes() {
+        std::lock_guard<std::mutex> lock(mu_);
+        return cached_bytes_;
+    }
+
+  private:
+    void trim_locked() {
         for (auto& kv : free_) {
             for (Cached& c : kv.second) {
                 if (c.ready) {
@@ -153,14 +174,6 @@ class DevicePool {
         cached_bytes_ = 0;
     }
 
-    size_t live_bytes() const {
-        size_t s = 0;
-        for (auto& kv : live_) s += kv.second;
-        return s;
-    }
-    size_t cached_bytes() const { return cached_bytes_; }
-
-  private:
     struct Cached {
         void* ptr;
         cudaStream_t stream;
@@ -189,6 +202,7 @@ class DevicePool {
     }
 
     int device_;
+    std::mutex mu_;
     std::unordered_map<size_t, std::vector<Cached>> free_;
     std::unordered_map<void*, size_t> live_;
     std::vector<cudaEvent_t> spare_events_;

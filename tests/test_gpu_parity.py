@@ -616,6 +616,49 @@ def test_device_pointer_api_matches_torch(lib, gpu_ctx):
     assert rel_frobenius(out.cpu().numpy(), ref.cpu().numpy()) < 1e-5
 
 
+def test_device_api_from_several_threads(lib, gpu_ctx):
+    """The device-pointer launches may share one context across host threads
+    (its pool is locked): four threads, each on its own stream, run the
+    3xTF32 GEMM (which takes pooled workspace) and get the single-threaded
+    results bit for bit."""
+    import threading
+
+    import torch
+
+    M, N, K = 512, 384, 256
+    g = torch.Generator(device="cuda").manual_seed(3)
+    A = torch.rand(M, K, device="cuda", generator=g) - 0.5
+    B = torch.rand(K, N, device="cuda", generator=g) - 0.5
+    steps = (mlib.EpStepDev * 1)()
+    steps[0] = mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0)
+    want = torch.empty(M, N, device="cuda")
+    assert lib.mxb_fused_gemm(gpu_ctx, A.data_ptr(), K, B.data_ptr(), N, want.data_ptr(), N, M, N, K, steps, 1, X3,
+                              None) == 0
+    assert lib.mxb_check_device_error(gpu_ctx) == 0
+    outs = [torch.empty(M, N, device="cuda") for _ in range(4)]
+    streams = [torch.cuda.Stream() for _ in range(4)]
+    errors = []
+
+    def work(i):
+        for _ in range(20):
+            rc = lib.mxb_fused_gemm(gpu_ctx, A.data_ptr(), K, B.data_ptr(), N, outs[i].data_ptr(), N, M, N, K, steps,
+                                    1, X3, streams[i].cuda_stream)
+            if rc != 0:
+                errors.append(mlib.last_error())
+                return
+
+    threads = [threading.Thread(target=work, args=(i,)) for i in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    torch.cuda.synchronize()
+    assert not errors, errors
+    assert lib.mxb_check_device_error(gpu_ctx) == 0
+    for o in outs:
+        assert torch.equal(o, want)
+
+
 def test_standalone_elementwise_device_api(lib, gpu_ctx):
     import torch
 
