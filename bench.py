@@ -59,6 +59,9 @@ def parse():
     p.add_argument("--kernels", action="store_true",
                    help="HBM-bound kernels alone (standalone add / relu, skinny GEMM) on operands larger than L2: "
                         "GB/s against the measured copy rate; one JSON line per kernel")
+    p.add_argument("--mlp", action="store_true",
+                   help="config 4 end to end: the 3-layer MLP built with the reference's g_* API and optimize(), "
+                        "run through gpu_execute_into, weights uploaded or kept resident; one JSON line per run")
     p.add_argument("--shape", type=int, default=0,
                    help="per-GPU M = N = K override (profiling on a smaller case); 0 = 8192")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -499,9 +502,37 @@ def ours_arm(args, rank, local_rank, world):
                 raise RuntimeError(mlib.last_error())
         r_ms = max_over_ranks((time.perf_counter() - e0) * 1e3 / args.e2e_steps)
         lib.gpu_ctx_release_resident(ctx, None)
+
+        # The same call with pageable host buffers (numpy arrays, as MiniXLA's
+        # malloc'd tensors are): through the context's pinned staging slots,
+        # and with staging off (the driver's own pageable copy path).
+        hp = HostGraph()
+        out_p = np.empty((M, N), dtype=np.float32)
+        root_p = hp.fused_node(hp.input_node(A), hp.input_node(B), [(OP_ADD, hp.input_node(Cm)), (OP_RELU, None)])
+        out_pt = hp.tensor(out_p)
+        pageable = {}
+        for label, staged in (("staged", "1"), ("driver_copy", "0")):
+            os.environ["MINIXLA_STAGED_COPY"] = staged
+            for _ in range(2):
+                if lib.gpu_execute_into(root_p, ctx, out_pt) != 0:
+                    raise RuntimeError(mlib.last_error())
+            barrier()
+            e0 = time.perf_counter()
+            for _ in range(args.e2e_steps):
+                if lib.gpu_execute_into(root_p, ctx, out_pt) != 0:
+                    raise RuntimeError(mlib.last_error())
+            p_ms = max_over_ranks((time.perf_counter() - e0) * 1e3 / args.e2e_steps)
+            pageable[label] = {"value": flops_job / (p_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": p_ms}
+        os.environ.pop("MINIXLA_STAGED_COPY", None)
+        if not np.array_equal(out_p, O_h.numpy()):
+            raise RuntimeError("pageable e2e result differs from the pinned one")
+        pageable["note"] = ("pageable host buffers (as create_tensor's malloc'd data): 'staged' copies through the "
+                            "context's pinned slots filled by several host threads; 'driver_copy' is the CUDA "
+                            "driver's own pageable path (MINIXLA_STAGED_COPY=0)")
         e2e["b_resident"] = {"value": flops_job / (r_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": r_ms,
                              "h2d_bytes_per_step": 4 * (M * K + M * N), "d2h_bytes_per_step": 4 * M * N,
                              "note": "B kept resident with gpu_ctx_keep_resident; not the headline e2e"}
+        e2e["pageable"] = pageable
 
     peak, peak_src = measured_tf32_peak()
     if prec == mlib.GPU_PRECISION_3XTF32:
@@ -832,6 +863,95 @@ def run_kernels(args):
     return 0
 
 
+def run_mlp(args):
+    """Config 4 through the reference-facing path: the 3-layer MLP (X 4096 x
+    1024; W1 1024 x 4096, W2 and W2' 4096 x 4096, W3 4096 x 1024; bias rows)
+    built with MiniXLA's own g_matmul / g_add / g_relu and optimize()
+    (oracle/_ref), then handed to gpu_execute_into.  Each step is one
+    synchronous call, host X in and host output out, timed on the host clock
+    (the call returns with the result on the host).  Runs: weights uploaded
+    every call (the reference's behaviour, gpu_exec.c:450-456) and kept
+    resident (gpu_ctx_keep_resident); the row-streamed and the one-stream
+    executors; both precision modes.  A few output rows are checked against
+    the oracle."""
+    import numpy as np
+    import torch
+
+    from minixla_b200 import datagen
+    from minixla_b200 import lib as mlib
+    from minixla_b200.abi import HostGraph
+    from oracle.bindings import RefGraph, fused_oracle, ref_available
+
+    if not ref_available():
+        print(json.dumps({"workload": "config 4 MLP", "unavailable": "oracle/_ref not built"}))
+        return 0
+    lib = mlib.load()
+    ctx = lib.gpu_ctx_create_on(0)
+    Mx, D, H = 4096, 1024, 4096
+    host = {
+        "X": datagen.uniform((Mx, D), 70),
+        "W1": datagen.normal((D, H), 71, 0.0, 1.0 / np.sqrt(D)),
+        "W2": datagen.normal((H, H), 72, 0.0, 1.0 / np.sqrt(H)),
+        "W2p": datagen.normal((H, H), 73, 0.0, 1.0 / np.sqrt(H)),
+        "W3": datagen.normal((H, D), 74, 0.0, 1.0 / np.sqrt(H)),
+        "b1": datagen.normal((H,), 75, 0.0, 0.1),
+        "b2": datagen.normal((H,), 76, 0.0, 0.1),
+        "b3": datagen.normal((D,), 77, 0.0, 0.1),
+    }
+    rg = RefGraph()
+    L = rg.lib
+    nodes = {k: rg.input(v) for k, v in host.items()}
+    hn = L.g_relu(L.g_add(L.g_matmul(nodes["X"], nodes["W1"]), nodes["b1"]))
+    yn = L.g_add(L.g_relu(L.g_add(L.g_matmul(hn, nodes["W2"]), nodes["b2"])), L.g_matmul(hn, nodes["W2p"]))
+    root = rg.own(rg.optimize(L.g_add(L.g_matmul(yn, nodes["W3"]), nodes["b3"])))
+    n_nodes = rg.node_count(root)
+    out_h = torch.empty((Mx, D), dtype=torch.float32).pin_memory()
+    hg = HostGraph()
+    out_t = hg.tensor(out_h)
+    flops = 2.0 * Mx * (D * H + 2 * H * H + H * D)
+
+    rows = [0, 2047, 4095]
+    X = host["X"][rows]
+    h_ref = fused_oracle(X, host["W1"], [("add", host["b1"]), ("relu",)])
+    hw_ref = fused_oracle(h_ref, host["W2p"], [])
+    y_ref = fused_oracle(h_ref, host["W2"], [("add", host["b2"]), ("relu",), ("add", hw_ref)])
+    want = fused_oracle(y_ref, host["W3"], [("add", host["b3"])])
+
+    weights = ["W1", "W2", "W2p", "W3", "b1", "b2", "b3"]
+    for prec_name, prec in (("tf32", mlib.GPU_PRECISION_TF32), ("3xtf32", mlib.GPU_PRECISION_3XTF32)):
+        lib.gpu_ctx_set_precision(ctx, prec)
+        for resident in (False, True):
+            if resident:
+                for k in weights:
+                    assert lib.gpu_ctx_keep_resident(ctx, nodes[k].contents.output) == 0, mlib.last_error()
+            for chunks in ("8", "1"):
+                os.environ["MINIXLA_STREAM_CHUNKS"] = chunks
+                for _ in range(2):
+                    assert lib.gpu_execute_into(root, ctx, out_t) == 0, mlib.last_error()
+                ts = []
+                for _ in range(10):
+                    t0 = time.perf_counter()
+                    assert lib.gpu_execute_into(root, ctx, out_t) == 0, mlib.last_error()
+                    ts.append(time.perf_counter() - t0)
+                got = out_h.numpy()[rows]
+                rel = float(np.linalg.norm(got - want) / np.linalg.norm(want))
+                tol = 3 * (2e-3 if prec == mlib.GPU_PRECISION_TF32 else 1e-5)
+                assert rel <= tol, f"config 4 check failed: {rel:.3g} > {tol}"
+                ms = min(ts) * 1e3
+                h2d = 4 * Mx * D + (0 if resident else 4 * sum(host[k].size for k in weights))
+                print(json.dumps({
+                    "workload": "config 4 MLP via optimize() + gpu_execute_into", "precision": prec_name,
+                    "nodes_after_optimize": n_nodes, "weights": "resident" if resident else "uploaded each call",
+                    "executor": "row-streamed (8 chunks)" if chunks == "8" else "one-stream (multi-stream DAG)",
+                    "ms_min": ms, "ms_median": statistics.median(ts) * 1e3, "tflops": flops / (ms * 1e-3) / 1e12,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4 * Mx * D, "rel_err_rows": rel}), flush=True)
+        lib.gpu_ctx_release_resident(ctx, None)
+    os.environ.pop("MINIXLA_STREAM_CHUNKS", None)
+    rg.close()
+    lib.gpu_ctx_destroy(ctx)
+    return 0
+
+
 def main():
     args = parse()
     rank, local_rank, world = env_rank()
@@ -839,6 +959,8 @@ def main():
         return run_sweep(args)
     if args.kernels:
         return run_kernels(args)
+    if args.mlp:
+        return run_mlp(args)
     if args.impl == "reference":
         return reference_arm(args, rank, world)
     return ours_arm(args, rank, local_rank, world)

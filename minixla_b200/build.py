@@ -17,7 +17,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "_lib"
 LIB = LIB_DIR / "libminixla_b200.so"
-SOURCES = ["runtime.cu", "fused_gemm.cu", "elementwise.cu", "skinny_gemm.cu", "noalloc.cu"]
+SOURCES = ["runtime.cu", "fused_gemm.cu", "elementwise.cu", "skinny_gemm.cu", "noalloc.cu", "hostcopy.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

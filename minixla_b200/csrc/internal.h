@@ -64,6 +64,16 @@ cudaError_t launch_relu(const float* x, long long n, float* out, int num_sms, cu
 cudaError_t launch_wait_timeout_probe(int* err, unsigned long long timeout_ns, cudaStream_t stream);
 cudaError_t launch_hold(unsigned long long ns, cudaStream_t stream);
 
+// Host <-> device copies (hostcopy.cu): pageable host memory goes through a
+// context's ring of pinned slots filled by several host threads; pinned
+// memory and small copies go straight to cudaMemcpyAsync.  copy_d2h into
+// pageable memory returns once the data has arrived.
+class Stager;
+Stager* stager_create();
+void stager_destroy(Stager* s);
+cudaError_t copy_h2d(Stager* s, void* dst, const void* src, size_t bytes, cudaStream_t stream);
+cudaError_t copy_d2h(Stager* s, void* dst, const void* src, size_t bytes, cudaStream_t stream);
+
 // Process-wide count of kernel launches issued by this library.
 void note_launch(unsigned n = 1);
 

@@ -241,6 +241,7 @@ struct GpuCtx {
     std::vector<cudaStream_t> side;  // extra compute streams for independent DAG nodes (made on first use)
     int* d_err = nullptr;
     mxb::DevicePool* pool = nullptr;
+    mxb::Stager* stager = nullptr;   // pinned slots for copies from / to pageable host memory
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     std::vector<cudaEvent_t> sync_events;  // reusable ordering events (no timing)
     std::vector<GpuCtx*> peers;            // devices 1..n-1 of a multi-GPU context
@@ -878,8 +879,8 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
     if (rc == MXB_OK && !order_after(hs, cs)) rc = MXB_E_CUDA;
     for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
         if (order[i]->op == OP_INPUT && !chunked[i] && !info[i].borrowed &&
-            !cuda_ok(cudaMemcpyAsync(info[i].dev, order[i]->output->data, static_cast<size_t>(info[i].size) * 4,
-                                     cudaMemcpyHostToDevice, hs),
+            !cuda_ok(copy_h2d(ctx->stager, info[i].dev, order[i]->output->data,
+                              static_cast<size_t>(info[i].size) * 4, hs),
                      "input upload"))
             rc = MXB_E_CUDA;
     }
@@ -918,8 +919,8 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
         for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
             if (!chunked[i]) continue;
             const long long cols = info[i].size / M;
-            if (!cuda_ok(cudaMemcpyAsync(info[i].dev + r0 * cols, order[i]->output->data + r0 * cols,
-                                         static_cast<size_t>((r1 - r0) * cols) * 4, cudaMemcpyHostToDevice, hs),
+            if (!cuda_ok(copy_h2d(ctx->stager, info[i].dev + r0 * cols, order[i]->output->data + r0 * cols,
+                                  static_cast<size_t>((r1 - r0) * cols) * 4, hs),
                          "chunk upload"))
                 rc = MXB_E_CUDA;
         }
@@ -991,8 +992,8 @@ static int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
         const long long r0 = static_cast<long long>(c) * rows_per;
         const long long r1 = std::min<long long>(M, r0 + rows_per);
         if (cudaStreamWaitEvent(ds, computed[c], 0) != cudaSuccess ||
-            !cuda_ok(cudaMemcpyAsync(host_dst + r0 * out_cols, root.dev + r0 * out_cols,
-                                     static_cast<size_t>((r1 - r0) * out_cols) * 4, cudaMemcpyDeviceToHost, ds),
+            !cuda_ok(copy_d2h(ctx->stager, host_dst + r0 * out_cols, root.dev + r0 * out_cols,
+                              static_cast<size_t>((r1 - r0) * out_cols) * 4, ds),
                      "chunk download"))
             rc = MXB_E_CUDA;
     }
@@ -1171,8 +1172,8 @@ static int execute_sharded(GpuCtx* ctx0, const std::vector<const Node*>& order,
                 if (!ptr[d][i]) continue;
                 DeviceScope scope(ctxs[d]->device);
                 const long long c = cols_of(i);
-                if (!cuda_ok(cudaMemcpyAsync(ptr[d][i], host + r0[d] * c, static_cast<size_t>((r1[d] - r0[d]) * c) * 4,
-                                             cudaMemcpyHostToDevice, ctxs[d]->stream),
+                if (!cuda_ok(copy_h2d(ctxs[d]->stager, ptr[d][i], host + r0[d] * c,
+                                      static_cast<size_t>((r1[d] - r0[d]) * c) * 4, ctxs[d]->stream),
                              "shard upload"))
                     rc = MXB_E_CUDA;
             }
@@ -1181,7 +1182,7 @@ static int execute_sharded(GpuCtx* ctx0, const std::vector<const Node*>& order,
         const size_t bytes = static_cast<size_t>(info[i].size) * 4;
         {
             DeviceScope scope(ctx0->device);
-            if (!cuda_ok(cudaMemcpyAsync(ptr[0][i], host, bytes, cudaMemcpyHostToDevice, ctx0->stream), "upload"))
+            if (!cuda_ok(copy_h2d(ctx0->stager, ptr[0][i], host, bytes, ctx0->stream), "upload"))
                 rc = MXB_E_CUDA;
         }
         cudaEvent_t e = nullptr;
@@ -1284,8 +1285,8 @@ static int execute_sharded(GpuCtx* ctx0, const std::vector<const Node*>& order,
         const long long m = r1[d] - r0[d];
         if (m <= 0) continue;
         DeviceScope scope(ctxs[d]->device);
-        if (!cuda_ok(cudaMemcpyAsync(host_dst + r0[d] * out_cols, rows(d, root_i), static_cast<size_t>(m * out_cols) * 4,
-                                     cudaMemcpyDeviceToHost, ctxs[d]->stream),
+        if (!cuda_ok(copy_d2h(ctxs[d]->stager, host_dst + r0[d] * out_cols, rows(d, root_i),
+                              static_cast<size_t>(m * out_cols) * 4, ctxs[d]->stream),
                      "shard download"))
             rc = MXB_E_CUDA;
     }
@@ -1463,8 +1464,8 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
         size_of[n] = f.size;
         switch (n->op) {
             case OP_INPUT:
-                if (!f.borrowed && !cuda_ok(cudaMemcpyAsync(f.dev, n->output->data, static_cast<size_t>(f.size) * 4,
-                                                            cudaMemcpyHostToDevice, st),
+                if (!f.borrowed && !cuda_ok(copy_h2d(ctx->stager, f.dev, n->output->data,
+                                                     static_cast<size_t>(f.size) * 4, st),
                                             "input upload"))
                     rc = MXB_E_CUDA;
                 break;
@@ -1536,8 +1537,7 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
                 set_error("gpu_execute_into: destination holds %zu elements, result has %lld",
                           dst ? static_cast<size_t>(dst->size) : 0, r.size);
                 rc = MXB_E_ARG;
-            } else if (!cuda_ok(cudaMemcpyAsync(dst->data, r.dev, static_cast<size_t>(r.size) * 4,
-                                                cudaMemcpyDeviceToHost, stream),
+            } else if (!cuda_ok(copy_d2h(ctx->stager, dst->data, r.dev, static_cast<size_t>(r.size) * 4, stream),
                                 "result download") ||
                        !cuda_ok(cudaStreamSynchronize(stream), "download synchronize")) {
                 rc = MXB_E_CUDA;
@@ -1547,8 +1547,7 @@ static int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) 
             if (!t) {
                 set_error("gpu_execute: host allocation of the result failed");
                 rc = MXB_E_NOMEM;
-            } else if (!cuda_ok(cudaMemcpyAsync(t->data, r.dev, static_cast<size_t>(r.size) * 4,
-                                                cudaMemcpyDeviceToHost, stream),
+            } else if (!cuda_ok(copy_d2h(ctx->stager, t->data, r.dev, static_cast<size_t>(r.size) * 4, stream),
                                 "result download") ||
                        !cuda_ok(cudaStreamSynchronize(stream), "download synchronize")) {
                 free(t->data);
@@ -1593,7 +1592,7 @@ struct SingleNode {
 static float* upload(GpuCtx* ctx, const Tensor* t) {
     float* d = static_cast<float*>(ctx->pool->alloc(t->size * 4, ctx->stream));
     if (!d) return nullptr;
-    if (!cuda_ok(cudaMemcpyAsync(d, t->data, t->size * 4, cudaMemcpyHostToDevice, ctx->stream), "upload")) {
+    if (!cuda_ok(copy_h2d(ctx->stager, d, t->data, t->size * 4, ctx->stream), "upload")) {
         ctx->pool->release(d, ctx->stream);
         return nullptr;
     }
@@ -1664,8 +1663,9 @@ static Tensor* run_single(const Node* fused, GpuCtx* ctx, int precision, const c
     if (rc == MXB_OK) {
         result = new_host_tensor({s.M, s.N});
         if (!result ||
-            !cuda_ok(cudaMemcpy(result->data, s.dOut, static_cast<size_t>(s.M) * s.N * 4, cudaMemcpyDeviceToHost),
-                     "result download")) {
+            !cuda_ok(copy_d2h(ctx->stager, result->data, s.dOut, static_cast<size_t>(s.M) * s.N * 4, ctx->stream),
+                     "result download") ||
+            !cuda_ok(cudaStreamSynchronize(ctx->stream), "download synchronize")) {
             if (result) {
                 free(result->data);
                 free(result->shape);
@@ -1776,7 +1776,8 @@ GpuCtx* gpu_ctx_create_on(int device) {
               cuda_ok(cudaMemset(g->d_err, 0, sizeof(int)), "error word clear") &&
               cuda_ok(cudaEventCreate(&g->ev0), "event create") && cuda_ok(cudaEventCreate(&g->ev1), "event create");
     if (ok) g->pool = new (std::nothrow) mxb::DevicePool(device);
-    if (!ok || !g->pool) {
+    if (ok) g->stager = mxb::stager_create();  // its pinned slots are made on first use
+    if (!ok || !g->pool || !g->stager) {
         gpu_ctx_destroy(g);
         return nullptr;
     }
@@ -1862,7 +1863,8 @@ int gpu_ctx_keep_resident(GpuCtx* ctx, const Tensor* t) {
             }
         }
         r.dev.push_back(p);
-        if (!cuda_ok(cudaMemcpy(p, t->data, bytes, cudaMemcpyHostToDevice), "resident upload")) {
+        if (!cuda_ok(mxb::copy_h2d(c->stager, p, t->data, bytes, c->stream), "resident upload") ||
+            !cuda_ok(cudaStreamSynchronize(c->stream), "resident upload synchronize")) {
             free_resident(ctx, r);
             return MXB_E_CUDA;
         }
@@ -1902,6 +1904,7 @@ void gpu_ctx_destroy(GpuCtx* g) {
     {
         mxb::DeviceScope scope(g->device);
         if (g->stream) cudaStreamSynchronize(g->stream);
+        mxb::stager_destroy(g->stager);
         delete g->pool;
         if (g->d_err) cudaFree(g->d_err);
         if (g->ev0) cudaEventDestroy(g->ev0);

@@ -455,6 +455,30 @@ def test_wide_dag_on_several_streams(lib, gpu_ctx, precision):
     assert np.array_equal(got, again)
 
 
+@pytest.mark.parametrize("chunks", ["1", "8"], ids=["one_stream", "row_streamed"])
+def test_staged_host_copies(lib, gpu_ctx, chunks, monkeypatch):
+    """Pageable host buffers above 2 MiB travel through the context's pinned
+    staging slots (several host threads fill a slot while the previous one
+    is on the link).  Results, into a library-made tensor and into a caller
+    buffer, equal those of the driver's own pageable copies
+    (MINIXLA_STAGED_COPY=0) bit for bit, on sizes that end mid-slot."""
+    monkeypatch.setenv("MINIXLA_STREAM_CHUNKS", chunks)
+    M, N, K = 1531, 1536, 1540  # 9-9.4 MB operands: one full 8 MiB slot and a partial one
+    A, B, C = _relu_abc(M, N, K, c_normal=True)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A), hg.input_node(B), [(OP_ADD, hg.input_node(C)), (OP_RELU, None)])
+    staged = run_execute(lib, gpu_ctx, root, TF32)
+    into = np.zeros((M, N), np.float32)
+    assert lib.gpu_execute_into(root, gpu_ctx, hg.tensor(into)) == 0, mlib.last_error()
+    monkeypatch.setenv("MINIXLA_STAGED_COPY", "0")
+    plain = run_execute(lib, gpu_ctx, root, TF32)
+    assert np.array_equal(staged, plain)
+    assert np.array_equal(into, plain)
+    rows = _sample_rows(M, 64)
+    want = bindings.fused_oracle(A, B, [("add", C), ("relu",)], rows=rows)
+    check(staged[rows], want, TF32, "staged copies")
+
+
 def test_resident_weights(lib, gpu_ctx):
     """gpu_ctx_keep_resident: the kept copy is read instead of the host data
     (so a change to the host data is not seen until release + keep), results
