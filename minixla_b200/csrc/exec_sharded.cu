@@ -218,7 +218,7 @@ int execute_sharded(GpuCtx* ctx0, const std::vector<const Node*>& order,
                     steps[n_steps++] = s;
                 }
                 rc = launch_gemm(c, rows(d, ia), K, ptr[d][ib], N, rows(d, i), N, static_cast<int>(m), N, K, steps,
-                                 n_steps, ctx0->precision, c->stream, nullptr, r0[d]);
+                                 n_steps, ctx0->precision, c->stream, nullptr, r0[d], nullptr, plan.M);
             } else if (nd->op == OP_ADD) {
                 const size_t ia = index.at(nd->inputs[0]), ib = index.at(nd->inputs[1]);
                 const bool same = info[ib].size == f.size;

@@ -152,6 +152,8 @@ int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
         if (ctx->precision != GPU_PRECISION_3XTF32 || (nd->op != OP_FUSED && nd->op != OP_MATMUL) || absorbed[i])
             continue;
         const Info& b = info[index.at(nd->inputs[1])];
+        // Nodes on the CUDA-core kernels (few rows, tiny problems) need no low parts.
+        if (M <= kSkinnyMaxRows || use_tiny_gemm(M, b.dims[1], b.dims[0], ctx->precision)) continue;
         b_small[i] = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(b.size) * 4, cs));
         if (!b_small[i]) {
             rc = MXB_E_NOMEM;
@@ -224,7 +226,8 @@ int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
                     prod = Product{a2.dev + r0 * K2, K2, b2.dev, N, K2, b2_small[i]};
                 }
                 rc = launch_gemm(ctx, a.dev + r0 * K, K, b.dev, N, f.dev + r0 * N, N, static_cast<int>(r1 - r0), N, K,
-                                 steps, n_steps, ctx->precision, cs, b_small[i], r0, absorb[i] >= 0 ? &prod : nullptr);
+                                 steps, n_steps, ctx->precision, cs, b_small[i], r0, absorb[i] >= 0 ? &prod : nullptr,
+                                 M);
             } else if (nd->op == OP_ADD) {
                 const Info& a = info[index.at(nd->inputs[0])];
                 const Info& b = info[index.at(nd->inputs[1])];

@@ -57,14 +57,15 @@ static bool dual_in_one_kernel(const GpuCtx* ctx, const float* A, long long lda,
 int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
                 long long ldo, int M, int N, int K, const EpStepDev* steps, int n_steps, int precision,
                 cudaStream_t stream, const float* B_small_pre, long long row_base,
-                const Product* prod) {
+                const Product* prod, int choice_rows) {
+    const int rows_for_choice = choice_rows > 0 ? choice_rows : M;
     if (prod && !dual_in_one_kernel(ctx, A, lda, M, N, K, *prod, precision)) {
         // Two launches: the second product into pooled workspace, then the
         // node reading it as a full add at the same step.
         float* ws = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(M) * N * sizeof(float), stream));
         if (!ws) return MXB_E_NOMEM;
         int rc = launch_gemm(ctx, prod->A, prod->lda, prod->B, prod->ldb, ws, N, M, N, prod->K, nullptr, 0, precision,
-                             stream, prod->B_small);
+                             stream, prod->B_small, 0, nullptr, rows_for_choice);
         if (rc == MXB_OK) {
             EpStepDev st2[MXB_MAX_EPILOGUE];
             for (int i = 0; i < n_steps; ++i) {
@@ -76,12 +77,19 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
                 }
             }
             rc = launch_gemm(ctx, A, lda, B, ldb, out, ldo, M, N, K, st2, n_steps, precision, stream, B_small_pre,
-                             row_base);
+                             row_base, nullptr, rows_for_choice);
         }
         ctx->pool->release(ws, stream);
         return rc;
     }
-    if (M <= kSkinnyMaxRows) {
+    if (rows_for_choice > kSkinnyMaxRows && use_tiny_gemm(rows_for_choice, N, K, precision)) {
+        // Small enough that one plain CUDA-core launch beats the set-up of the tensor-core kernels.
+        return cuda_ok(launch_tiny_gemm(A, lda, B, ldb, out, ldo, M, N, K, row_base, steps, n_steps, stream),
+                       "tiny GEMM launch")
+                   ? MXB_OK
+                   : MXB_E_CUDA;
+    }
+    if (rows_for_choice <= kSkinnyMaxRows) {
         // Few rows: HBM-bound on B, CUDA-core fp32 split over columns and K.
         const SkinnyPlan pl = plan_skinny(M, N, K, ctx->num_sms);
         float* ws = nullptr;  // the one-kernel form needs no workspace

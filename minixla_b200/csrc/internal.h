@@ -54,6 +54,19 @@ cudaError_t launch_skinny_gemm(const float* A, long long lda, const float* B, lo
                                int M, int N, int K, long long row_base, const EpStepDev* steps, int n_steps,
                                float* workspace, const SkinnyPlan& plan, int num_sms, cudaStream_t stream);
 
+// Tiny dense problems in 3xTF32 mode (skinny_gemm.cu): one CUDA-core fp32
+// kernel with 32 x 32 output tiles instead of two split kernels and the
+// tensor-core GEMM, up to M*N*K <= kTinyMaxMnk3x (measured: 128^3 10.1 vs
+// 19.4 us, 384^3 16.4 vs 25.5 us, 512^3 27.5 vs 25.5 us).  In TF32 mode the
+// tensor-core kernels were as fast or faster at every size (128^3 9.1 vs
+// 10.1 us), so kTinyMaxMnk is 0.  MINIXLA_TINY_MAX_MNK overrides both.
+constexpr long long kTinyMaxMnk = 0;
+constexpr long long kTinyMaxMnk3x = 1ll << 26;
+bool use_tiny_gemm(int M, int N, int K, int precision);
+cudaError_t launch_tiny_gemm(const float* A, long long lda, const float* B, long long ldb, float* out, long long ldo,
+                             int M, int N, int K, long long row_base, const EpStepDev* steps, int n_steps,
+                             cudaStream_t stream);
+
 // Kernel launchers (fused_gemm.cu, elementwise.cu).  Return cudaError_t.
 cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream);
 cudaError_t launch_split_tf32(const float* x, long long rows, long long cols, long long ld_in,

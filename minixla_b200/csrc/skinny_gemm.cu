@@ -344,6 +344,92 @@ SkinnyPlan plan_skinny(int M, int N, int K, int num_sms) {
     return p;
 }
 
+// ------------------------------------------------------------------ tiny problems
+//
+// Small dense problems in 3xTF32 mode (config 1's 128^3 and the like) are
+// set by latency, not throughput: one launch of a plain CUDA-core kernel,
+// fp32 FMAs (more accurate than 3xTF32), no tensor-map set-up and no split
+// pre-pass.  Each CTA owns a 32 x 32 output tile; 256 threads hold 2 x 2
+// outputs each; K runs in chunks of kTinyBK staged in shared memory (A
+// transposed, so a thread's two rows are one broadcast read per k), all of
+// a chunk's loads issued before its stores.
+
+namespace {
+
+constexpr int kTinyBK = 128;
+
+__global__ void __launch_bounds__(256)
+    tiny_gemm_kernel(const float* __restrict__ A, long long lda, const float* __restrict__ B, long long ldb,
+                     float* __restrict__ out, long long ldo, int M, int N, int K, long long row_base,
+                     const __grid_constant__ SkinnyEpilogue epi) {
+    __shared__ float As[kTinyBK][33];  // As[k][m]
+    __shared__ float Bs[kTinyBK][32];  // Bs[k][n]
+    constexpr int kPer = 32 * kTinyBK / 256;  // elements of each operand a thread stages per chunk
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int m0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+    float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+    for (int k0 = 0; k0 < K; k0 += kTinyBK) {
+        // All of the chunk's loads are issued before any store, so their latencies overlap.
+        float ra[kPer], rb[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int i = threadIdx.x + u * 256;
+            const int r = i / kTinyBK, k = i - r * kTinyBK;  // A: consecutive threads along k
+            ra[u] = (m0 + r < M && k0 + k < K) ? __ldg(A + static_cast<long long>(m0 + r) * lda + k0 + k) : 0.0f;
+            const int kb = i >> 5, c = i & 31;                // B: consecutive threads along n
+            rb[u] = (k0 + kb < K && n0 + c < N) ? __ldg(B + static_cast<long long>(k0 + kb) * ldb + n0 + c) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int i = threadIdx.x + u * 256;
+            const int r = i / kTinyBK, k = i - r * kTinyBK;
+            As[k][r] = ra[u];
+            Bs[i >> 5][i & 31] = rb[u];
+        }
+        __syncthreads();
+#pragma unroll 16
+        for (int k = 0; k < kTinyBK; ++k) {
+            const float a0 = As[k][2 * ty], a1 = As[k][2 * ty + 1];
+            const float b0 = Bs[k][2 * tx], b1 = Bs[k][2 * tx + 1];
+            acc[0][0] = fmaf(a0, b0, acc[0][0]);
+            acc[0][1] = fmaf(a0, b1, acc[0][1]);
+            acc[1][0] = fmaf(a1, b0, acc[1][0]);
+            acc[1][1] = fmaf(a1, b1, acc[1][1]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int m = m0 + 2 * ty + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int n = n0 + 2 * tx + j;
+            if (n < N) out[static_cast<long long>(m) * ldo + n] = skinny_epilogue(acc[i][j], m, n, N, row_base, epi);
+        }
+    }
+}
+
+}  // namespace
+
+bool use_tiny_gemm(int M, int N, int K, int precision) {
+    const long long mnk = static_cast<long long>(M) * N * K;
+    if (const char* v = getenv("MINIXLA_TINY_MAX_MNK")) return mnk <= atoll(v);
+    return mnk <= (precision == GPU_PRECISION_3XTF32 ? kTinyMaxMnk3x : kTinyMaxMnk);
+}
+
+cudaError_t launch_tiny_gemm(const float* A, long long lda, const float* B, long long ldb, float* out, long long ldo,
+                             int M, int N, int K, long long row_base, const EpStepDev* steps, int n_steps,
+                             cudaStream_t stream) {
+    SkinnyEpilogue epi{};
+    epi.n_steps = n_steps;
+    for (int i = 0; i < n_steps; ++i) epi.steps[i] = steps[i];
+    const dim3 grid((N + 31) / 32, (M + 31) / 32);
+    tiny_gemm_kernel<<<grid, 256, 0, stream>>>(A, lda, B, ldb, out, ldo, M, N, K, row_base, epi);
+    note_launch();
+    return cudaGetLastError();
+}
+
 cudaError_t launch_skinny_gemm(const float* A, long long lda, const float* B, long long ldb, float* out, long long ldo,
                                int M, int N, int K, long long row_base, const EpStepDev* steps, int n_steps,
                                float* workspace, const SkinnyPlan& pl, int num_sms, cudaStream_t stream) {

@@ -428,6 +428,27 @@ def test_skinny_rows_path(lib, gpu_ctx, M, form, NK, precision, monkeypatch, hos
 
 
 @pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
+@pytest.mark.parametrize("mnk", [(33, 47, 129), (100, 100, 300), (64, 1000, 5), (128, 128, 128), (200, 96, 1000)])
+def test_tiny_path(lib, gpu_ctx, mnk, precision, monkeypatch, host_threads):
+    """The one-launch CUDA-core kernel for tiny problems (3xTF32 mode up to
+    M*N*K = 2^26; forced here in both modes with MINIXLA_TINY_MAX_MNK):
+    ragged tiles, K not a multiple of the staged chunk, every epilogue kind,
+    against the oracle at the 3xTF32 tolerance (fp32 FMAs)."""
+    monkeypatch.setenv("MINIXLA_TINY_MAX_MNK", str(1 << 40))
+    M, N, K = mnk
+    A, B, C = _relu_abc(M, N, K, c_normal=True)
+    bias = datagen.normal((N,), 8, 0.0, 0.5)
+    odd = datagen.uniform((13,), 9)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A), hg.input_node(B),
+                         [(OP_ADD, hg.input_node(C)), (OP_ADD, hg.input_node(odd)), (OP_RELU, None),
+                          (OP_ADD, hg.input_node(bias))])
+    got = run_execute(lib, gpu_ctx, root, precision)
+    want = bindings.fused_oracle(A, B, [("add", C), ("add", odd), ("relu",), ("add", bias)], threads=host_threads)
+    check(got, want, X3, f"tiny {mnk}")
+
+
+@pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
 def test_wide_dag_on_several_streams(lib, gpu_ctx, precision):
     """Six independent branches from one input (spread over the executor's
     streams), joined by standalone adds and a final fused node: exercises
@@ -755,7 +776,9 @@ print("OK")
 
 @pytest.mark.parametrize("fail_at", [1, 3, 4, 5, 6])
 def test_allocation_failure_injection(fail_at):
-    env = dict(os.environ, MINIXLA_FAIL_ALLOC_AT=str(fail_at))
+    # The tensor-core path (not the tiny-problem kernel) so the graph makes its full set of
+    # allocations: inputs, output and the 3xTF32 low parts.
+    env = dict(os.environ, MINIXLA_FAIL_ALLOC_AT=str(fail_at), MINIXLA_TINY_MAX_MNK="0")
     r = subprocess.run([sys.executable, "-c", _OOM_CHILD, str(ROOT)], env=env, capture_output=True, text=True,
                        timeout=300)
     assert r.returncode == 0 and "OK" in r.stdout, r.stdout + r.stderr
