@@ -233,7 +233,8 @@ def reference_arm(args, rank, world):
     value = 2.0 * rows * len(timed) * NDIM * NDIM / total / 1e12
     line = {
         "metric": "fused relu(A.B+C) TFLOP/s (fp32 in/out)", "impl": "reference", "value": value,
-        "unit": "TFLOP/s", "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
+        "unit": "TFLOP/s", "n_gpus": args.gpus, "devices": "host CPU cores only (the reference's execute())",
+        "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * total / len(timed), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded splitmix64: A,B ~ U[-1,1], C ~ N(0,1))",
         "config": {"workload": "relu(A.B+C) 8192x8192x8192 per shard, row sample per step",
