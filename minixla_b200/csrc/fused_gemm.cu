@@ -117,6 +117,45 @@ __device__ __forceinline__ void raise_error(const FusedParams& p, volatile int* 
 // (graph.c:98-109): ADD adds the operand element, RELU is x > 0 ? x : 0.
 // `prod` (pair kernel, DUAL) holds this chunk of the second product, added
 // at the MXB_EP_ADD_PRODUCT step.
+// A row segment of W floats at an address that is 4-byte but not 16-byte
+// aligned (odd row pitches): PRE scalars up to the next 16-byte boundary,
+// float4s in the middle, scalars for the tail; PRE is the segment's
+// misalignment, so every index is a compile-time constant.
+template <int W, int PRE>
+__device__ __forceinline__ void add_segment(float (&v)[W], const float* src) {
+#pragma unroll
+    for (int i = 0; i < PRE; ++i) v[i] += __ldcs(src + i);
+    constexpr int kG = (W - PRE) / 4;
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+        const float4 c = __ldcs(reinterpret_cast<const float4*>(src + PRE) + g);
+        v[PRE + 4 * g + 0] += c.x;
+        v[PRE + 4 * g + 1] += c.y;
+        v[PRE + 4 * g + 2] += c.z;
+        v[PRE + 4 * g + 3] += c.w;
+    }
+#pragma unroll
+    for (int i = PRE + 4 * kG; i < W; ++i) v[i] += __ldcs(src + i);
+}
+
+template <int W, int PRE>
+__device__ __forceinline__ void store_segment(const float (&v)[W], float* dst) {
+#pragma unroll
+    for (int i = 0; i < PRE; ++i) __stcs(dst + i, v[i]);
+    constexpr int kG = (W - PRE) / 4;
+#pragma unroll
+    for (int g = 0; g < kG; ++g)
+        __stcs(reinterpret_cast<float4*>(dst + PRE) + g,
+               make_float4(v[PRE + 4 * g], v[PRE + 4 * g + 1], v[PRE + 4 * g + 2], v[PRE + 4 * g + 3]));
+#pragma unroll
+    for (int i = PRE + 4 * kG; i < W; ++i) __stcs(dst + i, v[i]);
+}
+
+// Scalars before the first 16-byte boundary of a 4-byte aligned address.
+__device__ __forceinline__ int lead_scalars(const float* p) {
+    return static_cast<int>((4 - ((reinterpret_cast<uintptr_t>(p) >> 2) & 3)) & 3);
+}
+
 template <int W = 32>
 __device__ __forceinline__ void apply_epilogue(float (&v)[W], int row, int col, bool row_ok,
                                                const FusedParams& p, const float* prod = nullptr) {
@@ -150,6 +189,13 @@ __device__ __forceinline__ void apply_epilogue(float (&v)[W], int row, int col, 
                     v[4 * i + 1] += c.y;
                     v[4 * i + 2] += c.z;
                     v[4 * i + 3] += c.w;
+                }
+            } else if (full_cols) {
+                switch (lead_scalars(src)) {
+                    case 0: add_segment<W, 0>(v, src); break;
+                    case 1: add_segment<W, 1>(v, src); break;
+                    case 2: add_segment<W, 2>(v, src); break;
+                    default: add_segment<W, 3>(v, src); break;
                 }
             } else {
 #pragma unroll
@@ -194,6 +240,14 @@ __device__ __forceinline__ void store_row_chunk(const float (&v)[W], int row, in
 #pragma unroll
         for (int i = 0; i < W / 4; ++i)
             __stcs(d4 + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+    } else if (col + W <= p.N) {
+        // Odd row pitch: align each row's segment on its own.
+        switch (lead_scalars(dst)) {
+            case 0: store_segment<W, 0>(v, dst); break;
+            case 1: store_segment<W, 1>(v, dst); break;
+            case 2: store_segment<W, 2>(v, dst); break;
+            default: store_segment<W, 3>(v, dst); break;
+        }
     } else {
 #pragma unroll
         for (int i = 0; i < W; ++i)
