@@ -1,0 +1,408 @@
+// TF32 CTA-pair kernels (cta_group::2): 256x256 and 256x512 tiles of one
+// product, and the two-product form on 128- or 256-wide tiles.
+#include "gemm_common.cuh"
+
+namespace mxb {
+
+namespace {
+
+// ------------------------------------------------------------------ CTA-pair kernel (TF32)
+//
+// Pair tile 256 x BN on a 2-CTA cluster (the two SMs of a TPC).  CTA r owns
+// output rows m0 + 128 r .. +128; per k-block it stages its 128 rows of A and
+// B columns n0 + (BN/2) r .. +BN/2 (half of the tile's B).  The leader (rank
+// 0) issues tcgen05.mma.cta_group::2 (M=256, N=BN, K=8), which reads the A
+// and B halves from both CTAs' shared memory and leaves each CTA's 128 x BN
+// accumulator in that CTA's TMEM.  Per SM that halves the B bytes staged and
+// read per MMA: with BN = 256 a stage is 32 KiB and six stages fit.  With
+// BN = 512 the leader issues two N = 256 MMAs per k step, each into its own
+// 256 accumulator columns; CTA r stages, for MMA h, B columns
+// nb*512 + 256 h + 128 r .. +128, so accumulator column c is output column
+// nb*512 + c.  A stage is 48 KiB (four fit) and the 512 columns leave one
+// TMEM buffer: the epilogue drains it before the next tile starts.
+//
+// DUAL: the node's epilogue holds one step that adds a second product
+// A @ B2 with the same A (a bare matmul on the same left operand whose only
+// consumer is this node: config 4's relu(h W2 + b2) + h W2').  Each k-block
+// stages A once with the B and B2 halves; the MMA warp issues A.B into
+// accumulator 0 and A.B2 into accumulator 1 next to it in TMEM; the epilogue
+// reads both and adds the second where the step stands.  The second product
+// never goes to HBM and A is read once for both.  With BN = 128 a stage holds
+// the same 32 KiB as the BN = 256 single product (A 16 KiB + two 8 KiB B
+// halves), and the two accumulators of both TMEM buffers fill the 512
+// columns, so the epilogue still overlaps the next tile's k-loop.
+//
+// Barriers: full[s] lives in the leader and counts both CTAs' TMA bytes (the
+// peer's loads signal it through its cluster address); empty[s] and tfull[a]
+// live in both CTAs and receive the leader's multicast commits; tempty[a]
+// lives in the leader and takes one arrival per epilogue warp of either CTA.
+
+template <int STAGES, int BN, bool DUAL, int EPI = 4>
+struct PairCfg {
+    static_assert(EPI == 4 || EPI == 8, "epilogue warps: one or two per TMEM lane quadrant");
+    static constexpr int kThreadsPerCta = 64 + 32 * EPI;         // TMA warp, MMA warp, epilogue warps
+    static constexpr int kABytes = 128 * kBK * 4;                // 16 KiB: this CTA's A rows
+    static constexpr int kBBytes = (BN / 2) * kBK * 4;           // this CTA's B columns (per product)
+    static constexpr int kStageBytes = kABytes + (DUAL ? 2 : 1) * kBBytes;
+    // One MMA covers at most N = 256: wider tiles issue BN / 256 of them per
+    // k step, each on its own 256 accumulator columns.
+    static constexpr int kSubN = BN < 256 ? BN : 256;
+    static constexpr int kSubs = BN / kSubN;
+    static constexpr int kSubBoxes = kSubN / 64;                 // 32-column B boxes per CTA per sub-MMA
+    static constexpr int kAccCols = (DUAL ? 2 : 1) * BN;         // TMEM columns of one tile's accumulators
+    static constexpr int kBufs = kAccCols <= 256 ? 2 : 1;        // accumulator buffers in TMEM
+    static constexpr int kTmemCols = kBufs * kAccCols;
+    static constexpr int kBarOffset = STAGES * kStageBytes;
+    static constexpr int kNumBars = 2 * STAGES + 5;
+    static constexpr int kSmemBytes = 1024 + kBarOffset + kNumBars * 8 + 16;
+    static_assert(BN == 128 || BN == 256 || BN == 512, "pair tile width");
+    static_assert(!(DUAL && BN == 512), "two products use 128- or 256-column tiles");
+    static_assert(kStageBytes % 1024 == 0, "stages must keep 1 KiB swizzle alignment");
+    static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+template <int STAGES, int BN, bool DUAL, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, DUAL, EPI>::kThreadsPerCta, 1)
+    fused_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+                           const __grid_constant__ FusedParams p) {
+    using C = PairCfg<STAGES, BN, DUAL, EPI>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::kNumBars);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t bar0 = smem_addr(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+    auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+    auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1;
+    const int num_pairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), 2 * EPI);  // every epilogue warp of the two CTAs
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+        if (DUAL) {
+            tma_prefetch_desc(&tmA2);
+            tma_prefetch_desc(&tmB2);
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_addr(tmem_slot), C::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer (both CTAs)
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            long long issued = 0;
+            bool ok = true;
+            for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+                int mb, nb;
+                tile_coords(t, p, mb, nb);
+                const int m0 = mb * 256 + static_cast<int>(rank) * 128;
+                // CTA r stages, for sub-MMA h, B columns nb*BN + h*kSubN + r*kSubN/2 ..
+                // + kSubN/2, so accumulator column c is output column nb*BN + c.
+                const int n0 = nb * BN + static_cast<int>(rank) * (C::kSubN / 2);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (*abort_flag) { ok = false; break; }
+                    if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1u, p.timeout_ns)) {
+                        raise_error(p, abort_flag, kErrProducer);
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = smem + stage * C::kStageBytes;
+                    if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * C::kStageBytes);
+                    const uint32_t fb = mapa_shared(full_bar(stage), 0);
+                    const int k0 = kb * kBK;
+                    tma_load_2d_pair(smem_addr(st), &tmA, fb, k0, m0);
+#pragma unroll
+                    for (int j = 0; j < BN / 64; ++j)
+                        tma_load_2d_pair(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb,
+                                         n0 + (j / C::kSubBoxes) * C::kSubN + 32 * (j % C::kSubBoxes), k0);
+                    if (DUAL) {
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j)
+                            tma_load_2d_pair(smem_addr(st + C::kABytes + C::kBBytes + j * kBoxBytes), &tmB2, fb,
+                                             n0 + 32 * j, k0);
+                    }
+                    ++issued;
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!ok && rank == 0) {
+                // The leader's full barriers count both CTAs' bytes: wait for the copies in flight.
+                const long long n = issued < STAGES ? issued : STAGES;
+                for (long long i = 1; i <= n; ++i) {
+                    const long long idx = issued - i;
+                    mbar_wait_cluster(full_bar(static_cast<int>(idx % STAGES)),
+                                      static_cast<uint32_t>((idx / STAGES) & 1), p.timeout_ns);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer (leader only)
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = idesc_tf32(256, C::kSubN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+                if (*abort_flag) break;
+                if (!mbar_wait_cluster(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns)) {
+                    raise_error(p, abort_flag, kErrMma);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tile = tmem_base + static_cast<uint32_t>(acc * C::kAccCols);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait_cluster(full_bar(stage), phase, p.timeout_ns)) {
+                        raise_error(p, abort_flag, kErrMma);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_addr(smem + stage * C::kStageBytes);
+                    const uint32_t b_addr = a_addr + C::kABytes;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 8; ++kk) {
+                        const uint64_t da = smem_desc(a_addr + kk * 32, 16, 1024, kLayoutSW128);
+                        const uint64_t db = smem_desc(b_addr + kk * 1024, kBoxBytes, 512, kLayoutSW128Base32B);
+                        const uint32_t accumulate = (kb | kk) != 0 ? 1u : 0u;
+                        mma_tf32_pair(d_tile, da, db, idesc, accumulate);
+#pragma unroll
+                        for (int h = 1; h < C::kSubs; ++h) {
+                            const uint64_t dbh = smem_desc(b_addr + h * C::kSubBoxes * kBoxBytes + kk * 1024,
+                                                           kBoxBytes, 512, kLayoutSW128Base32B);
+                            mma_tf32_pair(d_tile + h * C::kSubN, da, dbh, idesc, accumulate);
+                        }
+                        if (DUAL) {
+                            const uint64_t db2 =
+                                smem_desc(b_addr + C::kBBytes + kk * 1024, kBoxBytes, 512, kLayoutSW128Base32B);
+                            mma_tf32_pair(d_tile + BN, da, db2, idesc, accumulate);
+                        }
+                    }
+                    mma_commit_pair(empty_bar(stage), 0x3);
+                    if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                mma_commit_pair(tfull_bar(acc), 0x3);
+                if (C::kBufs == 2) acc ^= 1;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            mma_commit_pair(drain_bar, 0x1);
+            if (!mbar_wait_cluster(drain_bar, 0, p.timeout_ns)) raise_error(p, abort_flag, kErrMma);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        // Warp w reads TMEM lane quadrant w % 4; with EPI = 8 the two warps of a
+        // quadrant split the tile's columns in halves.
+        const int quad = warp & 3;
+        constexpr int kChunksPerWarp = BN / 32 / (EPI / 4);
+        const int c_first = ((warp - 2) >> 2) * kChunksPerWarp;
+        const int row_in_tile = static_cast<int>(rank) * 128 + quad * 32 + lane;
+        const uint32_t tempty_leader0 = mapa_shared(tempty_bar(0), 0);
+        const uint32_t tempty_leader1 = mapa_shared(tempty_bar(1), 0);
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int t = pair; t < p.num_tiles; t += num_pairs) {
+            int mb, nb;
+            tile_coords(t, p, mb, nb);
+            const int row = mb * 256 + row_in_tile;
+            const bool row_ok = row < p.M;
+            const int col0 = nb * BN;
+            int chunks = (p.N - col0 + 31) / 32;
+            if (chunks > c_first + kChunksPerWarp) chunks = c_first + kChunksPerWarp;
+            // C rows into L2: during the k-loop when it is short, else once the accumulator is ready.
+            const bool fetch = row_ok && chunks > c_first;
+            if (fetch && p.num_kb <= kShortKb)
+                prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p);
+            const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
+            const bool got = !stop && mbar_wait_cluster(tfull_bar(acc), acc_phase, p.timeout_ns);
+            if (!__all_sync(0xffffffffu, got)) {
+                if (lane == 0 && !stop) raise_error(p, abort_flag, kErrEpilogue);
+                break;
+            }
+            tc_fence_after();
+            if (fetch && p.num_kb > kShortKb)
+                prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p);
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                   static_cast<uint32_t>(acc * C::kAccCols);
+            if (chunks <= c_first) {
+                // No columns of this tile for this warp: release the accumulator at once.
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+            }
+            for (int c = c_first; c < chunks; ++c) {
+                uint32_t r[32];
+                float w[32];
+                tmem_ld_32x32b_x32(taddr + 32 * c, r);
+                if (DUAL) {
+                    uint32_t r2[32];
+                    tmem_ld_32x32b_x32(taddr + BN + 32 * c, r2);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) w[i] = __uint_as_float(r2[i]);
+                } else {
+                    tmem_ld_wait();
+                }
+                if (c == chunks - 1) {
+                    // This warp is done with the accumulator: tell the leader's MMA warp.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+                }
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                const int col = col0 + 32 * c;
+                if (DUAL)
+                    apply_epilogue(v, row, col, row_ok, p, w);
+                else
+                    apply_epilogue(v, row, col, row_ok, p);
+                if (row_ok) store_row_chunk(v, row, col, p);
+            }
+            if (C::kBufs == 2) acc ^= 1;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+    }
+
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, C::kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+template <int STAGES, int BN, bool DUAL, int EPI = 4>
+cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
+    using C = PairCfg<STAGES, BN, DUAL, EPI>;
+    auto kernel = fused_gemm_pair_kernel<STAGES, BN, DUAL, EPI>;
+    static std::mutex mu;
+    static uint64_t configured = 0;
+    static int max_clusters[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    int clusters = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (dev >= 64 || !(configured & (1ull << dev))) {
+            e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+            if (e != cudaSuccess) return e;
+            // How many 2-CTA clusters fit at once with this much shared memory.
+            cudaLaunchConfig_t cfg = {};
+            cudaLaunchAttribute attr;
+            attr.id = cudaLaunchAttributeClusterDimension;
+            attr.val.clusterDim.x = 2;
+            attr.val.clusterDim.y = 1;
+            attr.val.clusterDim.z = 1;
+            cfg.gridDim = dim3(2 * (g.num_sms / 2), 1, 1);
+            cfg.blockDim = dim3(C::kThreadsPerCta, 1, 1);
+            cfg.dynamicSmemBytes = C::kSmemBytes;
+            cfg.attrs = &attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n < 1) {
+                cudaGetLastError();
+                n = g.num_sms / 2;
+            }
+            if (dev < 64) {
+                max_clusters[dev] = n;
+                configured |= 1ull << dev;
+            }
+            clusters = n;
+        } else {
+            clusters = max_clusters[dev];
+        }
+    }
+
+    constexpr CUtensorMapSwizzle kSwA = CU_TENSOR_MAP_SWIZZLE_128B;
+    constexpr CUtensorMapSwizzle kSwB = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+    CUtensorMap mA, mB, mA2, mB2;
+    if (!make_map(&mA, g.A, g.M, g.K, g.lda, kBK, 128, kSwA) || !make_map(&mB, g.B, g.K, g.N, g.ldb, 32, kBK, kSwB))
+        return cudaErrorInvalidValue;
+    if (DUAL) {
+        // The second product shares A (same rows, K and pitch); only B2 has a map of its own.
+        if (g.A2 != g.A || g.K2 != g.K || g.lda2 != g.lda || !g.B2 ||
+            !make_map(&mB2, g.B2, g.K, g.N, g.ldb2, 32, kBK, kSwB))
+            return cudaErrorInvalidValue;
+        mA2 = mA;
+    } else {
+        mA2 = mA;
+        mB2 = mB;
+    }
+
+    FusedParams p{};
+    p.out = g.out;
+    p.ldo = g.ldo;
+    p.M = g.M;
+    p.N = g.N;
+    p.K = g.K;
+    p.n_steps = g.n_steps;
+    p.tiles_m = (g.M + 255) / 256;
+    p.tiles_n = (g.N + BN - 1) / BN;
+    p.num_tiles = p.tiles_m * p.tiles_n;
+    p.num_kb = (g.K + kBK - 1) / kBK;
+    p.group_m = 8;
+    p.seg_kb = p.num_kb;
+    p.row_base = g.row_base;
+    p.timeout_ns = g.timeout_ns;
+    p.err = g.err;
+    for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
+
+    const int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;
+    kernel<<<2 * pairs, C::kThreadsPerCta, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p);
+    note_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_pair_tf32(const GemmLaunch& g, bool wide_tiles, cudaStream_t stream) {
+    return wide_tiles ? run_pair_variant<4, 512, false>(g, stream) : run_pair_variant<6, 256, false>(g, stream);
+}
+
+// 256-column tiles put both accumulators in the 512 TMEM columns (one buffer,
+// 48 KiB stages); 128-column tiles keep two buffers for problems with few tiles.
+cudaError_t launch_pair_tf32_dual(const GemmLaunch& g, cudaStream_t stream) {
+    const long long tiles256 = static_cast<long long>((g.M + 255) / 256) * ((g.N + 255) / 256);
+    if (tiles256 >= g.num_sms / 2) return run_pair_variant<4, 256, true>(g, stream);
+    return run_pair_variant<6, 128, true>(g, stream);
+}
+
+}  // namespace mxb

@@ -1,0 +1,263 @@
+// Shared by the fused-GEMM translation units (fused_gemm.cu: single-CTA
+// kernels and the dispatcher; fused_gemm_pair.cu: TF32 CTA-pair kernels;
+// fused_gemm_pair3.cu: 3xTF32 CTA-pair kernels): tile constants, the kernel
+// parameter block, tile order, bounded-wait error reporting, the fused
+// epilogue in registers, and the TMA tensor-map encoder.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+
+#include "internal.h"
+#include "sm100_ptx.cuh"
+
+namespace mxb {
+
+// Launchers of the CTA-pair kernels (their translation units).
+cudaError_t launch_pair_tf32(const GemmLaunch& g, bool wide_tiles, cudaStream_t stream);
+cudaError_t launch_pair_tf32_dual(const GemmLaunch& g, cudaStream_t stream);
+cudaError_t launch_pair_3xtf32(const GemmLaunch& g, bool dual, cudaStream_t stream);
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 32;           // fp32 elements per 128-byte swizzle row
+constexpr int kThreads = 192;
+constexpr int kBoxBytes = 32 * 32 * 4;  // one B box: 32 k-rows x 128 bytes
+
+constexpr int kSegKb = 8;           // k-blocks (of 32) per accumulation segment in 3xTF32 mode
+// With at most this many k-blocks the main loop is short (K <= 1024), so the
+// epilogue prefetches its rows of the ADD operands before the accumulator is
+// ready; longer loops prefetch once it is (earlier lines would be evicted).
+constexpr int kShortKb = 32;
+
+struct FusedParams {
+    float* out;
+    long long ldo;
+    int M, N, K;
+    int n_steps;
+    int tiles_m, tiles_n, num_tiles, num_kb;
+    int group_m;
+    int seg_kb;                     // k-blocks per accumulation segment (num_kb: one segment)
+    long long row_base;             // global index of row 0 of this launch (modulo-rule operands)
+    unsigned long long timeout_ns;
+    int* err;
+    EpStepDev steps[MXB_MAX_EPILOGUE];
+};
+
+// Error bits written to the device error word.
+enum : int { kErrProducer = 1, kErrMma = 2, kErrEpilogue = 4, kErrProbe = 8 };
+
+__device__ __forceinline__ void tile_coords(int t, const FusedParams& p, int& mb, int& nb) {
+    // Groups of group_m row-blocks; inside a group the row-block varies fastest,
+    // so a wave of CTAs covers a compact group_m x (wave/group_m) patch.
+    const int group_tiles = p.group_m * p.tiles_n;
+    const int g = t / group_tiles;
+    const int first_m = g * p.group_m;
+    const int gm = min(p.tiles_m - first_m, p.group_m);
+    const int r = t - g * group_tiles;
+    mb = first_m + r % gm;
+    nb = r / gm;
+}
+
+__device__ __forceinline__ void raise_error(const FusedParams& p, volatile int* abort_flag, int bit) {
+    atomicOr(p.err, bit);
+    *abort_flag = 1;
+}
+
+// Applies the node's epilogue steps, in order, to 32 consecutive outputs of
+// one row (cols col..col+31), exactly as eval_fused does per cell
+// (graph.c:98-109): ADD adds the operand element, RELU is x > 0 ? x : 0.
+// `prod` (pair kernel, DUAL) holds this chunk of the second product, added
+// at the MXB_EP_ADD_PRODUCT step.
+// A row segment of W floats at an address that is 4-byte but not 16-byte
+// aligned (odd row pitches): PRE scalars up to the next 16-byte boundary,
+// float4s in the middle, scalars for the tail; PRE is the segment's
+// misalignment, so every index is a compile-time constant.
+template <int W, int PRE>
+__device__ __forceinline__ void add_segment(float (&v)[W], const float* src) {
+#pragma unroll
+    for (int i = 0; i < PRE; ++i) v[i] += __ldcs(src + i);
+    constexpr int kG = (W - PRE) / 4;
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+        const float4 c = __ldcs(reinterpret_cast<const float4*>(src + PRE) + g);
+        v[PRE + 4 * g + 0] += c.x;
+        v[PRE + 4 * g + 1] += c.y;
+        v[PRE + 4 * g + 2] += c.z;
+        v[PRE + 4 * g + 3] += c.w;
+    }
+#pragma unroll
+    for (int i = PRE + 4 * kG; i < W; ++i) v[i] += __ldcs(src + i);
+}
+
+template <int W, int PRE>
+__device__ __forceinline__ void store_segment(const float (&v)[W], float* dst) {
+#pragma unroll
+    for (int i = 0; i < PRE; ++i) __stcs(dst + i, v[i]);
+    constexpr int kG = (W - PRE) / 4;
+#pragma unroll
+    for (int g = 0; g < kG; ++g)
+        __stcs(reinterpret_cast<float4*>(dst + PRE) + g,
+               make_float4(v[PRE + 4 * g], v[PRE + 4 * g + 1], v[PRE + 4 * g + 2], v[PRE + 4 * g + 3]));
+#pragma unroll
+    for (int i = PRE + 4 * kG; i < W; ++i) __stcs(dst + i, v[i]);
+}
+
+// Scalars before the first 16-byte boundary of a 4-byte aligned address.
+__device__ __forceinline__ int lead_scalars(const float* p) {
+    return static_cast<int>((4 - ((reinterpret_cast<uintptr_t>(p) >> 2) & 3)) & 3);
+}
+
+template <int W = 32>
+__device__ __forceinline__ void apply_epilogue(float (&v)[W], int row, int col, bool row_ok,
+                                               const FusedParams& p, const float* prod = nullptr) {
+    static_assert(W % 4 == 0, "whole float4 groups");
+    const bool full_cols = col + W <= p.N;
+    for (int s = 0; s < p.n_steps; ++s) {
+        const int kind = p.steps[s].kind;
+        const float* ptr = p.steps[s].ptr;
+        if (kind == MXB_EP_ADD_PRODUCT) {
+            if (prod) {
+#pragma unroll
+                for (int i = 0; i < W; ++i) v[i] += prod[i];
+            }
+        } else if (kind == MXB_EP_RELU) {
+#pragma unroll
+            for (int i = 0; i < W; ++i) v[i] = v[i] > 0.0f ? v[i] : 0.0f;
+        } else if (kind == MXB_EP_SCALE) {
+            const float sc = p.steps[s].scale;
+#pragma unroll
+            for (int i = 0; i < W; ++i) v[i] = v[i] * sc;
+        } else if (kind == MXB_EP_ADD_FULL) {
+            if (!row_ok) continue;
+            const long long ld = p.steps[s].ld_or_size;
+            const float* src = ptr + static_cast<long long>(row) * ld + col;
+            if (full_cols && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+                const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+                for (int i = 0; i < W / 4; ++i) {
+                    const float4 c = __ldcs(s4 + i);
+                    v[4 * i + 0] += c.x;
+                    v[4 * i + 1] += c.y;
+                    v[4 * i + 2] += c.z;
+                    v[4 * i + 3] += c.w;
+                }
+            } else if (full_cols) {
+                switch (lead_scalars(src)) {
+                    case 0: add_segment<W, 0>(v, src); break;
+                    case 1: add_segment<W, 1>(v, src); break;
+                    case 2: add_segment<W, 2>(v, src); break;
+                    default: add_segment<W, 3>(v, src); break;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < W; ++i)
+                    if (col + i < p.N) v[i] += __ldg(src + i);
+            }
+        } else if (kind == MXB_EP_ADD_ROW) {
+            const float* src = ptr + col;
+            if (full_cols && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+                const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+                for (int i = 0; i < W / 4; ++i) {
+                    const float4 c = __ldg(s4 + i);
+                    v[4 * i + 0] += c.x;
+                    v[4 * i + 1] += c.y;
+                    v[4 * i + 2] += c.z;
+                    v[4 * i + 3] += c.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < W; ++i)
+                    if (col + i < p.N) v[i] += __ldg(src + i);
+            }
+        } else if (kind == MXB_EP_ADD_MOD) {
+            if (!row_ok) continue;
+            const unsigned long long size = static_cast<unsigned long long>(p.steps[s].ld_or_size);
+            const unsigned long long base =
+                static_cast<unsigned long long>(row + p.row_base) * static_cast<unsigned long long>(p.N) + col;
+#pragma unroll
+            for (int i = 0; i < W; ++i)
+                if (col + i < p.N) v[i] += __ldg(ptr + (base + i) % size);
+        }
+    }
+}
+
+template <int W = 32>
+__device__ __forceinline__ void store_row_chunk(const float (&v)[W], int row, int col,
+                                                const FusedParams& p) {
+    float* dst = p.out + static_cast<long long>(row) * p.ldo + col;
+    if (col + W <= p.N && (p.ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+        for (int i = 0; i < W / 4; ++i)
+            __stcs(d4 + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+    } else if (col + W <= p.N) {
+        // Odd row pitch: align each row's segment on its own.
+        switch (lead_scalars(dst)) {
+            case 0: store_segment<W, 0>(v, dst); break;
+            case 1: store_segment<W, 1>(v, dst); break;
+            case 2: store_segment<W, 2>(v, dst); break;
+            default: store_segment<W, 3>(v, dst); break;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < W; ++i)
+            if (col + i < p.N) dst[i] = v[i];
+    }
+}
+
+// Pulls this thread's rows of every full-matrix ADD operand, columns
+// col .. col + ncols, into L2 ahead of the epilogue's loads.
+__device__ __forceinline__ void prefetch_full_operands(int row, int col, int ncols, const FusedParams& p) {
+    for (int s = 0; s < p.n_steps; ++s) {
+        if (p.steps[s].kind != MXB_EP_ADD_FULL) continue;
+        const float* src = p.steps[s].ptr + static_cast<long long>(row) * p.steps[s].ld_or_size + col;
+        for (int c = 0; c < ncols; c += 32)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(src + c)));
+    }
+}
+
+// ------------------------------------------------------------------ tensor maps
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// Row-major [rows, cols] fp32 with row pitch `ld` elements; box [box_rows][box_cols].
+bool make_map(CUtensorMap* map, const float* base, long long rows, long long cols, long long ld,
+              int box_cols, int box_rows, CUtensorMapSwizzle swizzle) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    // TFLOAT32: TMA rounds each fp32 element to TF32 (nearest even) on load.
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, 2, const_cast<float*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+}  // namespace
+}  // namespace mxb
