@@ -308,11 +308,54 @@ def time_allgather(out_d, world, m_total, stream, warmup, steps, max_over_ranks)
     ms = max_over_ranks(e0.elapsed_time(e1) / steps)
     total_bytes = 4.0 * m_total * N
     recv = total_bytes - 4.0 * M * N
-    del full
     return {"ms_per_step": ms, "bytes_gathered": int(total_bytes), "bytes_received_per_gpu": int(recv),
             "algbw_GBs": total_bytes / (ms * 1e-3) / 1e9,
             "busbw_GBs": total_bytes * (world - 1) / world / (ms * 1e-3) / 1e9,
-            "collective": "torch.distributed all_gather_into_tensor (NCCL)", "in_value": False}
+            "collective": "torch.distributed all_gather_into_tensor (NCCL)", "in_value": False}, full
+
+
+def time_fused_allgather(lib, ctx, local_rank, A_d, B_d, steps_arr, r0, M, N, K, m_total, prec, stream, warmup,
+                         steps, max_over_ranks, ref_full):
+    """The fused form of the same gather: each step is one
+    mxb_fused_gemm_allgather (the kernel writes this rank's rows into every
+    rank's full buffer over NVLink) plus the one-element all-reduce a reader
+    needs before it reads peer rows.  Mean CUDA-event time per step, max over
+    ranks; the full buffer is compared bit for bit with the NCCL gather of
+    the separately computed rows."""
+    import torch
+    import torch.distributed as dist
+
+    from minixla_b200 import lib as mlib
+    from minixla_b200.peer_gather import GatherBuffers
+
+    gb = GatherBuffers(lib, local_rank, m_total, N)
+    try:
+        def step():
+            rc = gb.gemm(ctx, A_d.data_ptr(), K, B_d.data_ptr(), N, r0, M, N, K, steps_arr, 2, prec,
+                         stream.cuda_stream)
+            if rc != 0:
+                raise RuntimeError(f"mxb_fused_gemm_allgather failed: {mlib.last_error()}")
+            gb.barrier(stream)
+
+        for _ in range(max(1, warmup)):
+            step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        pushes0 = lib.mxb_gather_push_count()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+        in_kernel = max_over_ranks(0.0 if lib.mxb_gather_push_count() - pushes0 == steps else 1.0) == 0.0
+        exact = max_over_ranks(0.0 if torch.equal(gb.tensor(), ref_full) else 1.0) == 0.0
+    finally:
+        gb.close()
+    return {"ms_per_step": ms, "rows_written_by_kernel": in_kernel, "bit_equal_to_nccl_gather": exact,
+            "form": "mxb_fused_gemm_allgather: epilogue stores to CUDA-IPC peer buffers over NVLink, "
+                    "+ one-element NCCL all-reduce per step"}
 
 
 def traffic_from_profile(precision: str, m: int):
@@ -426,9 +469,14 @@ def ours_arm(args, rank, local_rank, world):
     # the row-sharded job only needs it when a consumer wants the full tensor.
     allgather = None
     if world > 1:
-        allgather = time_allgather(out_d, world, m_total, stream, args.warmup, args.steps, max_over_ranks)
+        allgather, gathered = time_allgather(out_d, world, m_total, stream, args.warmup, args.steps, max_over_ranks)
         allgather["kernel_plus_allgather_tflops"] = flops_job / (
             (total_ms / args.steps + allgather["ms_per_step"]) * 1e-3) / 1e12
+        fused = time_fused_allgather(lib, ctx, local_rank, A_d, B_d, steps, r0, M, N, K, m_total, prec, stream,
+                                     args.warmup, args.steps, max_over_ranks, gathered)
+        fused["kernel_plus_allgather_tflops"] = flops_job / (fused["ms_per_step"] * 1e-3) / 1e12
+        allgather["fused"] = fused
+        del gathered
 
     # spot check of this rank's result against the oracle on a few rows
     from oracle.bindings import fused_oracle

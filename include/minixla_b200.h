@@ -264,6 +264,49 @@ MXB_API int mxb_fused_gemm_noalloc(const float* A, long long lda,
                                    const mxb_ep_step* steps, int n_steps,
                                    void* stream);
 
+/* ---- Row-sharded GEMM with the all-gather in the epilogue ---------------
+ * No counterpart in the reference (its GPU path is single-device).  With one
+ * process per GPU, GPU g owns rows r0..r1 of out = epi(A @ B); a consumer
+ * that needs the whole [M, N] tensor on every GPU would otherwise run an
+ * NCCL all-gather after the kernel.  mxb_fused_gemm_allgather computes this
+ * GPU's rows like mxb_fused_gemm into `out` (its rows of its own copy of the
+ * full output) and writes the same rows into every peer GPU's copy:
+ * peer_out[i] is where those rows start in peer i's copy (same ldo), a
+ * device pointer opened with mxb_ipc_open.  In TF32 mode on the CTA-pair
+ * kernel (M >= 256 with enough tiles to occupy the GPU) the epilogue warps
+ * store each finished tile to the peers over NVLink while the tensor cores
+ * run the next tile; every other kernel is followed by one strided copy per
+ * peer on the same stream.  Values are identical either way.  Peer rows are
+ * complete once the kernel has finished on the writing GPU: before reading
+ * rows that peers wrote, or writing a buffer a peer may still read,
+ * synchronise the ranks on the stream (for example a one-element NCCL
+ * all-reduce).  n_peers <= MXB_MAX_PEERS.  MINIXLA_GATHER_PUSH=0 forces the
+ * copy form. */
+#define MXB_MAX_PEERS 7
+#define MXB_IPC_HANDLE_BYTES 64
+MXB_API int mxb_fused_gemm_allgather(GpuCtx* ctx,
+                   const float* A, long long lda,
+                   const float* B, long long ldb,
+                   float* out, long long ldo,
+                   float* const* peer_out, int n_peers,
+                   int M, int N, int K,
+                   const mxb_ep_step* steps, int n_steps,
+                   int precision, void* stream);
+
+/* Device buffers shared between processes (CUDA IPC, no multicast object).
+ * mxb_ipc_alloc allocates `bytes` on `device` and returns the pointer and a
+ * handle that another process passes to mxb_ipc_open to map the same memory
+ * (peer access over NVLink).  Every process that opened a handle closes it
+ * (mxb_ipc_close) before the owner frees it (mxb_ipc_free). */
+MXB_API int mxb_ipc_alloc(int device, size_t bytes, void** dptr, unsigned char* handle);
+MXB_API int mxb_ipc_open(int device, const unsigned char* handle, void** dptr);
+MXB_API int mxb_ipc_close(int device, void* dptr);
+MXB_API int mxb_ipc_free(int device, void* dptr);
+
+/* Launches of mxb_fused_gemm_allgather whose kernel wrote the peer rows
+ * itself (the rest used copies), in this process. */
+MXB_API unsigned long long mxb_gather_push_count(void);
+
 /* Standalone element-wise nodes (tensor.c:64-86 and 110-120 semantics):
  * out[i] = a[i] + b[i % b_size]  and  out[i] = x[i] > 0 ? x[i] : 0. */
 MXB_API int mxb_add(GpuCtx* ctx, const float* a, long long n, const float* b, long long b_size,

@@ -392,6 +392,7 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.row_base = g.row_base;
     p.timeout_ns = g.timeout_ns;
     p.err = g.err;
+    if (g.n_peers > 0) return cudaErrorInvalidValue;  // only the TF32 CTA-pair kernel writes peer rows
     for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
 
     const int grid = p.num_tiles < g.num_sms ? p.num_tiles : g.num_sms;
@@ -448,12 +449,16 @@ bool pair_wide_tiles(const GemmLaunch& g) {
 
 }  // namespace
 
+bool fused_gemm_pushes_rows(const GemmLaunch& g) {
+    const char* v = getenv("MINIXLA_GATHER_PUSH");
+    if (v && v[0] == '0') return false;
+    return !g.A2 && g.precision == GPU_PRECISION_TF32 && use_pair_kernel(g);
+}
+
 cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
     if (g.A2) {
         // Two products of one A in one kernel (callers run other cases as two launches).
         if (g.precision == GPU_PRECISION_3XTF32) return launch_pair_3xtf32(g, true, stream);
-        // TF32: 256-column tiles put both accumulators in the 512 TMEM columns (one buffer,
-        // 48 KiB stages); 128-column tiles keep two buffers for problems with few tiles.
         if (g.precision != GPU_PRECISION_TF32) return cudaErrorInvalidValue;
         return launch_pair_tf32_dual(g, stream);
     }

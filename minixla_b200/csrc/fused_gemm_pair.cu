@@ -62,7 +62,10 @@ struct PairCfg {
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-template <int STAGES, int BN, bool DUAL, int EPI>
+// PUSH: the epilogue also writes each tile's rows into the peers' copies
+// (FusedParams::peer_out), a separate instance so the other launches keep
+// their registers.
+template <int STAGES, int BN, bool DUAL, int EPI, bool PUSH>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, DUAL, EPI>::kThreadsPerCta, 1)
     fused_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
@@ -292,9 +295,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                     apply_epilogue(v, row, col, row_ok, p);
                 if (row_ok) store_row_chunk(v, row, col, p);
             }
+            if (PUSH) {
+                // The accumulator is already released: these copies overlap the next tile's k-loop.
+                const int c_end = col0 + 32 * chunks < p.N ? col0 + 32 * chunks : p.N;
+                push_rows(p, mb * 256 + row_in_tile - lane, col0 + 32 * c_first, c_end);
+            }
             if (C::kBufs == 2) acc ^= 1;
             if (acc == 0) acc_phase ^= 1u;
         }
+        // Peer stores performed before the kernel counts as finished.
+        if (PUSH) __threadfence_system();
     }
 
     __syncwarp();
@@ -308,10 +318,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
 
 // ------------------------------------------------------------------ host side
 
-template <int STAGES, int BN, bool DUAL, int EPI = 4>
+template <int STAGES, int BN, bool DUAL, int EPI = 4, bool PUSH = false>
 cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
     using C = PairCfg<STAGES, BN, DUAL, EPI>;
-    auto kernel = fused_gemm_pair_kernel<STAGES, BN, DUAL, EPI>;
+    auto kernel = fused_gemm_pair_kernel<STAGES, BN, DUAL, EPI, PUSH>;
     static std::mutex mu;
     static uint64_t configured = 0;
     static int max_clusters[64] = {0};
@@ -384,6 +394,18 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.timeout_ns = g.timeout_ns;
     p.err = g.err;
     for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
+    if (PUSH != (g.n_peers > 0)) return cudaErrorInvalidValue;
+    if (PUSH) {
+        if (DUAL || g.n_peers > kMaxPeers || !g.peer_out) return cudaErrorInvalidValue;
+        bool vec = (g.ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(g.out) & 15) == 0;
+        for (int i = 0; i < g.n_peers; ++i) {
+            if (!g.peer_out[i]) return cudaErrorInvalidValue;
+            p.peer_out[i] = g.peer_out[i];
+            vec = vec && (reinterpret_cast<uintptr_t>(g.peer_out[i]) & 15) == 0;
+        }
+        p.n_peers = g.n_peers;
+        p.push_vec = vec ? 1 : 0;
+    }
 
     const int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;
     kernel<<<2 * pairs, C::kThreadsPerCta, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p);
@@ -394,6 +416,9 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_pair_tf32(const GemmLaunch& g, bool wide_tiles, cudaStream_t stream) {
+    if (g.n_peers > 0)
+        return wide_tiles ? run_pair_variant<4, 512, false, 4, true>(g, stream)
+                          : run_pair_variant<6, 256, false, 4, true>(g, stream);
     return wide_tiles ? run_pair_variant<4, 512, false>(g, stream) : run_pair_variant<6, 256, false>(g, stream);
 }
 

@@ -404,6 +404,7 @@ cudaError_t run_pair3_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.row_base = g.row_base;
     p.timeout_ns = g.timeout_ns;
     p.err = g.err;
+    if (g.n_peers > 0) return cudaErrorInvalidValue;  // only the TF32 CTA-pair kernel writes peer rows
     for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
 
     const int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;

@@ -47,6 +47,12 @@ struct FusedParams {
     unsigned long long timeout_ns;
     int* err;
     EpStepDev steps[MXB_MAX_EPILOGUE];
+    // Row all-gather (TF32 CTA-pair kernel only): the same rows of `out` in
+    // each peer GPU's copy of the full output (same ldo), written by the
+    // epilogue warps once their tile is stored locally.
+    float* peer_out[kMaxPeers];
+    int n_peers;
+    int push_vec;                   // 16-byte aligned bases and ldo % 4 == 0: float4 copies
 };
 
 // Error bits written to the device error word.
@@ -209,6 +215,60 @@ __device__ __forceinline__ void store_row_chunk(const float (&v)[W], int row, in
 #pragma unroll
         for (int i = 0; i < W; ++i)
             if (col + i < p.N) dst[i] = v[i];
+    }
+}
+
+// Copies rows row0 .. row0 + 31 (those below M), columns c0 .. c1, of the
+// output into every peer's copy.  The calling warp stored these rows just
+// before (lane i row row0 + i), so __syncwarp orders those stores before the
+// loads, which hit L2.  One instruction moves 512 contiguous bytes of a row;
+// four rows are in flight at a time.  The stores are plain global stores to
+// peer addresses (NVLink), so this warp's cost is issue only while the link
+// drains, and it runs while the MMA warp is already on the next tile.
+__device__ __forceinline__ void push_rows(const FusedParams& p, int row0, int c0, int c1) {
+    __syncwarp();
+    const int lane = threadIdx.x & 31;
+    const int rows = min(32, p.M - row0);
+    if (rows <= 0 || c0 >= c1) return;
+    constexpr int kU = 4;
+    if (p.push_vec) {
+        // c0 is a multiple of 32, so every float4 below is 16-byte aligned.
+        const int segs = (c1 - c0 + 127) / 128;  // 128-column segments per row
+        const int items = rows * segs;
+        for (int i0 = 0; i0 < items; i0 += kU) {
+            float4 v[kU];
+            long long off[kU];
+            int col[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const int i = i0 + u;
+                const int r = i / segs;
+                col[u] = c0 + (i - r * segs) * 128 + 4 * lane;
+                if (i >= items) col[u] = c1;  // nothing to copy
+                off[u] = static_cast<long long>(row0 + r) * p.ldo + col[u];
+                if (col[u] + 4 <= c1) v[u] = *reinterpret_cast<const float4*>(p.out + off[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                if (col[u] + 4 <= c1) {
+                    for (int q = 0; q < p.n_peers; ++q) *reinterpret_cast<float4*>(p.peer_out[q] + off[u]) = v[u];
+                } else {
+                    // Row tail when N % 4 != 0: at most three scalars.
+                    for (int j = 0; col[u] + j < c1; ++j) {
+                        const float x = p.out[off[u] + j];
+                        for (int q = 0; q < p.n_peers; ++q) p.peer_out[q][off[u] + j] = x;
+                    }
+                }
+            }
+        }
+    } else {
+        for (int r = 0; r < rows; ++r) {
+            const long long base = static_cast<long long>(row0 + r) * p.ldo;
+            for (int c = c0 + lane; c < c1; c += 32) {
+                const float x = p.out[base + c];
+                for (int q = 0; q < p.n_peers; ++q) p.peer_out[q][base + c] = x;
+            }
+        }
     }
 }
 

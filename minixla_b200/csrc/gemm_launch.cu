@@ -57,7 +57,7 @@ static bool dual_in_one_kernel(const GpuCtx* ctx, const float* A, long long lda,
 int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
                 long long ldo, int M, int N, int K, const EpStepDev* steps, int n_steps, int precision,
                 cudaStream_t stream, const float* B_small_pre, long long row_base,
-                const Product* prod, int choice_rows) {
+                const Product* prod, int choice_rows, PeerRows* peers) {
     const int rows_for_choice = choice_rows > 0 ? choice_rows : M;
     if (prod && !dual_in_one_kernel(ctx, A, lda, M, N, K, *prod, precision)) {
         // Two launches: the second product into pooled workspace, then the
@@ -129,6 +129,10 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
     g.err = ctx->d_err;
     g.timeout_ns = ctx->timeout_ns;
     g.num_sms = ctx->num_sms;
+    if (peers && peers->n > 0 && !prod && fused_gemm_pushes_rows(g)) {
+        g.peer_out = peers->out;
+        g.n_peers = peers->n;
+    }
     float* ws[3] = {nullptr, nullptr, nullptr};
     int rc = MXB_OK;
     if (precision == GPU_PRECISION_3XTF32) {
@@ -154,6 +158,7 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
         }
     }
     if (rc == MXB_OK && !cuda_ok(launch_fused_gemm(g, stream), "fused GEMM launch")) rc = MXB_E_CUDA;
+    if (rc == MXB_OK && g.n_peers > 0) peers->pushed = true;
     for (float* w : ws) ctx->pool->release(w, stream);
     return rc;
 }

@@ -21,6 +21,10 @@ struct EpStepDev {
 static_assert(sizeof(EpStepDev) == sizeof(mxb_ep_step), "EpStepDev must mirror mxb_ep_step");
 
 // Everything a fused-GEMM launch needs besides the tensor maps.
+// Peer copies of a row all-gather that the TF32 CTA-pair kernel writes itself
+// (one process per GPU on one NVLink domain: at most eight GPUs).
+constexpr int kMaxPeers = MXB_MAX_PEERS;
+
 struct GemmLaunch {
     const float* A; long long lda;     // M x K, lda % 4 == 0
     const float* B; long long ldb;     // K x N, ldb % 4 == 0
@@ -38,6 +42,8 @@ struct GemmLaunch {
     int* err;                          // device error word
     unsigned long long timeout_ns;
     int num_sms;
+    float* const* peer_out;            // n_peers > 0: also write the rows here (TF32 CTA-pair kernel only)
+    int n_peers;
 };
 
 // Skinny GEMM (skinny_gemm.cu): few output rows, CUDA-core fp32, split over
@@ -69,6 +75,9 @@ cudaError_t launch_tiny_gemm(const float* A, long long lda, const float* B, long
 
 // Kernel launchers (fused_gemm.cu, elementwise.cu).  Return cudaError_t.
 cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream);
+// Whether launch_fused_gemm(g) runs the TF32 CTA-pair kernel for one product,
+// the kernel that writes peer rows itself (MINIXLA_GATHER_PUSH=0: never).
+bool fused_gemm_pushes_rows(const GemmLaunch& g);
 cudaError_t launch_split_tf32(const float* x, long long rows, long long cols, long long ld_in,
                               float* small, long long ld_out, int num_sms, cudaStream_t stream);
 cudaError_t launch_add(const float* a, long long n, const float* b, long long b_size, float* out,

@@ -57,6 +57,7 @@ namespace mxb {
 // ---------------------------------------------------------------- errors, counters
 
 static std::atomic<unsigned long long> g_launches{0};
+static std::atomic<unsigned long long> g_gather_pushes{0};  // all-gathers written by the kernel itself
 static thread_local std::string t_last_error;
 
 void note_launch(unsigned n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
@@ -480,16 +481,18 @@ Tensor* gpu_run_fused(const Node* fused, const char* ptx) {
     return r;
 }
 
-int mxb_fused_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
-                   long long ldo, int M, int N, int K, const mxb_ep_step* steps, int n_steps, int precision,
-                   void* stream) {
+// Argument checks shared by mxb_fused_gemm and mxb_fused_gemm_allgather, then
+// the launch (with peer rows when `peers` is given).
+static int fused_gemm_checked(const char* fn, GpuCtx* ctx, const float* A, long long lda, const float* B,
+                              long long ldb, float* out, long long ldo, int M, int N, int K, const mxb_ep_step* steps,
+                              int n_steps, int precision, void* stream, mxb::PeerRows* peers) {
     if (!ctx || !A || !B || !out || M < 1 || N < 1 || K < 1 || lda < K || ldb < N || ldo < N ||
         n_steps < 0 || n_steps > MXB_MAX_EPILOGUE || (n_steps > 0 && !steps) || !mxb::valid_precision(precision)) {
-        set_error("mxb_fused_gemm: invalid arguments");
+        set_error("%s: invalid arguments", fn);
         return MXB_E_ARG;
     }
     if (lda % 4 || ldb % 4 || (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15)) {
-        set_error("mxb_fused_gemm: A and B need 16-byte aligned bases and row pitches (lda %% 4 == 0, ldb %% 4 == 0)");
+        set_error("%s: A and B need 16-byte aligned bases and row pitches (lda %% 4 == 0, ldb %% 4 == 0)", fn);
         return MXB_E_ARG;
     }
     mxb::EpStepDev dev_steps[MXB_MAX_EPILOGUE];
@@ -498,14 +501,58 @@ int mxb_fused_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, l
         const bool is_add = s.kind == MXB_EP_ADD_FULL || s.kind == MXB_EP_ADD_ROW || s.kind == MXB_EP_ADD_MOD;
         if (s.kind < MXB_EP_ADD_FULL || s.kind > MXB_EP_SCALE || (is_add && !s.operand) ||
             (s.kind == MXB_EP_ADD_FULL && s.ld_or_size < N) || (s.kind == MXB_EP_ADD_MOD && s.ld_or_size < 1)) {
-            set_error("mxb_fused_gemm: invalid epilogue step %d", i);
+            set_error("%s: invalid epilogue step %d", fn, i);
             return MXB_E_ARG;
         }
         memcpy(&dev_steps[i], &s, sizeof(s));
     }
     mxb::DeviceScope scope(ctx->device);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
-    return mxb::launch_gemm(ctx, A, lda, B, ldb, out, ldo, M, N, K, dev_steps, n_steps, precision, st);
+    return mxb::launch_gemm(ctx, A, lda, B, ldb, out, ldo, M, N, K, dev_steps, n_steps, precision, st, nullptr, 0,
+                            nullptr, 0, peers);
+}
+
+int mxb_fused_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
+                   long long ldo, int M, int N, int K, const mxb_ep_step* steps, int n_steps, int precision,
+                   void* stream) {
+    return fused_gemm_checked("mxb_fused_gemm", ctx, A, lda, B, ldb, out, ldo, M, N, K, steps, n_steps, precision,
+                              stream, nullptr);
+}
+
+int mxb_fused_gemm_allgather(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
+                             long long ldo, float* const* peer_out, int n_peers, int M, int N, int K,
+                             const mxb_ep_step* steps, int n_steps, int precision, void* stream) {
+    if (n_peers < 0 || n_peers > MXB_MAX_PEERS || (n_peers > 0 && !peer_out)) {
+        set_error("mxb_fused_gemm_allgather: n_peers must be 0..%d with a pointer per peer", MXB_MAX_PEERS);
+        return MXB_E_ARG;
+    }
+    for (int i = 0; i < n_peers; ++i) {
+        if (!peer_out[i] || peer_out[i] == out) {
+            set_error("mxb_fused_gemm_allgather: peer_out[%d] is null or the local output", i);
+            return MXB_E_ARG;
+        }
+    }
+    mxb::PeerRows peers;
+    peers.out = peer_out;
+    peers.n = n_peers;
+    int rc = fused_gemm_checked("mxb_fused_gemm_allgather", ctx, A, lda, B, ldb, out, ldo, M, N, K, steps, n_steps,
+                                precision, stream, &peers);
+    if (rc != MXB_OK || n_peers == 0) return rc;
+    if (peers.pushed) {
+        mxb::g_gather_pushes.fetch_add(1, std::memory_order_relaxed);
+        return MXB_OK;
+    }
+    // The kernel wrote only local rows: one strided copy per peer (copy
+    // engines over NVLink), ordered after it on the same stream.
+    mxb::DeviceScope scope(ctx->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : ctx->stream;
+    for (int i = 0; i < n_peers; ++i) {
+        if (!mxb::cuda_ok(cudaMemcpy2DAsync(peer_out[i], ldo * 4, out, ldo * 4, static_cast<size_t>(N) * 4, M,
+                                            cudaMemcpyDeviceToDevice, st),
+                          "peer row copy"))
+            return MXB_E_CUDA;
+    }
+    return MXB_OK;
 }
 
 int mxb_fused_gemm2(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, const float* A2,
@@ -583,6 +630,8 @@ int mxb_selftest_wait_timeout(GpuCtx* ctx, unsigned long long timeout_ns) {
 }
 
 unsigned long long mxb_launch_count(void) { return mxb::g_launches.load(); }
+
+unsigned long long mxb_gather_push_count(void) { return mxb::g_gather_pushes.load(); }
 
 const char* mxb_last_error(void) { return mxb::t_last_error.c_str(); }
 

@@ -283,10 +283,17 @@ bool tma_operand(GpuCtx* ctx, const float* src, long long rows, long long cols, 
 // row-streamed and sharded executors pass the node's full row count, so a
 // node gets the same arithmetic (tensor-core or CUDA-core fp32) however its
 // rows are split.
+// `peers` (mxb_fused_gemm_allgather): peer copies of the output rows, handed
+// to the kernel when it is one that writes them itself (`pushed` set).
+struct PeerRows {
+    float* const* out = nullptr;
+    int n = 0;
+    bool pushed = false;
+};
 int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out, long long ldo,
                 int M, int N, int K, const EpStepDev* steps, int n_steps, int precision, cudaStream_t stream,
                 const float* B_small_pre = nullptr, long long row_base = 0, const Product* prod = nullptr,
-                int choice_rows = 0);
+                int choice_rows = 0, PeerRows* peers = nullptr);
 int build_epilogue(const Node* n, int M, int N, long long batch, long long bt,
                    const std::unordered_map<const Node*, const float*>& dev_of,
                    const std::unordered_map<const Node*, long long>& size_of, EpStepDev* out,

@@ -20,6 +20,8 @@ GPU_PRECISION_3XTF32 = 3
 MXB_EP_ADD_FULL, MXB_EP_ADD_ROW, MXB_EP_ADD_MOD, MXB_EP_RELU, MXB_EP_SCALE, MXB_EP_ADD_PRODUCT = range(6)
 MXB_OK, MXB_E_ARG, MXB_E_CUDA, MXB_E_NOMEM, MXB_E_TIMEOUT, MXB_E_UNSUPPORTED = 0, -1, -2, -3, -4, -5
 MXB_MAX_EPILOGUE = 16
+MXB_MAX_PEERS = 7
+MXB_IPC_HANDLE_BYTES = 64
 
 # Every symbol the header declares, with (restype, argtypes).
 PROTOTYPES = {
@@ -56,6 +58,16 @@ PROTOTYPES = {
         [C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong,
          C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_void_p],
     ),
+    "mxb_fused_gemm_allgather": (
+        C.c_int,
+        [C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong,
+         C.POINTER(C.c_void_p), C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p],
+    ),
+    "mxb_ipc_alloc": (C.c_int, [C.c_int, C.c_size_t, C.POINTER(C.c_void_p), C.POINTER(C.c_ubyte)]),
+    "mxb_ipc_open": (C.c_int, [C.c_int, C.POINTER(C.c_ubyte), C.POINTER(C.c_void_p)]),
+    "mxb_ipc_close": (C.c_int, [C.c_int, C.c_void_p]),
+    "mxb_ipc_free": (C.c_int, [C.c_int, C.c_void_p]),
+    "mxb_gather_push_count": (C.c_ulonglong, []),
     "mxb_add": (C.c_int, [C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]),
     "mxb_relu": (C.c_int, [C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]),
     "mxb_check_device_error": (C.c_int, [C.c_void_p]),
