@@ -5,7 +5,7 @@ CPU (gloo, world size 2): the host-side plumbing against a fake library --
 handle exchange, peer addresses in rank order, the arguments of the launch,
 unmap-before-free on close.
 
-GPU (two processes on two GPUs, NCCL): every rank's full buffer after the
+GPU (one process per visible GPU, up to eight, NCCL): every rank's full buffer after the
 fused gather must equal, bit for bit, the NCCL all-gather of the same
 shards computed by mxb_fused_gemm, and sampled rows must match the oracle.
 Covers the in-kernel push (256 x 256 and 256 x 512 pair tiles, float4 and
@@ -223,8 +223,8 @@ def _ngpu():
 
 @pytest.mark.gpu
 @pytest.mark.skipif(_ngpu() < 2, reason="needs at least two GPUs")
-def test_fused_allgather_two_gpus():
-    world, port = 2, _free_port()
+def test_fused_allgather_all_gpus():
+    world, port = min(_ngpu(), 8), _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     procs = [ctx.Process(target=_gpu_worker, args=(r, world, port, q)) for r in range(world)]
