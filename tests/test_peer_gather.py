@@ -123,17 +123,19 @@ def test_gather_buffers_host_logic_gloo():
         assert calls[4] == ("free", rank, own_addr)
 
 
-# ---------------------------------------------------------------- GPU: two processes, two GPUs
+# ---------------------------------------------------------------- GPU: one process per GPU
 
-# (M_total, N, K, precision, MINIXLA_GATHER_PUSH, expect the in-kernel push)
+# (rows per rank, extra rows, N, K, precision, MINIXLA_GATHER_PUSH, expect the
+# in-kernel push): M = rows per rank x ranks + extra, so every rank runs the
+# same kernel family whatever the GPU count.
 GPU_CASES = [
-    (4096, 2048, 256, 1, "1", True),     # 256 x 256 pair tiles, float4 copies
-    (8192, 4096, 128, 1, "1", True),     # 256 x 512 pair tiles
-    (4097, 2047, 200, 1, "1", True),     # uneven shards, odd pitch: scalar copies, K tail
-    (4096, 2048, 256, 1, "0", False),    # copy form forced
-    (4096, 2048, 256, 3, "1", False),    # 3xTF32: copy form
-    (200, 96, 64, 1, "1", False),        # single-CTA kernel
-    (16, 512, 256, 1, "1", False),       # 8 rows per rank: skinny kernel
+    (2048, 0, 2048, 256, 1, "1", True),    # 256 x 256 pair tiles, float4 copies
+    (4096, 0, 4096, 128, 1, "1", True),    # 256 x 512 pair tiles
+    (2048, 1, 2047, 200, 1, "1", True),    # uneven shards, odd pitch: scalar copies, K tail
+    (2048, 0, 2048, 256, 1, "0", False),   # copy form forced
+    (2048, 0, 2048, 256, 3, "1", False),   # 3xTF32: copy form
+    (100, 0, 96, 64, 1, "1", False),       # single-CTA kernel
+    (8, 0, 512, 256, 1, "1", False),       # skinny kernel
 ]
 
 
@@ -155,7 +157,8 @@ def _gpu_worker(rank, world, port, q):
         assert ctx, mlib.last_error()
         stream = torch.cuda.Stream(dev)
         results = []
-        for (M, N, K, prec, push_env, _) in GPU_CASES:
+        for (per_rank, extra, N, K, prec, push_env, _) in GPU_CASES:
+            M = per_rank * world + extra
             os.environ["MINIXLA_GATHER_PUSH"] = push_env
             r0, r1 = C.c_longlong(), C.c_longlong()
             assert lib.mxb_shard_rows(M, world, rank, C.byref(r0), C.byref(r1)) == 0
@@ -240,7 +243,7 @@ def test_fused_allgather_all_gpus():
     for rank in range(world):
         res = out[rank]
         assert isinstance(res, list), res
-        for r, (M, N, K, prec, push_env, expect_push) in zip(res, GPU_CASES):
+        for r, (_, _, N, K, prec, push_env, expect_push) in zip(res, GPU_CASES):
             assert r["exact"], r
             assert r["err"] <= (2e-3 if prec == 1 else 1e-5), r
             assert r["pushed"] == (1 if expect_push else 0), r
