@@ -64,12 +64,18 @@ struct Cfg {
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-template <int BN, int STAGES, bool SPLIT3, bool SEG>
+// KSPLIT: tile t is a K slice of output tile t / p.splits; each epilogue warp
+// writes its rows' raw slice to workspace, and the warp whose slice lands
+// last (per-tile, per-quadrant counter) sums the slices in slice order and
+// applies the epilogue.  No barrier across warps or CTAs, so no wait can
+// block on another CTA.
+template <int BN, int STAGES, bool SPLIT3, bool SEG, bool KSPLIT = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fused_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                       const __grid_constant__ FusedParams p) {
     using C = Cfg<BN, STAGES, SPLIT3>;
+    static_assert(!(KSPLIT && (SPLIT3 || SEG)), "K split is a TF32 form");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -124,9 +130,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
                 int mb, nb;
-                tile_coords(t, p, mb, nb);
+                int kb_lo = 0, kb_hi = p.num_kb;
+                if (KSPLIT) {
+                    tile_coords(t / p.splits, p, mb, nb);
+                    kb_lo = (t % p.splits) * p.kb_per_split;
+                    kb_hi = min(p.num_kb, kb_lo + p.kb_per_split);
+                } else {
+                    tile_coords(t, p, mb, nb);
+                }
                 const int m0 = mb * kBM, n0 = nb * BN;
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb = kb_lo; kb < kb_hi; ++kb) {
                     if (*abort_flag) { ok = false; break; }
                     if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.timeout_ns)) {
                         raise_error(p, abort_flag, kErrProducer);
@@ -174,8 +187,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t acc_phase = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-                for (int k_begin = 0; k_begin < p.num_kb && ok; k_begin += p.seg_kb) {
-                    const int k_end = min(p.num_kb, k_begin + p.seg_kb);
+                int kb_lo = 0, kb_hi = p.num_kb;
+                if (KSPLIT) {
+                    kb_lo = (t % p.splits) * p.kb_per_split;
+                    kb_hi = min(p.num_kb, kb_lo + p.kb_per_split);
+                }
+                for (int k_begin = kb_lo; k_begin < kb_hi && ok; k_begin += p.seg_kb) {
+                    const int k_end = min(kb_hi, k_begin + p.seg_kb);
                     if (*abort_flag) { ok = false; break; }
                     if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns)) {
                         raise_error(p, abort_flag, kErrMma);
@@ -235,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t acc_phase = 0;
         for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
             int mb, nb;
-            tile_coords(t, p, mb, nb);
+            tile_coords(KSPLIT ? t / p.splits : t, p, mb, nb);
             const int row = mb * kBM + row_in_tile;
             const bool row_ok = row < p.M;
             const int col0 = nb * BN;
@@ -243,11 +261,65 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (chunks > BN / 32) chunks = BN / 32;
             const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
             bool failed = false;
-            if (row_ok) {
+            if (!KSPLIT && row_ok) {
                 // Short k-loops: fetch C while the MMAs run; long ones: just before the drain.
                 if (p.num_kb <= kShortKb) prefetch_full_operands(row, col0, min(BN, p.N - col0), p);
             }
-            if (SEG) {
+            if (KSPLIT) {
+                // Short slices: fetch C while the MMAs run (whichever CTA of the tile ends last reads it).
+                if (row_ok) prefetch_full_operands(row, col0, min(BN, p.N - col0), p);
+                const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
+                const bool got = !stop && mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns);
+                if (!__all_sync(0xffffffffu, got)) {
+                    if (lane == 0 && !stop) raise_error(p, abort_flag, kErrEpilogue);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * BN);
+                float* slice = p.ks_ws + static_cast<long long>(t % p.splits) * p.ks_stride +
+                               static_cast<long long>(row) * p.ks_ld;
+                for (int c = 0; c < chunks; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + 32 * c, r);
+                    tmem_ld_wait();
+                    if (c == chunks - 1) {
+                        tc_fence_before();
+                        mbar_arrive(tempty_bar(acc));
+                    }
+                    if (row_ok) store_partial(r, slice + col0 + 32 * c, col0 + 32 * c, p.N);
+                }
+                // Slice stored: count it; the warp that brings the count to
+                // p.splits finishes these 32 rows of the tile.
+                __threadfence();
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) {
+                    int* cnt = p.ks_counters + 4 * (t / p.splits) + quad;
+                    last = atomicAdd(cnt, 1) == p.splits - 1;
+                    if (last) {
+                        *cnt = 0;  // zero again for the next launch on this workspace
+                        __threadfence();
+                    }
+                }
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    __syncwarp();  // lane 0 saw every slice counted: order the loads after it
+                    for (int c = 0; c < chunks; ++c) {
+                        const int col = col0 + 32 * c;
+                        float v[32];
+                        if (row_ok) {
+                            sum_partials(v, p, row, col);
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+                        }
+                        apply_epilogue(v, row, col, row_ok, p);
+                        if (row_ok) store_row_chunk(v, row, col, p);
+                    }
+                }
+                acc ^= 1;
+                if (acc == 0) acc_phase ^= 1u;
+            } else if (SEG) {
                 // Sum the K segments in registers (fp32, round to nearest), 16
                 // columns at a time.  After the last segment the totals go back
                 // into that accumulator and the epilogue reads them from there,
@@ -341,10 +413,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------------ host side
 
-template <int BN, int STAGES, bool SPLIT3, bool SEG>
+template <int BN, int STAGES, bool SPLIT3, bool SEG, bool KSPLIT = false>
 cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     using C = Cfg<BN, STAGES, SPLIT3>;
-    auto kernel = fused_gemm_kernel<BN, STAGES, SPLIT3, SEG>;
+    auto kernel = fused_gemm_kernel<BN, STAGES, SPLIT3, SEG, KSPLIT>;
     // The shared-memory opt-in is per device: remember which devices have it.
     static std::mutex mu;
     static uint64_t configured = 0;
@@ -394,6 +466,22 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.err = g.err;
     if (g.n_peers > 0) return cudaErrorInvalidValue;  // only the TF32 CTA-pair kernel writes peer rows
     for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
+    p.splits = 1;
+    p.kb_per_split = p.num_kb;
+    if (KSPLIT) {
+        static_assert(!KSPLIT || (BN == kKsplitTileCols && kBM == kKsplitTileRows), "K-split tile");
+        if (g.k_splits < 2 || !g.ks_ws || !g.ks_counters) return cudaErrorInvalidValue;
+        // Whole k-blocks per slice and no empty slice: splits <= k_splits.
+        p.kb_per_split = (p.num_kb + g.k_splits - 1) / g.k_splits;
+        p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
+        p.num_tiles *= p.splits;
+        p.ks_ws = g.ks_ws;
+        p.ks_ld = (g.N + 3) / 4 * 4;
+        p.ks_stride = static_cast<long long>(g.M) * p.ks_ld;
+        p.ks_counters = g.ks_counters;
+    } else if (g.k_splits > 1) {
+        return cudaErrorInvalidValue;
+    }
 
     const int grid = p.num_tiles < g.num_sms ? p.num_tiles : g.num_sms;
     kernel<<<grid, kThreads, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p);
@@ -449,6 +537,44 @@ bool pair_wide_tiles(const GemmLaunch& g) {
 
 }  // namespace
 
+// K split of the single-CTA TF32 kernel on 128 x 128 tiles: when those tiles
+// would fill at most half the SMs and K is long, up to four CTAs share each
+// tile's k-loop.  The slices' round trip through L2 and the final sum cost
+// tens of microseconds per tile, so the split pays only on long k-loops:
+// measured at K = 8192, (1024, 1024) 85 -> 68 us, (2048, 256) 81 -> 53 us,
+// (512, 512) 81 -> 51 us, (8192, 64) 81 -> 67 us, and (1024, 1024, 16384)
+// 155 -> 108 us; at K <= 4100 it lost to the unsplit narrow tiles
+// ((8191, 127, 3000) 44 -> 65 us), hence kKsplitMinKb, and so did
+// (8191, 127, 6200) (73 -> 83 us), hence the tile-width rule below.
+// The count follows the node's full row count (choice_rows), so a node run
+// in row chunks or shards gets the same sums.  MINIXLA_KSPLIT=0 turns it off,
+// =n forces n ways (2..8); MINIXLA_SINGLE_BN alone leaves K unsplit.
+constexpr int kKsplitMinKb = 192;  // K >= 6113
+
+int fused_gemm_k_splits(const GemmLaunch& g) {
+    if (g.precision != GPU_PRECISION_TF32 || g.A2 || g.n_peers > 0 || use_pair_kernel(g)) return 1;
+    const long long rows = g.choice_rows > 0 ? g.choice_rows : g.M;
+    const long long tiles = ((rows + kKsplitTileRows - 1) / kKsplitTileRows) *
+                            ((g.N + kKsplitTileCols - 1) / kKsplitTileCols);
+    const int num_kb = (g.K + kBK - 1) / kBK;
+    // Unsplit, such a problem runs on 64- or 32-wide tiles.  The split pays
+    // when it replaces 32-wide tiles, or 64-wide ones on a wide N (which read
+    // every A row-block N / 64 times); 64-wide tiles of a narrow N already
+    // keep enough SMs busy and read A twice at most.
+    const long long tiles64 = ((rows + kKsplitTileRows - 1) / kKsplitTileRows) * ((g.N + 63) / 64);
+    const bool narrow_unsplit = 2 * tiles64 < g.num_sms || g.N >= 512;
+    int s = 1;
+    if (num_kb >= kKsplitMinKb && 2 * tiles <= g.num_sms && narrow_unsplit)
+        s = static_cast<int>(std::min<long long>(4, g.num_sms / tiles));
+    if (const char* v = getenv("MINIXLA_KSPLIT")) {
+        const int f = atoi(v);
+        if (f == 0 || f == 1) return 1;
+        if (f >= 2 && f <= 8) return std::min(f, num_kb);
+    }
+    if (getenv("MINIXLA_SINGLE_BN")) return 1;  // a forced tile width runs unsplit
+    return std::max(1, std::min(s, num_kb));
+}
+
 bool fused_gemm_pushes_rows(const GemmLaunch& g) {
     const char* v = getenv("MINIXLA_GATHER_PUSH");
     if (v && v[0] == '0') return false;
@@ -474,6 +600,7 @@ cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
     if (use_pair_kernel(g)) {
         return launch_pair_tf32(g, pair_wide_tiles(g), stream);
     }
+    if (g.k_splits > 1) return run_variant<128, 6, false, false, true>(g, stream);
     // One TF32 product on one CTA.  Narrower tiles for problems with few
     // tiles, so more SMs share the k-loops and the epilogue.
     switch (single_cta_width(g)) {

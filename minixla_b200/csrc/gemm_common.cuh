@@ -7,6 +7,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -53,6 +54,16 @@ struct FusedParams {
     float* peer_out[kMaxPeers];
     int n_peers;
     int push_vec;                   // 16-byte aligned bases and ldo % 4 == 0: float4 copies
+    // K split (single-CTA TF32 kernel, KSPLIT instances): tile t is output
+    // tile t / splits, k-blocks [s * kb_per_split, +kb_per_split) with
+    // s = t % splits.  Slice s of a tile goes raw to ks_ws + s * ks_stride
+    // (row pitch ks_ld); ks_counters holds one zeroed int per output tile and
+    // TMEM lane quadrant.
+    int splits;
+    int kb_per_split;
+    float* ks_ws;
+    long long ks_stride, ks_ld;
+    int* ks_counters;
 };
 
 // Error bits written to the device error word.
@@ -268,6 +279,61 @@ __device__ __forceinline__ void push_rows(const FusedParams& p, int row0, int c0
                 const float x = p.out[base + c];
                 for (int q = 0; q < p.n_peers; ++q) p.peer_out[q][base + c] = x;
             }
+        }
+    }
+}
+
+// Stores one row's 32 raw accumulator values (columns col .. col + 31, those
+// below n) at dst, 16-byte aligned when the chunk is whole.
+__device__ __forceinline__ void store_partial(const uint32_t (&r)[32], float* dst, int col, int n) {
+    if (col + 32 <= n) {
+        float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            __stcg(d4 + i, make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                       __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])));
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (col + i < n) __stcg(dst + i, __uint_as_float(r[i]));
+    }
+}
+
+// v = slice 0 + slice 1 + ... of one row's 32 columns (zero past N), in
+// slice order, read at L2 (other SMs wrote the slices during this launch).
+// One row per lane, as the accumulator comes out of TMEM: the 32 rows of a
+// warp are summed side by side.
+__device__ __forceinline__ void sum_partials(float (&v)[32], const FusedParams& p, int row, int col) {
+    const float* src = p.ks_ws + static_cast<long long>(row) * p.ks_ld + col;
+    if (col + 32 <= p.N) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 x = __ldcg(reinterpret_cast<const float4*>(src) + i);
+            v[4 * i] = x.x;
+            v[4 * i + 1] = x.y;
+            v[4 * i + 2] = x.z;
+            v[4 * i + 3] = x.w;
+        }
+        for (int s = 1; s < p.splits; ++s) {
+            const float4* s4 = reinterpret_cast<const float4*>(src + s * p.ks_stride);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float4 x = __ldcg(s4 + i);
+                v[4 * i] += x.x;
+                v[4 * i + 1] += x.y;
+                v[4 * i + 2] += x.z;
+                v[4 * i + 3] += x.w;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            float x = 0.0f;
+            if (col + i < p.N) {
+                x = __ldcg(src + i);
+                for (int s = 1; s < p.splits; ++s) x += __ldcg(src + s * p.ks_stride + i);
+            }
+            v[i] = x;
         }
     }
 }

@@ -44,6 +44,10 @@ struct GemmLaunch {
     int num_sms;
     float* const* peer_out;            // n_peers > 0: also write the rows here (TF32 CTA-pair kernel only)
     int n_peers;
+    int choice_rows;                   // rows the K split is chosen for (0: M)
+    int k_splits;                      // > 1: single-CTA TF32 kernel with K split this many ways
+    float* ks_ws;                      // k_splits * M * round4(N) floats
+    int* ks_counters;                  // 4 * output tiles ints, zero at launch
 };
 
 // Skinny GEMM (skinny_gemm.cu): few output rows, CUDA-core fp32, split over
@@ -78,6 +82,10 @@ cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream);
 // Whether launch_fused_gemm(g) runs the TF32 CTA-pair kernel for one product,
 // the kernel that writes peer rows itself (MINIXLA_GATHER_PUSH=0: never).
 bool fused_gemm_pushes_rows(const GemmLaunch& g);
+// How many ways launch_fused_gemm(g) splits K (1: none); the caller supplies
+// the workspace and zeroed counters that a split needs.
+int fused_gemm_k_splits(const GemmLaunch& g);
+constexpr int kKsplitTileRows = 128, kKsplitTileCols = 128;
 cudaError_t launch_split_tf32(const float* x, long long rows, long long cols, long long ld_in,
                               float* small, long long ld_out, int num_sms, cudaStream_t stream);
 cudaError_t launch_add(const float* a, long long n, const float* b, long long b_size, float* out,

@@ -348,16 +348,20 @@ def test_full_size_checksums(lib, gpu_ctx, precision):
 
 
 @pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
-@pytest.mark.parametrize("variant", ["pair", "pair512", "single", "single64", "single32"])
+@pytest.mark.parametrize("variant", ["pair", "pair512", "single", "single64", "single32", "ksplit3"])
 @pytest.mark.parametrize("mnk", [(256, 256, 32), (300, 520, 100), (1000, 1000, 1000), (257, 4097, 129),
                                  (8191, 127, 3000), (2048, 2048, 2048), (4096, 300, 1024), (640, 384, 4100)])
 def test_kernel_variants(lib, gpu_ctx, mnk, variant, precision, monkeypatch, host_threads):
     """Every kernel of each mode (CTA pair with 256- and, in TF32, 512-wide
-    tiles; single CTA with 128/256-, 64- and 32-wide tiles) on tile-edge shapes, with a full-matrix add, a bias
-    row and relu in the epilogue.  K = 4100 ends on a partial k-block and a
-    partial 3xTF32 segment."""
-    if variant == "pair512" and precision == X3:
-        pytest.skip("3xTF32 has one pair tile width")
+    tiles; single CTA with 128/256-, 64- and 32-wide tiles; in TF32 the
+    single-CTA kernel with K split three ways) on tile-edge shapes, with a
+    full-matrix add, a bias row and relu in the epilogue.  K = 4100 ends on a
+    partial k-block and a partial 3xTF32 segment."""
+    if variant in ("pair512", "ksplit3") and precision == X3:
+        pytest.skip("TF32-only kernel form")
+    if variant == "ksplit3":
+        monkeypatch.setenv("MINIXLA_KSPLIT", "3")
+        variant = "single"
     if variant.startswith("single") and variant != "single":
         monkeypatch.setenv("MINIXLA_SINGLE_BN", variant[len("single"):])
         variant = "single"
@@ -372,6 +376,37 @@ def test_kernel_variants(lib, gpu_ctx, mnk, variant, precision, monkeypatch, hos
     rows = None if M * N * K <= 2048 ** 3 else _sample_rows(M, 256)
     want = bindings.fused_oracle(A, B, [("add", C), ("relu",), ("add", bias)], rows=rows, threads=host_threads)
     check(got if rows is None else got[rows], want, precision, f"{variant} {mnk}")
+
+
+@pytest.mark.parametrize("mnk", [(2047, 250, 6200), (2048, 256, 8192), (1024, 1024, 8192)])
+def test_k_split(lib, gpu_ctx, mnk, monkeypatch, host_threads):
+    """TF32 shapes whose 128 x 128 tiles fill under half the SMs with a long
+    K (>= 192 k-blocks) run the single-CTA kernel with K split across CTAs
+    (here two and four ways; (2047, 250, 6200) ends on a partial row tile,
+    column tile and k-block): the result matches
+    the oracle, repeats bit for bit (the slices are summed in slice order
+    whichever CTA finishes last), equals the row-streamed executor's bit for
+    bit (the split follows the node's full row count), and stays within
+    tolerance of the unsplit kernel."""
+    M, N, K = mnk
+    A, B, C = _relu_abc(M, N, K, c_normal=True)
+    bias = datagen.normal((N,), 5, 0.0, 0.5)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A), hg.input_node(B),
+                         [(OP_ADD, hg.input_node(C)), (OP_RELU, None), (OP_ADD, hg.input_node(bias))])
+    monkeypatch.setenv("MINIXLA_STREAM_CHUNKS", "1")
+    got = run_execute(lib, gpu_ctx, root, TF32)
+    assert np.array_equal(got, run_execute(lib, gpu_ctx, root, TF32)), "K-split result not repeatable"
+    rows = _sample_rows(M, 256)
+    want = bindings.fused_oracle(A, B, [("add", C), ("relu",), ("add", bias)], rows=rows, threads=host_threads)
+    check(got[rows], want, TF32, f"k-split {mnk}")
+    monkeypatch.setenv("MINIXLA_STREAM_CHUNKS", "8")
+    assert np.array_equal(got, run_execute(lib, gpu_ctx, root, TF32)), "row-streamed K split differs"
+    monkeypatch.setenv("MINIXLA_STREAM_CHUNKS", "1")
+    monkeypatch.setenv("MINIXLA_KSPLIT", "0")
+    unsplit = run_execute(lib, gpu_ctx, root, TF32)
+    check(got, unsplit, TF32, f"k-split vs unsplit {mnk}")
+    assert not np.array_equal(got, unsplit), "same bits as the unsplit kernel: K was not split"
 
 
 @pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
