@@ -64,11 +64,9 @@ struct Cfg {
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-// KSPLIT: tile t is a K slice of output tile t / p.splits; each epilogue warp
-// writes its rows' raw slice to workspace, and the warp whose slice lands
-// last (per-tile, per-quadrant counter) sums the slices in slice order and
-// applies the epilogue.  No barrier across warps or CTAs, so no wait can
-// block on another CTA.
+// KSPLIT: tile t is a K slice of output tile t / p.splits; the epilogue warps
+// write the slice raw to workspace and ksplit_reduce_kernel, launched next,
+// sums the slices in slice order and applies the epilogue.
 template <int BN, int STAGES, bool SPLIT3, bool SEG, bool KSPLIT = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fused_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -266,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (p.num_kb <= kShortKb) prefetch_full_operands(row, col0, min(BN, p.N - col0), p);
             }
             if (KSPLIT) {
-                // Short slices: fetch C while the MMAs run (whichever CTA of the tile ends last reads it).
+                // Fetch C into L2 for the reduce kernel while the MMAs run.
                 if (row_ok) prefetch_full_operands(row, col0, min(BN, p.N - col0), p);
                 const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
                 const bool got = !stop && mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns);
@@ -287,35 +285,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         mbar_arrive(tempty_bar(acc));
                     }
                     if (row_ok) store_partial(r, slice + col0 + 32 * c, col0 + 32 * c, p.N);
-                }
-                // Slice stored: count it; the warp that brings the count to
-                // p.splits finishes these 32 rows of the tile.
-                __threadfence();
-                __syncwarp();
-                int last = 0;
-                if (lane == 0) {
-                    int* cnt = p.ks_counters + 4 * (t / p.splits) + quad;
-                    last = atomicAdd(cnt, 1) == p.splits - 1;
-                    if (last) {
-                        *cnt = 0;  // zero again for the next launch on this workspace
-                        __threadfence();
-                    }
-                }
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) {
-                    __syncwarp();  // lane 0 saw every slice counted: order the loads after it
-                    for (int c = 0; c < chunks; ++c) {
-                        const int col = col0 + 32 * c;
-                        float v[32];
-                        if (row_ok) {
-                            sum_partials(v, p, row, col);
-                        } else {
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) v[i] = 0.0f;
-                        }
-                        apply_epilogue(v, row, col, row_ok, p);
-                        if (row_ok) store_row_chunk(v, row, col, p);
-                    }
                 }
                 acc ^= 1;
                 if (acc == 0) acc_phase ^= 1u;
@@ -411,6 +380,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// Second kernel of a K-split launch: the slices summed in slice order, then
+// the node's epilogue.  Thread i takes four consecutive columns of one row,
+// so a warp reads 512 contiguous bytes of a slice row; every SM takes part.
+__global__ void __launch_bounds__(256) ksplit_reduce_kernel(const __grid_constant__ FusedParams p) {
+    const int groups = (p.N + 3) / 4;
+    const long long total = static_cast<long long>(p.M) * groups;
+    for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total; i += static_cast<long long>(gridDim.x) * 256) {
+        const int row = static_cast<int>(i / groups);
+        const int col = static_cast<int>(i - static_cast<long long>(row) * groups) * 4;
+        float v[4];
+        sum_slices4(v, p, row, col);
+        apply_epilogue<4>(v, row, col, true, p);
+        store_row_chunk<4>(v, row, col, p);
+    }
+}
+
 // ------------------------------------------------------------------ host side
 
 template <int BN, int STAGES, bool SPLIT3, bool SEG, bool KSPLIT = false>
@@ -470,7 +455,7 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.kb_per_split = p.num_kb;
     if (KSPLIT) {
         static_assert(!KSPLIT || (BN == kKsplitTileCols && kBM == kKsplitTileRows), "K-split tile");
-        if (g.k_splits < 2 || !g.ks_ws || !g.ks_counters) return cudaErrorInvalidValue;
+        if (g.k_splits < 2 || !g.ks_ws) return cudaErrorInvalidValue;
         // Whole k-blocks per slice and no empty slice: splits <= k_splits.
         p.kb_per_split = (p.num_kb + g.k_splits - 1) / g.k_splits;
         p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
@@ -478,7 +463,6 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
         p.ks_ws = g.ks_ws;
         p.ks_ld = (g.N + 3) / 4 * 4;
         p.ks_stride = static_cast<long long>(g.M) * p.ks_ld;
-        p.ks_counters = g.ks_counters;
     } else if (g.k_splits > 1) {
         return cudaErrorInvalidValue;
     }
@@ -486,6 +470,14 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     const int grid = p.num_tiles < g.num_sms ? p.num_tiles : g.num_sms;
     kernel<<<grid, kThreads, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p);
     note_launch();
+    if (KSPLIT) {
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        const long long items = static_cast<long long>(g.M) * ((g.N + 3) / 4);
+        const long long blocks = std::min<long long>((items + 255) / 256, 8ll * g.num_sms);
+        ksplit_reduce_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(p);
+        note_launch();
+    }
     return cudaGetLastError();
 }
 
@@ -538,18 +530,18 @@ bool pair_wide_tiles(const GemmLaunch& g) {
 }  // namespace
 
 // K split of the single-CTA TF32 kernel on 128 x 128 tiles: when those tiles
-// would fill at most half the SMs and K is long, up to four CTAs share each
-// tile's k-loop.  The slices' round trip through L2 and the final sum cost
-// tens of microseconds per tile, so the split pays only on long k-loops:
-// measured at K = 8192, (1024, 1024) 85 -> 68 us, (2048, 256) 81 -> 53 us,
-// (512, 512) 81 -> 51 us, (8192, 64) 81 -> 67 us, and (1024, 1024, 16384)
-// 155 -> 108 us; at K <= 4100 it lost to the unsplit narrow tiles
-// ((8191, 127, 3000) 44 -> 65 us), hence kKsplitMinKb, and so did
-// (8191, 127, 6200) (73 -> 83 us), hence the tile-width rule below.
-// The count follows the node's full row count (choice_rows), so a node run
-// in row chunks or shards gets the same sums.  MINIXLA_KSPLIT=0 turns it off,
-// =n forces n ways (2..8); MINIXLA_SINGLE_BN alone leaves K unsplit.
-constexpr int kKsplitMinKb = 192;  // K >= 6113
+// would fill at most half the SMs and K has at least 64 k-blocks, up to
+// min(4, SMs / tiles) CTAs share each tile's k-loop, and a reduce kernel sums
+// the slices.  Measured against the unsplit 64- / 32-wide tiles (TF32, held-
+// stream CUDA events): (8191, 127, 3000) 44.1 -> 41.5 us, (4096, 128, 2048)
+// 27.4 -> 21.4, (1024, 1024, 4096) 48.0 -> 37.7, (640, 384, 4100) 45.9 ->
+// 25.6, (2048, 256, 8192) 80.8 -> 37.3, (512, 512, 8192) 78.8 -> 33.8,
+// (1024, 1024, 16384) 156.7 -> 97.2; with 32 k-blocks ((1000)^3) it lost
+// (19.4 -> 21.4), hence kKsplitMinKb.  The count follows the node's full row
+// count (choice_rows), so a node run in row chunks or shards gets the same
+// sums.  MINIXLA_KSPLIT=0 turns it off, =n forces n ways (2..8);
+// MINIXLA_SINGLE_BN alone leaves K unsplit.
+constexpr int kKsplitMinKb = 64;  // K >= 2017
 
 int fused_gemm_k_splits(const GemmLaunch& g) {
     if (g.precision != GPU_PRECISION_TF32 || g.A2 || g.n_peers > 0 || use_pair_kernel(g)) return 1;
@@ -557,14 +549,8 @@ int fused_gemm_k_splits(const GemmLaunch& g) {
     const long long tiles = ((rows + kKsplitTileRows - 1) / kKsplitTileRows) *
                             ((g.N + kKsplitTileCols - 1) / kKsplitTileCols);
     const int num_kb = (g.K + kBK - 1) / kBK;
-    // Unsplit, such a problem runs on 64- or 32-wide tiles.  The split pays
-    // when it replaces 32-wide tiles, or 64-wide ones on a wide N (which read
-    // every A row-block N / 64 times); 64-wide tiles of a narrow N already
-    // keep enough SMs busy and read A twice at most.
-    const long long tiles64 = ((rows + kKsplitTileRows - 1) / kKsplitTileRows) * ((g.N + 63) / 64);
-    const bool narrow_unsplit = 2 * tiles64 < g.num_sms || g.N >= 512;
     int s = 1;
-    if (num_kb >= kKsplitMinKb && 2 * tiles <= g.num_sms && narrow_unsplit)
+    if (num_kb >= kKsplitMinKb && 2 * tiles <= g.num_sms)
         s = static_cast<int>(std::min<long long>(4, g.num_sms / tiles));
     if (const char* v = getenv("MINIXLA_KSPLIT")) {
         const int f = atoi(v);

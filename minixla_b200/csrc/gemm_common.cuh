@@ -56,14 +56,12 @@ struct FusedParams {
     int push_vec;                   // 16-byte aligned bases and ldo % 4 == 0: float4 copies
     // K split (single-CTA TF32 kernel, KSPLIT instances): tile t is output
     // tile t / splits, k-blocks [s * kb_per_split, +kb_per_split) with
-    // s = t % splits.  Slice s of a tile goes raw to ks_ws + s * ks_stride
-    // (row pitch ks_ld); ks_counters holds one zeroed int per output tile and
-    // TMEM lane quadrant.
+    // s = t % splits.  Slice s of the product goes raw to ks_ws + s * ks_stride
+    // (row pitch ks_ld); a second kernel sums the slices and applies the epilogue.
     int splits;
     int kb_per_split;
     float* ks_ws;
     long long ks_stride, ks_ld;
-    int* ks_counters;
 };
 
 // Error bits written to the device error word.
@@ -299,35 +297,26 @@ __device__ __forceinline__ void store_partial(const uint32_t (&r)[32], float* ds
     }
 }
 
-// v = slice 0 + slice 1 + ... of one row's 32 columns (zero past N), in
-// slice order, read at L2 (other SMs wrote the slices during this launch).
-// One row per lane, as the accumulator comes out of TMEM: the 32 rows of a
-// warp are summed side by side.
-__device__ __forceinline__ void sum_partials(float (&v)[32], const FusedParams& p, int row, int col) {
+// v = slice 0 + slice 1 + ... of row `row`, columns col .. col + 3 (zero past
+// N), in slice order.
+__device__ __forceinline__ void sum_slices4(float (&v)[4], const FusedParams& p, int row, int col) {
     const float* src = p.ks_ws + static_cast<long long>(row) * p.ks_ld + col;
-    if (col + 32 <= p.N) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 x = __ldcg(reinterpret_cast<const float4*>(src) + i);
-            v[4 * i] = x.x;
-            v[4 * i + 1] = x.y;
-            v[4 * i + 2] = x.z;
-            v[4 * i + 3] = x.w;
-        }
+    if (col + 4 <= p.N) {
+        float4 x = __ldcg(reinterpret_cast<const float4*>(src));
+        v[0] = x.x;
+        v[1] = x.y;
+        v[2] = x.z;
+        v[3] = x.w;
         for (int s = 1; s < p.splits; ++s) {
-            const float4* s4 = reinterpret_cast<const float4*>(src + s * p.ks_stride);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float4 x = __ldcg(s4 + i);
-                v[4 * i] += x.x;
-                v[4 * i + 1] += x.y;
-                v[4 * i + 2] += x.z;
-                v[4 * i + 3] += x.w;
-            }
+            x = __ldcg(reinterpret_cast<const float4*>(src + s * p.ks_stride));
+            v[0] += x.x;
+            v[1] += x.y;
+            v[2] += x.z;
+            v[3] += x.w;
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 4; ++i) {
             float x = 0.0f;
             if (col + i < p.N) {
                 x = __ldcg(src + i);

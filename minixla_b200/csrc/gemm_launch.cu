@@ -138,21 +138,11 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
     int rc = MXB_OK;
     g.k_splits = fused_gemm_k_splits(g);
     if (g.k_splits > 1) {
-        // K slices: raw partial sums per slice plus one counter per 128 x 128
-        // tile and TMEM lane quadrant, zeroed here on the launch stream.
-        const long long tiles = static_cast<long long>((M + kKsplitTileRows - 1) / kKsplitTileRows) *
-                                ((N + kKsplitTileCols - 1) / kKsplitTileCols);
+        // Raw partial sums, one M x round4(N) slice per K slice.
         const size_t slice = static_cast<size_t>(M) * ((N + 3) / 4 * 4);
-        const size_t cnt_bytes = static_cast<size_t>(4 * tiles) * sizeof(int);
         ws[0] = static_cast<float*>(ctx->pool->alloc(g.k_splits * slice * sizeof(float), stream));
-        ws[1] = static_cast<float*>(ctx->pool->alloc(cnt_bytes, stream));
-        if (!ws[0] || !ws[1]) {
-            rc = MXB_E_NOMEM;
-        } else if (!cuda_ok(cudaMemsetAsync(ws[1], 0, cnt_bytes, stream), "K-split counters")) {
-            rc = MXB_E_CUDA;
-        }
+        if (!ws[0]) rc = MXB_E_NOMEM;
         g.ks_ws = ws[0];
-        g.ks_counters = reinterpret_cast<int*>(ws[1]);
     }
     if (precision == GPU_PRECISION_3XTF32) {
         const size_t a_bytes = static_cast<size_t>(M) * lda * 4, b_bytes = static_cast<size_t>(K) * ldb * 4;

@@ -47,7 +47,6 @@ struct GemmLaunch {
     int choice_rows;                   // rows the K split is chosen for (0: M)
     int k_splits;                      // > 1: single-CTA TF32 kernel with K split this many ways
     float* ks_ws;                      // k_splits * M * round4(N) floats
-    int* ks_counters;                  // 4 * output tiles ints, zero at launch
 };
 
 // Skinny GEMM (skinny_gemm.cu): few output rows, CUDA-core fp32, split over
@@ -83,7 +82,7 @@ cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream);
 // the kernel that writes peer rows itself (MINIXLA_GATHER_PUSH=0: never).
 bool fused_gemm_pushes_rows(const GemmLaunch& g);
 // How many ways launch_fused_gemm(g) splits K (1: none); the caller supplies
-// the workspace and zeroed counters that a split needs.
+// the workspace a split needs (GemmLaunch::ks_ws).
 int fused_gemm_k_splits(const GemmLaunch& g);
 constexpr int kKsplitTileRows = 128, kKsplitTileCols = 128;
 cudaError_t launch_split_tf32(const float* x, long long rows, long long cols, long long ld_in,

@@ -378,10 +378,10 @@ def test_kernel_variants(lib, gpu_ctx, mnk, variant, precision, monkeypatch, hos
     check(got if rows is None else got[rows], want, precision, f"{variant} {mnk}")
 
 
-@pytest.mark.parametrize("mnk", [(2047, 250, 6200), (2048, 256, 8192), (1024, 1024, 8192)])
+@pytest.mark.parametrize("mnk", [(8191, 127, 3000), (2047, 250, 6200), (2048, 256, 8192), (1024, 1024, 8192)])
 def test_k_split(lib, gpu_ctx, mnk, monkeypatch, host_threads):
     """TF32 shapes whose 128 x 128 tiles fill under half the SMs with a long
-    K (>= 192 k-blocks) run the single-CTA kernel with K split across CTAs
+    K (>= 64 k-blocks) run the single-CTA kernel with K split across CTAs
     (here two and four ways; (2047, 250, 6200) ends on a partial row tile,
     column tile and k-block): the result matches
     the oracle, repeats bit for bit (the slices are summed in slice order
