@@ -73,7 +73,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                       const __grid_constant__ FusedParams p) {
     using C = Cfg<BN, STAGES, SPLIT3>;
-    static_assert(!(KSPLIT && (SPLIT3 || SEG)), "K split is a TF32 form");
+    static_assert(!KSPLIT || SPLIT3 == SEG, "K split: TF32, or 3xTF32 with segments");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -263,9 +263,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // Short k-loops: fetch C while the MMAs run; long ones: just before the drain.
                 if (p.num_kb <= kShortKb) prefetch_full_operands(row, col0, min(BN, p.N - col0), p);
             }
-            if (KSPLIT) {
+            if (KSPLIT && row_ok) {
                 // Fetch C into L2 for the reduce kernel while the MMAs run.
-                if (row_ok) prefetch_full_operands(row, col0, min(BN, p.N - col0), p);
+                prefetch_full_operands(row, col0, min(BN, p.N - col0), p);
+            }
+            if (KSPLIT && !SEG) {
                 const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
                 const bool got = !stop && mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns);
                 if (!__all_sync(0xffffffffu, got)) {
@@ -293,10 +295,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // columns at a time.  After the last segment the totals go back
                 // into that accumulator and the epilogue reads them from there,
                 // with the registers free.
+                // K split: this CTA's slice [kb_lo, kb_hi) in segments; its
+                // total goes raw to the slice workspace for the reduce kernel.
+                int kb_lo = 0, kb_hi = p.num_kb;
+                if (KSPLIT) {
+                    kb_lo = (t % p.splits) * p.kb_per_split;
+                    kb_hi = min(p.num_kb, kb_lo + p.kb_per_split);
+                }
                 float total[BN];
-                for (int k_begin = 0; k_begin < p.num_kb; k_begin += p.seg_kb) {
-                    const bool first = k_begin == 0;
-                    const bool last = k_begin + p.seg_kb >= p.num_kb;
+                for (int k_begin = kb_lo; k_begin < kb_hi; k_begin += p.seg_kb) {
+                    const bool first = k_begin == kb_lo;
+                    const bool last = k_begin + p.seg_kb >= kb_hi;
                     const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
                     const bool got = !stop && mbar_wait(tfull_bar(acc), acc_phase, p.timeout_ns);
                     if (!__all_sync(0xffffffffu, got)) {
@@ -322,16 +331,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (last) {
                         tmem_st_wait();
+                        float* slice = nullptr;
+                        if (KSPLIT)
+                            slice = p.ks_ws + static_cast<long long>(t % p.splits) * p.ks_stride +
+                                    static_cast<long long>(row) * p.ks_ld;
                         for (int c = 0; c < chunks; ++c) {
                             uint32_t r[32];
                             tmem_ld_32x32b_x32(taddr + 32 * c, r);
                             tmem_ld_wait();
-                            float v[32];
-#pragma unroll
-                            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
                             const int col = col0 + 32 * c;
-                            apply_epilogue(v, row, col, row_ok, p);
-                            if (row_ok) store_row_chunk(v, row, col, p);
+                            if (KSPLIT) {
+                                if (row_ok) store_partial(r, slice + col, col, p.N);
+                            } else {
+                                float v[32];
+#pragma unroll
+                                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                                apply_epilogue(v, row, col, row_ok, p);
+                                if (row_ok) store_row_chunk(v, row, col, p);
+                            }
                         }
                     }
                     tc_fence_before();
@@ -529,7 +546,8 @@ bool pair_wide_tiles(const GemmLaunch& g) {
 
 }  // namespace
 
-// K split of the single-CTA TF32 kernel on 128 x 128 tiles: when those tiles
+// K split of the single-CTA kernels on 128 x 128 tiles (TF32, and 3xTF32
+// with its segments inside each slice): when those tiles
 // would fill at most half the SMs and K has at least 64 k-blocks, up to
 // min(4, SMs / tiles) CTAs share each tile's k-loop, and a reduce kernel sums
 // the slices.  Measured against the unsplit 64- / 32-wide tiles (TF32, held-
@@ -537,14 +555,15 @@ bool pair_wide_tiles(const GemmLaunch& g) {
 // 27.4 -> 21.4, (1024, 1024, 4096) 48.0 -> 37.7, (640, 384, 4100) 45.9 ->
 // 25.6, (2048, 256, 8192) 80.8 -> 37.3, (512, 512, 8192) 78.8 -> 33.8,
 // (1024, 1024, 16384) 156.7 -> 97.2; with 32 k-blocks ((1000)^3) it lost
-// (19.4 -> 21.4), hence kKsplitMinKb.  The count follows the node's full row
+// (19.4 -> 21.4), hence kKsplitMinKb.  3xTF32: (4096, 128, 2048) 62.3 ->
+// 42.0 us, (512, 512, 8192) 170.9 -> 70.5.  The count follows the node's full row
 // count (choice_rows), so a node run in row chunks or shards gets the same
 // sums.  MINIXLA_KSPLIT=0 turns it off, =n forces n ways (2..8);
 // MINIXLA_SINGLE_BN alone leaves K unsplit.
 constexpr int kKsplitMinKb = 64;  // K >= 2017
 
 int fused_gemm_k_splits(const GemmLaunch& g) {
-    if (g.precision != GPU_PRECISION_TF32 || g.A2 || g.n_peers > 0 || use_pair_kernel(g)) return 1;
+    if (g.A2 || g.n_peers > 0 || use_pair_kernel(g)) return 1;
     const long long rows = g.choice_rows > 0 ? g.choice_rows : g.M;
     const long long tiles = ((rows + kKsplitTileRows - 1) / kKsplitTileRows) *
                             ((g.N + kKsplitTileCols - 1) / kKsplitTileCols);
@@ -576,6 +595,7 @@ cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
     }
     if (g.precision == GPU_PRECISION_3XTF32) {
         if (use_pair_kernel(g)) return launch_pair_3xtf32(g, false, stream);
+        if (g.k_splits > 1) return run_variant<128, 3, true, true, true>(g, stream);
         switch (single_cta_width(g)) {
             case 256:
             case 128: return run_variant<128, 3, true, true>(g, stream);

@@ -134,17 +134,17 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
         g.n_peers = peers->n;
     }
     g.choice_rows = rows_for_choice;
-    float* ws[3] = {nullptr, nullptr, nullptr};
+    float* ws[4] = {nullptr, nullptr, nullptr, nullptr};  // 3xTF32 low parts of A, B, B2; K-split slices
     int rc = MXB_OK;
     g.k_splits = fused_gemm_k_splits(g);
     if (g.k_splits > 1) {
         // Raw partial sums, one M x round4(N) slice per K slice.
         const size_t slice = static_cast<size_t>(M) * ((N + 3) / 4 * 4);
-        ws[0] = static_cast<float*>(ctx->pool->alloc(g.k_splits * slice * sizeof(float), stream));
-        if (!ws[0]) rc = MXB_E_NOMEM;
-        g.ks_ws = ws[0];
+        ws[3] = static_cast<float*>(ctx->pool->alloc(g.k_splits * slice * sizeof(float), stream));
+        if (!ws[3]) rc = MXB_E_NOMEM;
+        g.ks_ws = ws[3];
     }
-    if (precision == GPU_PRECISION_3XTF32) {
+    if (rc == MXB_OK && precision == GPU_PRECISION_3XTF32) {
         const size_t a_bytes = static_cast<size_t>(M) * lda * 4, b_bytes = static_cast<size_t>(K) * ldb * 4;
         const bool need_b2 = prod && !prod->B_small;
         ws[0] = static_cast<float*>(ctx->pool->alloc(a_bytes, stream));

@@ -353,11 +353,11 @@ def test_full_size_checksums(lib, gpu_ctx, precision):
                                  (8191, 127, 3000), (2048, 2048, 2048), (4096, 300, 1024), (640, 384, 4100)])
 def test_kernel_variants(lib, gpu_ctx, mnk, variant, precision, monkeypatch, host_threads):
     """Every kernel of each mode (CTA pair with 256- and, in TF32, 512-wide
-    tiles; single CTA with 128/256-, 64- and 32-wide tiles; in TF32 the
-    single-CTA kernel with K split three ways) on tile-edge shapes, with a
+    tiles; single CTA with 128/256-, 64- and 32-wide tiles; the single-CTA
+    kernel with K split three ways) on tile-edge shapes, with a
     full-matrix add, a bias row and relu in the epilogue.  K = 4100 ends on a
     partial k-block and a partial 3xTF32 segment."""
-    if variant in ("pair512", "ksplit3") and precision == X3:
+    if variant == "pair512" and precision == X3:
         pytest.skip("TF32-only kernel form")
     if variant == "ksplit3":
         monkeypatch.setenv("MINIXLA_KSPLIT", "3")
@@ -378,9 +378,10 @@ def test_kernel_variants(lib, gpu_ctx, mnk, variant, precision, monkeypatch, hos
     check(got if rows is None else got[rows], want, precision, f"{variant} {mnk}")
 
 
+@pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
 @pytest.mark.parametrize("mnk", [(8191, 127, 3000), (2047, 250, 6200), (2048, 256, 8192), (1024, 1024, 8192)])
-def test_k_split(lib, gpu_ctx, mnk, monkeypatch, host_threads):
-    """TF32 shapes whose 128 x 128 tiles fill under half the SMs with a long
+def test_k_split(lib, gpu_ctx, mnk, precision, monkeypatch, host_threads):
+    """Shapes whose 128 x 128 tiles fill under half the SMs with a long
     K (>= 64 k-blocks) run the single-CTA kernel with K split across CTAs
     (here two and four ways; (2047, 250, 6200) ends on a partial row tile,
     column tile and k-block): the result matches
@@ -395,17 +396,17 @@ def test_k_split(lib, gpu_ctx, mnk, monkeypatch, host_threads):
     root = hg.fused_node(hg.input_node(A), hg.input_node(B),
                          [(OP_ADD, hg.input_node(C)), (OP_RELU, None), (OP_ADD, hg.input_node(bias))])
     monkeypatch.setenv("MINIXLA_STREAM_CHUNKS", "1")
-    got = run_execute(lib, gpu_ctx, root, TF32)
-    assert np.array_equal(got, run_execute(lib, gpu_ctx, root, TF32)), "K-split result not repeatable"
+    got = run_execute(lib, gpu_ctx, root, precision)
+    assert np.array_equal(got, run_execute(lib, gpu_ctx, root, precision)), "K-split result not repeatable"
     rows = _sample_rows(M, 256)
     want = bindings.fused_oracle(A, B, [("add", C), ("relu",), ("add", bias)], rows=rows, threads=host_threads)
-    check(got[rows], want, TF32, f"k-split {mnk}")
+    check(got[rows], want, precision, f"k-split {mnk}")
     monkeypatch.setenv("MINIXLA_STREAM_CHUNKS", "8")
-    assert np.array_equal(got, run_execute(lib, gpu_ctx, root, TF32)), "row-streamed K split differs"
+    assert np.array_equal(got, run_execute(lib, gpu_ctx, root, precision)), "row-streamed K split differs"
     monkeypatch.setenv("MINIXLA_STREAM_CHUNKS", "1")
     monkeypatch.setenv("MINIXLA_KSPLIT", "0")
-    unsplit = run_execute(lib, gpu_ctx, root, TF32)
-    check(got, unsplit, TF32, f"k-split vs unsplit {mnk}")
+    unsplit = run_execute(lib, gpu_ctx, root, precision)
+    check(got, unsplit, precision, f"k-split vs unsplit {mnk}")
     assert not np.array_equal(got, unsplit), "same bits as the unsplit kernel: K was not split"
 
 
