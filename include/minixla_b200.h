@@ -307,6 +307,28 @@ MXB_API int mxb_ipc_free(int device, void* dptr);
  * itself (the rest used copies), in this process. */
 MXB_API unsigned long long mxb_gather_push_count(void);
 
+/* ---- Which kernel runs a product ---------------------------------------
+ * No counterpart in the reference (its GPU path has one kernel per mode).
+ * mxb_gemm_plan_for reports what mxb_fused_gemm / gpu_execute run for an
+ * M x N x K product (M: the node's full row count) in `precision` on a GPU
+ * with `num_sms` SMs, under the current MINIXLA_* settings: the kernel family,
+ * its output tile and how many ways K is split across CTAs.  Host-only: it
+ * touches no GPU.  0 or MXB_E_ARG. */
+enum {
+    MXB_KERNEL_SKINNY = 1,     /* CUDA-core fp32 over column blocks x K slices (few rows)     */
+    MXB_KERNEL_TINY = 2,       /* CUDA-core fp32, 32 x 32 tiles, one launch (tiny problems)    */
+    MXB_KERNEL_SINGLE_CTA = 3, /* tcgen05, one CTA per 128-row tile                           */
+    MXB_KERNEL_CTA_PAIR = 4    /* tcgen05 cta_group::2, 256-row tiles on two SMs              */
+};
+typedef struct {
+    int kernel;                /* MXB_KERNEL_*                                                */
+    int tile_rows, tile_cols;  /* output tile of one CTA (pair: of the two CTAs)              */
+    int k_splits;              /* CTAs sharing one tile's K range (1: none)                   */
+    int products;              /* 1 (mxb_gemm_plan_for reports single products)               */
+    int reserved[3];
+} mxb_gemm_plan;
+MXB_API int mxb_gemm_plan_for(int M, int N, int K, int precision, int num_sms, mxb_gemm_plan* plan);
+
 /* Standalone element-wise nodes (tensor.c:64-86 and 110-120 semantics):
  * out[i] = a[i] + b[i % b_size]  and  out[i] = x[i] > 0 ? x[i] : 0. */
 MXB_API int mxb_add(GpuCtx* ctx, const float* a, long long n, const float* b, long long b_size,

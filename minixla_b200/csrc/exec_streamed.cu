@@ -153,7 +153,7 @@ int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
             continue;
         const Info& b = info[index.at(nd->inputs[1])];
         // Nodes on the CUDA-core kernels (few rows, tiny problems) need no low parts.
-        if (M <= kSkinnyMaxRows || use_tiny_gemm(M, b.dims[1], b.dims[0], ctx->precision)) continue;
+        if (use_skinny_gemm(M, ctx->precision) || use_tiny_gemm(M, b.dims[1], b.dims[0], ctx->precision)) continue;
         b_small[i] = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(b.size) * 4, cs));
         if (!b_small[i]) {
             rc = MXB_E_NOMEM;

@@ -548,9 +548,9 @@ bool pair_wide_tiles(const GemmLaunch& g) {
 
 // K split of the single-CTA kernels on 128 x 128 tiles (TF32, and 3xTF32
 // with its segments inside each slice): when those tiles
-// would fill at most half the SMs and K has at least 64 k-blocks, up to
-// min(4, SMs / tiles) CTAs share each tile's k-loop, and a reduce kernel sums
-// the slices.  Measured against the unsplit 64- / 32-wide tiles (TF32, held-
+// would fill at most half the SMs and K has at least 64 k-blocks,
+// min(8, SMs / tiles, k-blocks / 16) CTAs share each tile's k-loop, and a
+// reduce kernel sums the slices.  Measured against the unsplit 64- / 32-wide tiles (TF32, held-
 // stream CUDA events): (8191, 127, 3000) 44.1 -> 41.5 us, (4096, 128, 2048)
 // 27.4 -> 21.4, (1024, 1024, 4096) 48.0 -> 37.7, (640, 384, 4100) 45.9 ->
 // 25.6, (2048, 256, 8192) 80.8 -> 37.3, (512, 512, 8192) 78.8 -> 33.8,
@@ -570,7 +570,7 @@ int fused_gemm_k_splits(const GemmLaunch& g) {
     const int num_kb = (g.K + kBK - 1) / kBK;
     int s = 1;
     if (num_kb >= kKsplitMinKb && 2 * tiles <= g.num_sms)
-        s = static_cast<int>(std::min<long long>(4, g.num_sms / tiles));
+        s = static_cast<int>(std::min<long long>({8, g.num_sms / tiles, num_kb / 16}));
     if (const char* v = getenv("MINIXLA_KSPLIT")) {
         const int f = atoi(v);
         if (f == 0 || f == 1) return 1;
@@ -586,30 +586,59 @@ bool fused_gemm_pushes_rows(const GemmLaunch& g) {
     return !g.A2 && g.precision == GPU_PRECISION_TF32 && use_pair_kernel(g);
 }
 
-cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
+GemmPlan plan_fused_gemm(const GemmLaunch& g, int k_splits) {
+    GemmPlan pl{};
+    pl.products = g.A2 ? 2 : 1;
+    pl.k_splits = 1;
     if (g.A2) {
-        // Two products of one A in one kernel (callers run other cases as two launches).
-        if (g.precision == GPU_PRECISION_3XTF32) return launch_pair_3xtf32(g, true, stream);
-        if (g.precision != GPU_PRECISION_TF32) return cudaErrorInvalidValue;
-        return launch_pair_tf32_dual(g, stream);
+        // Two products of one A in one kernel (callers run other cases as two
+        // launches): 3xTF32 on 256 x 128 pair tiles; TF32 on 256 x 256 tiles
+        // once they give every CTA pair a tile, else 256 x 128.
+        pl.kernel = MXB_KERNEL_CTA_PAIR;
+        pl.tile_rows = 256;
+        const long long tiles256 = static_cast<long long>((g.M + 255) / 256) * ((g.N + 255) / 256);
+        pl.tile_cols = g.precision == GPU_PRECISION_TF32 && tiles256 >= g.num_sms / 2 ? 256 : 128;
+        return pl;
     }
-    if (g.precision == GPU_PRECISION_3XTF32) {
-        if (use_pair_kernel(g)) return launch_pair_3xtf32(g, false, stream);
-        if (g.k_splits > 1) return run_variant<128, 3, true, true, true>(g, stream);
-        switch (single_cta_width(g)) {
-            case 256:
+    if (use_pair_kernel(g)) {
+        pl.kernel = MXB_KERNEL_CTA_PAIR;
+        pl.tile_rows = 256;
+        pl.tile_cols = g.precision == GPU_PRECISION_TF32 && pair_wide_tiles(g) ? 512 : 256;
+        return pl;
+    }
+    pl.kernel = MXB_KERNEL_SINGLE_CTA;
+    pl.tile_rows = kBM;
+    if (k_splits > 1) {
+        pl.k_splits = k_splits;
+        pl.tile_cols = kKsplitTileCols;
+        return pl;
+    }
+    // Narrower tiles for problems with few tiles, so more SMs share the
+    // k-loops and the epilogue; 3xTF32 stages two operand pairs, so its
+    // widest single-CTA tile is 128.
+    const int w = single_cta_width(g);
+    pl.tile_cols = g.precision == GPU_PRECISION_3XTF32 && w == 256 ? 128 : w;
+    return pl;
+}
+
+cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
+    if (g.precision != GPU_PRECISION_TF32 && g.precision != GPU_PRECISION_3XTF32) return cudaErrorInvalidValue;
+    const bool x3 = g.precision == GPU_PRECISION_3XTF32;
+    const GemmPlan pl = plan_fused_gemm(g, g.k_splits);
+    if (pl.kernel == MXB_KERNEL_CTA_PAIR) {
+        if (pl.products == 2) return x3 ? launch_pair_3xtf32(g, true, stream) : launch_pair_tf32_dual(g, stream);
+        return x3 ? launch_pair_3xtf32(g, false, stream) : launch_pair_tf32(g, pl.tile_cols == 512, stream);
+    }
+    if (pl.k_splits > 1)
+        return x3 ? run_variant<128, 3, true, true, true>(g, stream) : run_variant<128, 6, false, false, true>(g, stream);
+    if (x3) {
+        switch (pl.tile_cols) {
             case 128: return run_variant<128, 3, true, true>(g, stream);
             case 64: return run_variant<64, 4, true, true>(g, stream);
             default: return run_variant<32, 5, true, true>(g, stream);
         }
     }
-    if (use_pair_kernel(g)) {
-        return launch_pair_tf32(g, pair_wide_tiles(g), stream);
-    }
-    if (g.k_splits > 1) return run_variant<128, 6, false, false, true>(g, stream);
-    // One TF32 product on one CTA.  Narrower tiles for problems with few
-    // tiles, so more SMs share the k-loops and the epilogue.
-    switch (single_cta_width(g)) {
+    switch (pl.tile_cols) {
         case 256: return run_variant<256, 4, false, false>(g, stream);
         case 128: return run_variant<128, 6, false, false>(g, stream);
         case 64: return run_variant<64, 8, false, false>(g, stream);

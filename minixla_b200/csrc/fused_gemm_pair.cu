@@ -423,10 +423,10 @@ cudaError_t launch_pair_tf32(const GemmLaunch& g, bool wide_tiles, cudaStream_t 
 }
 
 // 256-column tiles put both accumulators in the 512 TMEM columns (one buffer,
-// 48 KiB stages); 128-column tiles keep two buffers for problems with few tiles.
+// 48 KiB stages); 128-column tiles keep two buffers for problems with few tiles
+// (the choice is plan_fused_gemm's).
 cudaError_t launch_pair_tf32_dual(const GemmLaunch& g, cudaStream_t stream) {
-    const long long tiles256 = static_cast<long long>((g.M + 255) / 256) * ((g.N + 255) / 256);
-    if (tiles256 >= g.num_sms / 2) return run_pair_variant<4, 256, true>(g, stream);
+    if (plan_fused_gemm(g, 1).tile_cols == 256) return run_pair_variant<4, 256, true>(g, stream);
     return run_pair_variant<6, 128, true>(g, stream);
 }
 

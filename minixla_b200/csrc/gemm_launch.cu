@@ -82,14 +82,15 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
         ctx->pool->release(ws, stream);
         return rc;
     }
-    if (rows_for_choice > kSkinnyMaxRows && use_tiny_gemm(rows_for_choice, N, K, precision)) {
+    const bool skinny = use_skinny_gemm(rows_for_choice, precision);
+    if (!skinny && use_tiny_gemm(rows_for_choice, N, K, precision)) {
         // Small enough that one plain CUDA-core launch beats the set-up of the tensor-core kernels.
         return cuda_ok(launch_tiny_gemm(A, lda, B, ldb, out, ldo, M, N, K, row_base, steps, n_steps, stream),
                        "tiny GEMM launch")
                    ? MXB_OK
                    : MXB_E_CUDA;
     }
-    if (rows_for_choice <= kSkinnyMaxRows) {
+    if (skinny) {
         // Few rows: HBM-bound on B, CUDA-core fp32 split over columns and K.
         const SkinnyPlan pl = plan_skinny(M, N, K, ctx->num_sms);
         float* ws = nullptr;  // the one-kernel form needs no workspace

@@ -52,6 +52,10 @@ struct GemmLaunch {
 // Skinny GEMM (skinny_gemm.cu): few output rows, CUDA-core fp32, split over
 // column blocks x K ranges; workspace holds splits * M * N floats.
 constexpr int kSkinnyMaxRows = 16;
+// Whether an M-row product (M: the node's full row count) runs on the skinny
+// kernels: up to 8 rows in TF32 mode, 16 in 3xTF32 mode;
+// MINIXLA_SKINNY_MAX_ROWS=n (0..16) sets the limit for both.
+bool use_skinny_gemm(int M, int precision);
 struct SkinnyPlan {
     bool one_kernel = false;  // cluster kernel: no workspace (splits == 0)
     int col_blocks = 1;
@@ -81,6 +85,16 @@ cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream);
 // Whether launch_fused_gemm(g) runs the TF32 CTA-pair kernel for one product,
 // the kernel that writes peer rows itself (MINIXLA_GATHER_PUSH=0: never).
 bool fused_gemm_pushes_rows(const GemmLaunch& g);
+// Kernel family (MXB_KERNEL_*), tile and K split that launch_fused_gemm runs
+// for g when the caller provides workspace for `k_splits` slices (0 or 1:
+// none); products = 2 for a shared-A second product in the same kernel.
+struct GemmPlan {
+    int kernel;
+    int tile_rows, tile_cols;
+    int k_splits;
+    int products;
+};
+GemmPlan plan_fused_gemm(const GemmLaunch& g, int k_splits);
 // How many ways launch_fused_gemm(g) splits K (1: none); the caller supplies
 // the workspace a split needs (GemmLaunch::ks_ws).
 int fused_gemm_k_splits(const GemmLaunch& g);

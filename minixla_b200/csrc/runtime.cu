@@ -519,6 +519,43 @@ int mxb_fused_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, l
                               stream, nullptr);
 }
 
+int mxb_gemm_plan_for(int M, int N, int K, int precision, int num_sms, mxb_gemm_plan* plan) {
+    if (!plan || M < 1 || N < 1 || K < 1 || num_sms < 2 || !mxb::valid_precision(precision)) {
+        set_error("mxb_gemm_plan_for: invalid arguments");
+        return MXB_E_ARG;
+    }
+    memset(plan, 0, sizeof(*plan));
+    plan->products = 1;
+    plan->k_splits = 1;
+    // The same order as launch_gemm: skinny, tiny, then the tensor-core plan.
+    if (mxb::use_skinny_gemm(M, precision)) {
+        const mxb::SkinnyPlan sp = mxb::plan_skinny(M, N, K, num_sms);
+        plan->kernel = MXB_KERNEL_SKINNY;
+        plan->tile_rows = M;
+        plan->tile_cols = sp.one_kernel ? 128 : (N + sp.col_blocks - 1) / sp.col_blocks;
+        plan->k_splits = sp.one_kernel ? 8 : sp.splits;
+        return MXB_OK;
+    }
+    if (mxb::use_tiny_gemm(M, N, K, precision)) {
+        plan->kernel = MXB_KERNEL_TINY;
+        plan->tile_rows = plan->tile_cols = 32;
+        return MXB_OK;
+    }
+    mxb::GemmLaunch g{};
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.precision = precision;
+    g.num_sms = num_sms;
+    g.choice_rows = M;
+    const mxb::GemmPlan pl = mxb::plan_fused_gemm(g, mxb::fused_gemm_k_splits(g));
+    plan->kernel = pl.kernel;
+    plan->tile_rows = pl.tile_rows;
+    plan->tile_cols = pl.tile_cols;
+    plan->k_splits = pl.k_splits;
+    return MXB_OK;
+}
+
 int mxb_fused_gemm_allgather(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
                              long long ldo, float* const* peer_out, int n_peers, int M, int N, int K,
                              const mxb_ep_step* steps, int n_steps, int precision, void* stream) {

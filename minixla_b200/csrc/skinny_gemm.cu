@@ -412,6 +412,17 @@ __global__ void __launch_bounds__(256)
 
 }  // namespace
 
+// TF32 mode: up to 8 rows.  From 9 rows the tensor-core kernel with its K
+// split streams B faster than the CUDA cores multiply it (K = N = 8192:
+// M = 8 65 -> 54 us, 12 rows 90 -> 54 us, 16 rows 96 -> 56 us; M = 4 51 vs
+// 54 us stays here).  3xTF32 mode: up to 16 rows, as the low-part pass over
+// B alone costs more than the whole CUDA-core product (M = 16: 95 vs 200 us).
+bool use_skinny_gemm(int M, int precision) {
+    int limit = precision == GPU_PRECISION_3XTF32 ? kSkinnyMaxRows : 8;
+    if (const char* v = getenv("MINIXLA_SKINNY_MAX_ROWS")) limit = std::min(kSkinnyMaxRows, std::max(0, atoi(v)));
+    return M <= limit;
+}
+
 bool use_tiny_gemm(int M, int N, int K, int precision) {
     const long long mnk = static_cast<long long>(M) * N * K;
     if (const char* v = getenv("MINIXLA_TINY_MAX_MNK")) return mnk <= atoll(v);

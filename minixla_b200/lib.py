@@ -68,6 +68,7 @@ PROTOTYPES = {
     "mxb_ipc_close": (C.c_int, [C.c_int, C.c_void_p]),
     "mxb_ipc_free": (C.c_int, [C.c_int, C.c_void_p]),
     "mxb_gather_push_count": (C.c_ulonglong, []),
+    "mxb_gemm_plan_for": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]),
     "mxb_add": (C.c_int, [C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]),
     "mxb_relu": (C.c_int, [C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]),
     "mxb_check_device_error": (C.c_int, [C.c_void_p]),
@@ -75,6 +76,31 @@ PROTOTYPES = {
     "mxb_launch_count": (C.c_ulonglong, []),
     "mxb_last_error": (C.c_char_p, []),
 }
+
+
+MXB_KERNEL_SKINNY, MXB_KERNEL_TINY, MXB_KERNEL_SINGLE_CTA, MXB_KERNEL_CTA_PAIR = 1, 2, 3, 4
+
+
+class GemmPlan(C.Structure):
+    """Mirror of ``mxb_gemm_plan``."""
+
+    _fields_ = [
+        ("kernel", C.c_int),
+        ("tile_rows", C.c_int),
+        ("tile_cols", C.c_int),
+        ("k_splits", C.c_int),
+        ("products", C.c_int),
+        ("reserved", C.c_int * 3),
+    ]
+
+
+def gemm_plan(M: int, N: int, K: int, precision: int, num_sms: int = 148) -> GemmPlan:
+    """What mxb_gemm_plan_for reports for an M x N x K product (host-only)."""
+    plan = GemmPlan()
+    rc = load().mxb_gemm_plan_for(M, N, K, precision, num_sms, C.byref(plan))
+    if rc != 0:
+        raise ValueError(f"mxb_gemm_plan_for: {last_error()}")
+    return plan
 
 
 class EpStepDev(C.Structure):

@@ -1,0 +1,84 @@
+"""Kernel choice per shape (mxb_gemm_plan_for), host-only: the rules the
+dispatcher follows, on a 148-SM GPU, without a GPU.  The same plan function
+drives the launches (launch_fused_gemm dispatches on it), so these cases pin
+what the GPU runs."""
+import pytest
+
+from minixla_b200 import lib as mlib
+
+TF32, X3 = mlib.GPU_PRECISION_TF32, mlib.GPU_PRECISION_3XTF32
+SKINNY, TINY, SINGLE, PAIR = (mlib.MXB_KERNEL_SKINNY, mlib.MXB_KERNEL_TINY, mlib.MXB_KERNEL_SINGLE_CTA,
+                              mlib.MXB_KERNEL_CTA_PAIR)
+
+# (M, N, K, precision) -> (kernel, tile_rows, tile_cols, k_splits)
+CASES = [
+    ((8192, 8192, 8192, TF32), (PAIR, 256, 512, 1)),      # headline: wide pair tiles
+    ((8192, 8192, 8192, X3), (PAIR, 256, 256, 1)),
+    ((32768, 8192, 8192, TF32), (PAIR, 256, 512, 1)),
+    ((2048, 2048, 2048, TF32), (PAIR, 256, 256, 1)),      # too few 256 x 512 tiles
+    ((1024, 1024, 1024, TF32), (SINGLE, 128, 64, 1)),     # 32 k-blocks: no K split
+    ((8191, 127, 3000, TF32), (SINGLE, 128, 128, 2)),     # few tiles, long K
+    ((8191, 127, 3000, X3), (SINGLE, 128, 128, 2)),
+    ((4096, 128, 2048, TF32), (SINGLE, 128, 128, 4)),
+    ((512, 512, 8192, TF32), (SINGLE, 128, 128, 8)),
+    ((16, 8192, 8192, TF32), (SINGLE, 128, 128, 2)),      # 9..16 rows: tensor cores in TF32 mode
+    ((9, 4096, 4096, TF32), (SINGLE, 128, 128, 4)),
+    ((16, 8192, 8192, X3), (SKINNY, 16, 128, 8)),         # ... CUDA cores in 3xTF32 mode
+    ((8, 8192, 8192, TF32), (SKINNY, 8, 128, 8)),
+    ((1, 4096, 4096, TF32), (SKINNY, 1, 128, 8)),
+    ((128, 128, 128, X3), (TINY, 32, 32, 1)),             # config 1 in 3xTF32 mode
+    ((128, 128, 128, TF32), (SINGLE, 128, 32, 1)),
+    ((257, 4097, 129, TF32), (SINGLE, 128, 128, 1)),     # 99 tiles of 128 x 128
+    ((1, 4096, 4096, X3), (SKINNY, 1, 128, 8)),
+]
+
+
+@pytest.mark.parametrize("shape,want", CASES, ids=[f"{m}x{n}x{k}-{'tf32' if p == TF32 else '3x'}"
+                                                   for (m, n, k, p), _ in CASES])
+def test_plan(shape, want, monkeypatch):
+    for var in ("MINIXLA_KSPLIT", "MINIXLA_SKINNY_MAX_ROWS", "MINIXLA_GEMM_VARIANT", "MINIXLA_SINGLE_BN",
+                "MINIXLA_TINY_MAX_MNK", "MINIXLA_SKINNY_FORM"):
+        monkeypatch.delenv(var, raising=False)
+    p = mlib.gemm_plan(*shape)
+    assert (p.kernel, p.tile_rows, p.tile_cols, p.k_splits) == want
+    assert p.products == 1
+
+
+def test_plan_follows_settings(monkeypatch):
+    for var in ("MINIXLA_KSPLIT", "MINIXLA_SKINNY_MAX_ROWS", "MINIXLA_GEMM_VARIANT", "MINIXLA_SINGLE_BN"):
+        monkeypatch.delenv(var, raising=False)
+    monkeypatch.setenv("MINIXLA_KSPLIT", "0")
+    p = mlib.gemm_plan(8191, 127, 3000, TF32)
+    assert (p.kernel, p.tile_cols, p.k_splits) == (SINGLE, 64, 1)
+    monkeypatch.setenv("MINIXLA_KSPLIT", "3")
+    assert mlib.gemm_plan(8191, 127, 3000, TF32).k_splits == 3
+    monkeypatch.delenv("MINIXLA_KSPLIT")
+    monkeypatch.setenv("MINIXLA_SKINNY_MAX_ROWS", "16")
+    assert mlib.gemm_plan(16, 8192, 8192, TF32).kernel == SKINNY
+    monkeypatch.setenv("MINIXLA_SKINNY_MAX_ROWS", "0")
+    assert mlib.gemm_plan(1, 4096, 4096, TF32).kernel == SINGLE
+    assert mlib.gemm_plan(1, 4096, 4096, X3).kernel == TINY        # 2^24 <= 2^26 in 3xTF32 mode
+    monkeypatch.delenv("MINIXLA_SKINNY_MAX_ROWS")
+    monkeypatch.setenv("MINIXLA_GEMM_VARIANT", "single")
+    p = mlib.gemm_plan(8192, 8192, 8192, TF32)
+    assert (p.kernel, p.tile_cols) == (SINGLE, 256)
+    monkeypatch.setenv("MINIXLA_GEMM_VARIANT", "pair")
+    p = mlib.gemm_plan(8192, 8192, 8192, TF32)
+    assert (p.kernel, p.tile_cols) == (PAIR, 256)
+    monkeypatch.delenv("MINIXLA_GEMM_VARIANT")
+    monkeypatch.setenv("MINIXLA_SINGLE_BN", "32")
+    p = mlib.gemm_plan(8191, 127, 3000, TF32)
+    assert (p.kernel, p.tile_cols, p.k_splits) == (SINGLE, 32, 1)   # a forced width runs unsplit
+
+
+def test_plan_depends_on_sm_count():
+    # Fewer SMs: the same 8192-row product already fills the GPU with 256 x 512 tiles.
+    assert mlib.gemm_plan(2048, 2048, 2048, TF32, num_sms=32).tile_cols == 512
+    # More tiles than half the SMs: no K split.
+    assert mlib.gemm_plan(8191, 127, 3000, TF32, num_sms=100).k_splits == 1
+
+
+@pytest.mark.parametrize("args", [(0, 8, 8, TF32, 148), (8, 8, 8, 2, 148), (8, 8, 8, TF32, 1)])
+def test_plan_rejects_bad_arguments(args):
+    with pytest.raises(ValueError):
+        mlib.gemm_plan(*args)

@@ -447,7 +447,10 @@ def test_skinny_rows_path(lib, gpu_ctx, M, form, NK, precision, monkeypatch, hos
     epilogue kind, ragged N, against the oracle at the 3xTF32 tolerance.
     Both forms -- one kernel reducing over a cluster's shared memory, and
     partial sums + reduce kernel (MINIXLA_SKINNY_FORM=split) -- and K = 20000,
-    whose slices of A do not fit in shared memory (two kernels by itself)."""
+    whose slices of A do not fit in shared memory (two kernels by itself).
+    TF32 mode sends 9 to 16 rows to the tensor-core kernel by default; the
+    limit is raised here to cover the skinny kernels' 16-row forms."""
+    monkeypatch.setenv("MINIXLA_SKINNY_MAX_ROWS", "16")
     if form:
         monkeypatch.setenv("MINIXLA_SKINNY_FORM", form)
     N, K = NK
@@ -461,6 +464,26 @@ def test_skinny_rows_path(lib, gpu_ctx, M, form, NK, precision, monkeypatch, hos
     got = run_execute(lib, gpu_ctx, root, precision)
     want = bindings.fused_oracle(A, B, [("add", C), ("add", odd), ("relu",), ("add", bias)], threads=host_threads)
     check(got, want, X3, f"skinny M={M}")
+
+
+@pytest.mark.parametrize("M", [9, 16])
+@pytest.mark.parametrize("NK", [(1000, 777), (2501, 8000)], ids=["short_k", "k_split"])
+def test_few_rows_tensor_path(lib, gpu_ctx, M, NK, host_threads):
+    """TF32 mode runs 9 to 16 rows on the tensor-core kernel (one 128-row
+    tile, rows past M filled with zeros by TMA), with K split when K is long:
+    every epilogue kind, ragged N, against the oracle at the TF32 tolerance,
+    and the same bits through the row-streamed executor."""
+    N, K = NK
+    A, B, C = _relu_abc(M, N, K, c_normal=True)
+    bias = datagen.normal((N,), 8, 0.0, 0.5)
+    odd = datagen.uniform((13,), 9)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A), hg.input_node(B),
+                         [(OP_ADD, hg.input_node(C)), (OP_ADD, hg.input_node(odd)), (OP_RELU, None),
+                          (OP_ADD, hg.input_node(bias))])
+    got = run_execute(lib, gpu_ctx, root, TF32)
+    want = bindings.fused_oracle(A, B, [("add", C), ("add", odd), ("relu",), ("add", bias)], threads=host_threads)
+    check(got, want, TF32, f"few rows M={M} {NK}")
 
 
 @pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
