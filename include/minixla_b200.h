@@ -109,7 +109,8 @@ MXB_API void    gpu_ctx_destroy(GpuCtx* ctx);
 MXB_API Tensor* gpu_execute(Node* root, GpuCtx* ctx);
 /* Kernel-only timing of one OP_FUSED node: inputs uploaded once, `warmup`
  * launches, then the minimum over `reps` CUDA-event-timed launches, in ms;
- * -1.0 on failure -- gpu_exec.h:21-32. */
+ * -1.0 on failure -- gpu_exec.h:21-32.  Also times rank-3 (batched) nodes,
+ * which the reference's timer refused: every product of the batch. */
 MXB_API double  gpu_time_kernel_ms(Node* root, GpuCtx* ctx, int warmup, int reps);
 /* One OP_FUSED node through a single TF32 tensor-core product -- gpu_exec.h:34-39. */
 MXB_API Tensor* gpu_run_tensorcore(const Node* fused, GpuCtx* ctx);

@@ -67,13 +67,18 @@ struct Cfg {
 // KSPLIT: tile t is a K slice of output tile t / p.splits; the epilogue warps
 // write the slice raw to workspace and ksplit_reduce_kernel, launched next,
 // sums the slices in slice order and applies the epilogue.
-template <int BN, int STAGES, bool SPLIT3, bool SEG, bool KSPLIT = false>
+//
+// BATCHED: p.batch products of the same shape in one launch; A, B (and their
+// low parts) are 3-D tensor maps whose third coordinate is the product, so a
+// partial tile or k-block never reads the next product's rows.
+template <int BN, int STAGES, bool SPLIT3, bool SEG, bool KSPLIT = false, bool BATCHED = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fused_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                       const __grid_constant__ FusedParams p) {
     using C = Cfg<BN, STAGES, SPLIT3>;
     static_assert(!KSPLIT || SPLIT3 == SEG, "K split: TF32, or 3xTF32 with segments");
+    static_assert(!(KSPLIT && BATCHED), "a batched launch does not split K");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -129,10 +134,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
                 int mb, nb;
                 int kb_lo = 0, kb_hi = p.num_kb;
+                int b = 0;
                 if (KSPLIT) {
                     tile_coords(t / p.splits, p, mb, nb);
                     kb_lo = (t % p.splits) * p.kb_per_split;
                     kb_hi = min(p.num_kb, kb_lo + p.kb_per_split);
+                } else if (BATCHED) {
+                    b = t / p.tiles_per_batch;
+                    tile_coords(t - b * p.tiles_per_batch, p, mb, nb);
                 } else {
                     tile_coords(t, p, mb, nb);
                 }
@@ -148,17 +157,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t fb = full_bar(stage);
                     mbar_arrive_expect_tx(fb, C::kStageBytes);
                     const int k0 = kb * kBK;
-                    tma_load_2d(smem_addr(st), &tmA, fb, k0, m0);
-#pragma unroll
-                    for (int j = 0; j < BN / 32; ++j)
-                        tma_load_2d(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb, n0 + 32 * j, k0);
-                    if (SPLIT3) {
-                        uint8_t* st2 = st + C::kOperandBytes;
-                        tma_load_2d(smem_addr(st2), &tmA2, fb, k0, m0);
+                    if (BATCHED) {
+                        tma_load_3d(smem_addr(st), &tmA, fb, k0, m0, b);
 #pragma unroll
                         for (int j = 0; j < BN / 32; ++j)
-                            tma_load_2d(smem_addr(st2 + C::kABytes + j * kBoxBytes), &tmB2, fb,
-                                        n0 + 32 * j, k0);
+                            tma_load_3d(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb, n0 + 32 * j, k0, b);
+                        if (SPLIT3) {
+                            uint8_t* st2 = st + C::kOperandBytes;
+                            tma_load_3d(smem_addr(st2), &tmA2, fb, k0, m0, b);
+#pragma unroll
+                            for (int j = 0; j < BN / 32; ++j)
+                                tma_load_3d(smem_addr(st2 + C::kABytes + j * kBoxBytes), &tmB2, fb,
+                                            n0 + 32 * j, k0, b);
+                        }
+                    } else {
+                        tma_load_2d(smem_addr(st), &tmA, fb, k0, m0);
+#pragma unroll
+                        for (int j = 0; j < BN / 32; ++j)
+                            tma_load_2d(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb, n0 + 32 * j, k0);
+                        if (SPLIT3) {
+                            uint8_t* st2 = st + C::kOperandBytes;
+                            tma_load_2d(smem_addr(st2), &tmA2, fb, k0, m0);
+#pragma unroll
+                            for (int j = 0; j < BN / 32; ++j)
+                                tma_load_2d(smem_addr(st2 + C::kABytes + j * kBoxBytes), &tmB2, fb,
+                                            n0 + 32 * j, k0);
+                        }
                     }
                     ++issued;
                     if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -251,7 +275,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t acc_phase = 0;
         for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
             int mb, nb;
-            tile_coords(KSPLIT ? t / p.splits : t, p, mb, nb);
+            int b = 0;
+            if (BATCHED) {
+                b = t / p.tiles_per_batch;
+                tile_coords(t - b * p.tiles_per_batch, p, mb, nb);
+            } else {
+                tile_coords(KSPLIT ? t / p.splits : t, p, mb, nb);
+            }
+            const long long out_off = BATCHED ? b * p.out_bstride : 0;
             const int row = mb * kBM + row_in_tile;
             const bool row_ok = row < p.M;
             const int col0 = nb * BN;
@@ -261,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool failed = false;
             if (!KSPLIT && row_ok) {
                 // Short k-loops: fetch C while the MMAs run; long ones: just before the drain.
-                if (p.num_kb <= kShortKb) prefetch_full_operands(row, col0, min(BN, p.N - col0), p);
+                if (p.num_kb <= kShortKb) prefetch_full_operands(row, col0, min(BN, p.N - col0), p, b);
             }
             if (KSPLIT && row_ok) {
                 // Fetch C into L2 for the reduce kernel while the MMAs run.
@@ -346,8 +377,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 float v[32];
 #pragma unroll
                                 for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-                                apply_epilogue(v, row, col, row_ok, p);
-                                if (row_ok) store_row_chunk(v, row, col, p);
+                                apply_epilogue(v, row, col, row_ok, p, nullptr, b);
+                                if (row_ok) store_row_chunk(v, row, col, p, out_off);
                             }
                         }
                     }
@@ -365,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                if (row_ok && p.num_kb > kShortKb) prefetch_full_operands(row, col0, min(BN, p.N - col0), p);
+                if (row_ok && p.num_kb > kShortKb) prefetch_full_operands(row, col0, min(BN, p.N - col0), p, b);
                 const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * BN);
                 for (int c = 0; c < chunks; ++c) {
                     uint32_t r[32];
@@ -380,8 +411,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
                     const int col = col0 + 32 * c;
-                    apply_epilogue(v, row, col, row_ok, p);
-                    if (row_ok) store_row_chunk(v, row, col, p);
+                    apply_epilogue(v, row, col, row_ok, p, nullptr, b);
+                    if (row_ok) store_row_chunk(v, row, col, p, out_off);
                 }
                 acc ^= 1;
                 if (acc == 0) acc_phase ^= 1u;
@@ -415,10 +446,11 @@ __global__ void __launch_bounds__(256) ksplit_reduce_kernel(const __grid_constan
 
 // ------------------------------------------------------------------ host side
 
-template <int BN, int STAGES, bool SPLIT3, bool SEG, bool KSPLIT = false>
+template <int BN, int STAGES, bool SPLIT3, bool SEG, bool KSPLIT = false, bool BATCHED = false>
 cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     using C = Cfg<BN, STAGES, SPLIT3>;
-    auto kernel = fused_gemm_kernel<BN, STAGES, SPLIT3, SEG, KSPLIT>;
+    auto kernel = fused_gemm_kernel<BN, STAGES, SPLIT3, SEG, KSPLIT, BATCHED>;
+    if (BATCHED != (g.batch > 1)) return cudaErrorInvalidValue;
     // The shared-memory opt-in is per device: remember which devices have it.
     static std::mutex mu;
     static uint64_t configured = 0;
@@ -439,13 +471,23 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     CUtensorMap mA, mB, mA2, mB2;
     constexpr CUtensorMapSwizzle kSwA = CU_TENSOR_MAP_SWIZZLE_128B;
     constexpr CUtensorMapSwizzle kSwB = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-    if (!make_map(&mA, a_hi, g.M, g.K, g.lda, kBK, kBM, kSwA) || !make_map(&mB, b_hi, g.K, g.N, g.ldb, 32, kBK, kSwB))
-        return cudaErrorInvalidValue;
-    if (SPLIT3) {
-        if (!make_map(&mA2, g.A_small, g.M, g.K, g.lda, kBK, kBM, kSwA) ||
-            !make_map(&mB2, g.B_small, g.K, g.N, g.ldb, 32, kBK, kSwB))
+    if (BATCHED) {
+        // Products stored back to back: A_b = A + b * a_bstride, B_b = B + b * b_bstride.
+        if (!make_map_3d(&mA, a_hi, g.batch, g.M, g.K, g.lda, g.a_bstride, kBK, kBM, kSwA) ||
+            !make_map_3d(&mB, b_hi, g.batch, g.K, g.N, g.ldb, g.b_bstride, 32, kBK, kSwB))
+            return cudaErrorInvalidValue;
+        if (SPLIT3 && (!make_map_3d(&mA2, g.A_small, g.batch, g.M, g.K, g.lda, g.a_bstride, kBK, kBM, kSwA) ||
+                       !make_map_3d(&mB2, g.B_small, g.batch, g.K, g.N, g.ldb, g.b_bstride, 32, kBK, kSwB)))
             return cudaErrorInvalidValue;
     } else {
+        if (!make_map(&mA, a_hi, g.M, g.K, g.lda, kBK, kBM, kSwA) ||
+            !make_map(&mB, b_hi, g.K, g.N, g.ldb, 32, kBK, kSwB))
+            return cudaErrorInvalidValue;
+        if (SPLIT3 && (!make_map(&mA2, g.A_small, g.M, g.K, g.lda, kBK, kBM, kSwA) ||
+                       !make_map(&mB2, g.B_small, g.K, g.N, g.ldb, 32, kBK, kSwB)))
+            return cudaErrorInvalidValue;
+    }
+    if (!SPLIT3) {
         mA2 = mA;
         mB2 = mB;
     }
@@ -482,6 +524,16 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
         p.ks_stride = static_cast<long long>(g.M) * p.ks_ld;
     } else if (g.k_splits > 1) {
         return cudaErrorInvalidValue;
+    }
+    p.batch = 1;
+    if (BATCHED) {
+        const long long tiles = static_cast<long long>(p.num_tiles) * g.batch;
+        if (tiles >= (1ll << 31) || !g.ep_bstride) return cudaErrorInvalidValue;
+        p.batch = static_cast<int>(g.batch);
+        p.tiles_per_batch = p.num_tiles;
+        p.num_tiles = static_cast<int>(tiles);
+        p.out_bstride = g.out_bstride;
+        for (int i = 0; i < g.n_steps; ++i) p.ep_bstride[i] = g.ep_bstride[i];
     }
 
     const int grid = p.num_tiles < g.num_sms ? p.num_tiles : g.num_sms;
@@ -563,7 +615,7 @@ bool pair_wide_tiles(const GemmLaunch& g) {
 constexpr int kKsplitMinKb = 64;  // K >= 2017
 
 int fused_gemm_k_splits(const GemmLaunch& g) {
-    if (g.A2 || g.n_peers > 0 || use_pair_kernel(g)) return 1;
+    if (g.A2 || g.n_peers > 0 || g.batch > 1 || use_pair_kernel(g)) return 1;
     const long long rows = g.choice_rows > 0 ? g.choice_rows : g.M;
     const long long tiles = ((rows + kKsplitTileRows - 1) / kKsplitTileRows) *
                             ((g.N + kKsplitTileCols - 1) / kKsplitTileCols);
@@ -590,7 +642,7 @@ GemmPlan plan_fused_gemm(const GemmLaunch& g, int k_splits) {
     GemmPlan pl{};
     pl.products = g.A2 ? 2 : 1;
     pl.k_splits = 1;
-    if (g.A2) {
+    if (g.A2 && g.batch <= 1) {
         // Two products of one A in one kernel (callers run other cases as two
         // launches): 3xTF32 on 256 x 128 pair tiles; TF32 on 256 x 256 tiles
         // once they give every CTA pair a tile, else 256 x 128.
@@ -600,7 +652,7 @@ GemmPlan plan_fused_gemm(const GemmLaunch& g, int k_splits) {
         pl.tile_cols = g.precision == GPU_PRECISION_TF32 && tiles256 >= g.num_sms / 2 ? 256 : 128;
         return pl;
     }
-    if (use_pair_kernel(g)) {
+    if (g.batch <= 1 && use_pair_kernel(g)) {
         pl.kernel = MXB_KERNEL_CTA_PAIR;
         pl.tile_rows = 256;
         pl.tile_cols = g.precision == GPU_PRECISION_TF32 && pair_wide_tiles(g) ? 512 : 256;
@@ -608,6 +660,12 @@ GemmPlan plan_fused_gemm(const GemmLaunch& g, int k_splits) {
     }
     pl.kernel = MXB_KERNEL_SINGLE_CTA;
     pl.tile_rows = kBM;
+    if (g.batch > 1) {
+        // All products in one launch on 128 x 128 tiles (the caller batches
+        // only products too small to fill the GPU alone).
+        pl.tile_cols = 128;
+        return pl;
+    }
     if (k_splits > 1) {
         pl.k_splits = k_splits;
         pl.tile_cols = kKsplitTileCols;
@@ -628,6 +686,11 @@ cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
     if (pl.kernel == MXB_KERNEL_CTA_PAIR) {
         if (pl.products == 2) return x3 ? launch_pair_3xtf32(g, true, stream) : launch_pair_tf32_dual(g, stream);
         return x3 ? launch_pair_3xtf32(g, false, stream) : launch_pair_tf32(g, pl.tile_cols == 512, stream);
+    }
+    if (g.batch > 1) {
+        if (g.A2 || g.k_splits > 1 || g.n_peers > 0) return cudaErrorInvalidValue;
+        return x3 ? run_variant<128, 3, true, true, false, true>(g, stream)
+                  : run_variant<128, 6, false, false, false, true>(g, stream);
     }
     if (pl.k_splits > 1)
         return x3 ? run_variant<128, 3, true, true, true>(g, stream) : run_variant<128, 6, false, false, true>(g, stream);

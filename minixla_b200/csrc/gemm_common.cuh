@@ -62,6 +62,14 @@ struct FusedParams {
     int kb_per_split;
     float* ks_ws;
     long long ks_stride, ks_ld;
+    // Batched launch (single-CTA BATCHED instances): tile t is tile
+    // t % tiles_per_batch of product b = t / tiles_per_batch; out and each
+    // FULL operand step s advance by out_bstride / ep_bstride[s] elements per
+    // product, and the modulo rule counts rows from row_base + b * M.
+    int batch;
+    int tiles_per_batch;
+    long long out_bstride;
+    long long ep_bstride[MXB_MAX_EPILOGUE];
 };
 
 // Error bits written to the device error word.
@@ -130,7 +138,7 @@ __device__ __forceinline__ int lead_scalars(const float* p) {
 
 template <int W = 32>
 __device__ __forceinline__ void apply_epilogue(float (&v)[W], int row, int col, bool row_ok,
-                                               const FusedParams& p, const float* prod = nullptr) {
+                                               const FusedParams& p, const float* prod = nullptr, int b = 0) {
     static_assert(W % 4 == 0, "whole float4 groups");
     const bool full_cols = col + W <= p.N;
     for (int s = 0; s < p.n_steps; ++s) {
@@ -152,6 +160,7 @@ __device__ __forceinline__ void apply_epilogue(float (&v)[W], int row, int col, 
             if (!row_ok) continue;
             const long long ld = p.steps[s].ld_or_size;
             const float* src = ptr + static_cast<long long>(row) * ld + col;
+            if (b) src += b * p.ep_bstride[s];
             if (full_cols && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
                 const float4* s4 = reinterpret_cast<const float4*>(src);
 #pragma unroll
@@ -195,7 +204,8 @@ __device__ __forceinline__ void apply_epilogue(float (&v)[W], int row, int col, 
             if (!row_ok) continue;
             const unsigned long long size = static_cast<unsigned long long>(p.steps[s].ld_or_size);
             const unsigned long long base =
-                static_cast<unsigned long long>(row + p.row_base) * static_cast<unsigned long long>(p.N) + col;
+                static_cast<unsigned long long>(row + p.row_base + static_cast<long long>(b) * p.M) *
+                    static_cast<unsigned long long>(p.N) + col;
 #pragma unroll
             for (int i = 0; i < W; ++i)
                 if (col + i < p.N) v[i] += __ldg(ptr + (base + i) % size);
@@ -205,8 +215,8 @@ __device__ __forceinline__ void apply_epilogue(float (&v)[W], int row, int col, 
 
 template <int W = 32>
 __device__ __forceinline__ void store_row_chunk(const float (&v)[W], int row, int col,
-                                                const FusedParams& p) {
-    float* dst = p.out + static_cast<long long>(row) * p.ldo + col;
+                                                const FusedParams& p, long long off = 0) {
+    float* dst = p.out + off + static_cast<long long>(row) * p.ldo + col;
     if (col + W <= p.N && (p.ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
         float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
@@ -329,10 +339,12 @@ __device__ __forceinline__ void sum_slices4(float (&v)[4], const FusedParams& p,
 
 // Pulls this thread's rows of every full-matrix ADD operand, columns
 // col .. col + ncols, into L2 ahead of the epilogue's loads.
-__device__ __forceinline__ void prefetch_full_operands(int row, int col, int ncols, const FusedParams& p) {
+__device__ __forceinline__ void prefetch_full_operands(int row, int col, int ncols, const FusedParams& p,
+                                                       int b = 0) {
     for (int s = 0; s < p.n_steps; ++s) {
         if (p.steps[s].kind != MXB_EP_ADD_FULL) continue;
         const float* src = p.steps[s].ptr + static_cast<long long>(row) * p.steps[s].ld_or_size + col;
+        if (b) src += b * p.ep_bstride[s];
         for (int c = 0; c < ncols; c += 32)
             asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(src + c)));
     }
@@ -371,6 +383,24 @@ bool make_map(CUtensorMap* map, const float* base, long long rows, long long col
     const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, 2, const_cast<float*>(base), dims,
                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// `batch` row-major [rows, cols] fp32 matrices, `bstride` elements apart, row
+// pitch `ld`; box [1][box_rows][box_cols].  Rows and columns past a matrix's
+// edge read as zeros, never as the next matrix's.
+bool make_map_3d(CUtensorMap* map, const float* base, long long batch, long long rows, long long cols,
+                 long long ld, long long bstride, int box_cols, int box_rows, CUtensorMapSwizzle swizzle) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(batch)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(bstride) * 4};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, 3, const_cast<float*>(base), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 

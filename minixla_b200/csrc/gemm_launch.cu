@@ -57,8 +57,10 @@ static bool dual_in_one_kernel(const GpuCtx* ctx, const float* A, long long lda,
 int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out,
                 long long ldo, int M, int N, int K, const EpStepDev* steps, int n_steps, int precision,
                 cudaStream_t stream, const float* B_small_pre, long long row_base,
-                const Product* prod, int choice_rows, PeerRows* peers) {
+                const Product* prod, int choice_rows, PeerRows* peers, const BatchSpec* batch) {
     const int rows_for_choice = choice_rows > 0 ? choice_rows : M;
+    const long long nb = batch && batch->count > 1 ? batch->count : 1;
+    if (nb > 1 && (prod || (peers && peers->n > 0) || !batch->ep_bstride)) return MXB_E_ARG;
     if (prod && !dual_in_one_kernel(ctx, A, lda, M, N, K, *prod, precision)) {
         // Two launches: the second product into pooled workspace, then the
         // node reading it as a full add at the same step.
@@ -82,8 +84,9 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
         ctx->pool->release(ws, stream);
         return rc;
     }
-    const bool skinny = use_skinny_gemm(rows_for_choice, precision);
-    if (!skinny && use_tiny_gemm(rows_for_choice, N, K, precision)) {
+    // A batch was routed here by batched_in_one_launch: tensor-core kernels only.
+    const bool skinny = nb == 1 && use_skinny_gemm(rows_for_choice, precision);
+    if (nb == 1 && !skinny && use_tiny_gemm(rows_for_choice, N, K, precision)) {
         // Small enough that one plain CUDA-core launch beats the set-up of the tensor-core kernels.
         return cuda_ok(launch_tiny_gemm(A, lda, B, ldb, out, ldo, M, N, K, row_base, steps, n_steps, stream),
                        "tiny GEMM launch")
@@ -135,6 +138,13 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
         g.n_peers = peers->n;
     }
     g.choice_rows = rows_for_choice;
+    if (nb > 1) {
+        g.batch = nb;
+        g.a_bstride = static_cast<long long>(M) * lda;
+        g.b_bstride = static_cast<long long>(K) * ldb;
+        g.out_bstride = static_cast<long long>(M) * ldo;
+        g.ep_bstride = batch->ep_bstride;
+    }
     float* ws[4] = {nullptr, nullptr, nullptr, nullptr};  // 3xTF32 low parts of A, B, B2; K-split slices
     int rc = MXB_OK;
     g.k_splits = fused_gemm_k_splits(g);
@@ -146,7 +156,8 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
         g.ks_ws = ws[3];
     }
     if (rc == MXB_OK && precision == GPU_PRECISION_3XTF32) {
-        const size_t a_bytes = static_cast<size_t>(M) * lda * 4, b_bytes = static_cast<size_t>(K) * ldb * 4;
+        // Low parts of every product of a batch (stored back to back like A and B).
+        const size_t a_bytes = static_cast<size_t>(nb * M) * lda * 4, b_bytes = static_cast<size_t>(nb * K) * ldb * 4;
         const bool need_b2 = prod && !prod->B_small;
         ws[0] = static_cast<float*>(ctx->pool->alloc(a_bytes, stream));
         if (ws[0] && !B_small_pre) ws[1] = static_cast<float*>(ctx->pool->alloc(b_bytes, stream));
@@ -154,9 +165,9 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
             ws[2] = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(K) * prod->ldb * 4, stream));
         if (!ws[0] || (!B_small_pre && !ws[1]) || (need_b2 && !ws[2])) {
             rc = MXB_E_NOMEM;
-        } else if (!cuda_ok(launch_split_tf32(A, M, K, lda, ws[0], lda, ctx->num_sms, stream), "split A") ||
+        } else if (!cuda_ok(launch_split_tf32(A, nb * M, K, lda, ws[0], lda, ctx->num_sms, stream), "split A") ||
                    (!B_small_pre &&
-                    !cuda_ok(launch_split_tf32(B, K, N, ldb, ws[1], ldb, ctx->num_sms, stream), "split B")) ||
+                    !cuda_ok(launch_split_tf32(B, nb * K, N, ldb, ws[1], ldb, ctx->num_sms, stream), "split B")) ||
                    (need_b2 && !cuda_ok(launch_split_tf32(prod->B, K, N, prod->ldb, ws[2], prod->ldb, ctx->num_sms,
                                                           stream),
                                         "split B2"))) {
@@ -218,6 +229,24 @@ int build_epilogue(const Node* n, int M, int N, long long batch, long long bt,
     return k;
 }
 
+// Batched (rank-3) nodes: products that leave most of the GPU idle one at a
+// time run together in one launch of the single-CTA kernel (3-D tensor maps,
+// the product index from the tile index).  Larger products keep their own
+// launches on the kernels chosen for their shape, as do few-row products
+// (skinny kernels) and, in 3xTF32 mode, batches small enough in total for the
+// one-launch CUDA-core kernel.  MINIXLA_BATCH_LAUNCH=0 keeps one launch per
+// product.
+bool batched_in_one_launch(const GpuCtx* ctx, long long batch, int M, int N, int K, int precision) {
+    if (batch < 2) return false;
+    if (const char* v = getenv("MINIXLA_BATCH_LAUNCH"))
+        if (v[0] == '0') return false;
+    if (use_skinny_gemm(M, precision)) return false;
+    const long long rows_total = batch * M;
+    if (rows_total < (1ll << 31) && use_tiny_gemm(static_cast<int>(rows_total), N, K, precision)) return false;
+    const long long tiles = static_cast<long long>((M + 127) / 128) * ((N + 127) / 128);
+    return tiles < ctx->num_sms;
+}
+
 // Runs one matmul-anchored node on device buffers: `batch` products of
 // A[M,K] @ B[K,N] stored back to back (batch = 1 for 2-D nodes).
 int run_gemm_node(GpuCtx* ctx, const Node* n, const float* dA, int M, int K, const float* dB, int N,
@@ -230,6 +259,27 @@ int run_gemm_node(GpuCtx* ctx, const Node* n, const float* dA, int M, int K, con
     // Pitch padding treats the batches as one tall matrix (rows are contiguous).
     if (!tma_operand(ctx, dA, batch * M, K, a, stream) || !tma_operand(ctx, dB, batch * K, N, b, stream)) {
         rc = MXB_E_NOMEM;
+    }
+    if (rc == MXB_OK && !prod && batched_in_one_launch(ctx, batch, M, N, K, precision)) {
+        // Every product in one launch.  A FULL operand's step for product 1
+        // differs from product 0's by its batch stride (M * N for an operand
+        // holding every product, 0 for one M x N block); the modulo rule's
+        // row count advances by M per product inside the kernel.
+        EpStepDev steps[MXB_MAX_EPILOGUE], next[MXB_MAX_EPILOGUE];
+        long long bstride[MXB_MAX_EPILOGUE] = {};
+        int n_steps = 0;
+        if (n->op == OP_FUSED) {
+            n_steps = build_epilogue(n, M, N, batch, 0, dev_of, size_of, steps, absorbed);
+            build_epilogue(n, M, N, batch, 1, dev_of, size_of, next, absorbed);
+            for (int i = 0; i < n_steps; ++i)
+                if (steps[i].kind == MXB_EP_ADD_FULL) bstride[i] = next[i].ptr - steps[i].ptr;
+        }
+        BatchSpec bs;
+        bs.count = batch;
+        bs.ep_bstride = bstride;
+        rc = launch_gemm(ctx, a.ptr, a.ld, b.ptr, b.ld, dOut, N, M, N, K, steps, n_steps, precision, stream, nullptr,
+                         0, nullptr, 0, nullptr, &bs);
+        batch = 0;  // done
     }
     for (long long bt = 0; bt < batch && rc == MXB_OK; ++bt) {
         EpStepDev steps[MXB_MAX_EPILOGUE];

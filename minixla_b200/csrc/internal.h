@@ -47,6 +47,12 @@ struct GemmLaunch {
     int choice_rows;                   // rows the K split is chosen for (0: M)
     int k_splits;                      // > 1: single-CTA TF32 kernel with K split this many ways
     float* ks_ws;                      // k_splits * M * round4(N) floats
+    // batch > 1: that many products of this shape in one launch, the b-th at
+    // A + b * a_bstride, B + b * b_bstride (and the low parts likewise), out +
+    // b * out_bstride; FULL epilogue step s reads b * ep_bstride[s] further on.
+    long long batch;
+    long long a_bstride, b_bstride, out_bstride;
+    const long long* ep_bstride;
 };
 
 // Skinny GEMM (skinny_gemm.cu): few output rows, CUDA-core fp32, split over

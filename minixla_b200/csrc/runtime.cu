@@ -86,6 +86,7 @@ namespace mxb {
 // hanging off its inputs (runtime.c:17-84 and gpu_exec.c:339-362 do the same).
 struct SingleNode {
     int M = 0, N = 0, K = 0;
+    long long batch = 1;  // rank-3 and higher nodes (kernel timers only): products stored back to back
     float *dA = nullptr, *dB = nullptr, *dOut = nullptr;
     std::vector<float*> ops;
     std::unordered_map<const Node*, const float*> dev_of;
@@ -111,7 +112,8 @@ static float* upload(GpuCtx* ctx, const Tensor* t) {
     return d;
 }
 
-static int prepare_single(const Node* fused, GpuCtx* ctx, const char* who, SingleNode& s) {
+static int prepare_single(const Node* fused, GpuCtx* ctx, const char* who, SingleNode& s,
+                          bool allow_batch = false) {
     if (!fused || !ctx) {
         set_error("%s: NULL node or context", who);
         return MXB_E_ARG;
@@ -126,21 +128,29 @@ static int prepare_single(const Node* fused, GpuCtx* ctx, const char* who, Singl
         set_error("%s: matmul operands need host tensors", who);
         return MXB_E_ARG;
     }
-    if (a->ndim != 2 || b->ndim != 2) {
+    if (a->ndim != b->ndim || a->ndim < 2 || (a->ndim > 2 && !allow_batch)) {
         set_error("%s: only 2D tensors supported", who);
         return MXB_E_UNSUPPORTED;
     }
-    if (a->shape[1] != b->shape[0]) {
+    const int r = a->ndim;
+    if (a->shape[r - 1] != b->shape[r - 2]) {
         set_error("%s: incompatible matmul operand shapes", who);
         return MXB_E_ARG;
+    }
+    for (int d = 0; d < r - 2; ++d) {
+        if (a->shape[d] != b->shape[d]) {  // eval_fused's rule (graph.c:71-76)
+            set_error("%s: matmul batch dimension %d mismatch", who, d);
+            return MXB_E_ARG;
+        }
     }
     if (fused->op == OP_FUSED && fused->n_epilogue > MXB_MAX_EPILOGUE) {
         set_error("%s: too many epilogue steps", who);
         return MXB_E_UNSUPPORTED;
     }
-    s.M = a->shape[0];
-    s.K = a->shape[1];
-    s.N = b->shape[1];
+    s.M = a->shape[r - 2];
+    s.K = a->shape[r - 1];
+    s.N = b->shape[r - 1];
+    s.batch = static_cast<long long>(a->size) / (static_cast<long long>(s.M) * s.K);
     if (!(s.dA = upload(ctx, a)) || !(s.dB = upload(ctx, b))) return MXB_E_NOMEM;
     if (fused->op == OP_FUSED) {
         for (int e = 0; e < fused->n_epilogue; ++e) {
@@ -159,7 +169,7 @@ static int prepare_single(const Node* fused, GpuCtx* ctx, const char* who, Singl
             s.size_of[st.operand] = static_cast<long long>(t->size);
         }
     }
-    s.dOut = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(s.M) * s.N * 4, ctx->stream));
+    s.dOut = static_cast<float*>(ctx->pool->alloc(static_cast<size_t>(s.batch * s.M) * s.N * 4, ctx->stream));
     return s.dOut ? MXB_OK : MXB_E_NOMEM;
 }
 
@@ -205,11 +215,11 @@ static double time_fused(Node* root, GpuCtx* ctx, int warmup, int reps, int prec
     DeviceScope scope(ctx->device);
     SingleNode s;
     double best = -1.0;
-    int rc = prepare_single(root, ctx, who, s);
+    int rc = prepare_single(root, ctx, who, s, /*allow_batch=*/true);
     if (rc == MXB_OK) {
         for (int w = 0; w < warmup && rc == MXB_OK; ++w) {
             rc = run_gemm_node(ctx, root, s.dA, s.M, s.K, s.dB, s.N, s.dOut, s.dev_of, s.size_of, precision,
-                               ctx->stream);
+                               ctx->stream, s.batch);
             if (rc == MXB_OK) rc = finish(ctx);
         }
         double lo = 1e30;
@@ -223,7 +233,7 @@ static double time_fused(Node* root, GpuCtx* ctx, int warmup, int reps, int prec
             }
             cudaEventRecord(ctx->ev0, ctx->stream);
             rc = run_gemm_node(ctx, root, s.dA, s.M, s.K, s.dB, s.N, s.dOut, s.dev_of, s.size_of, precision,
-                               ctx->stream);
+                               ctx->stream, s.batch);
             cudaEventRecord(ctx->ev1, ctx->stream);
             if (rc == MXB_OK && cuda_ok(cudaEventSynchronize(ctx->ev1), "event synchronize")) {
                 float ms = 0.f;

@@ -290,10 +290,21 @@ struct PeerRows {
     int n = 0;
     bool pushed = false;
 };
+// `batch` (run_gemm_node): count > 1 products of this shape stored back to
+// back (A every M * lda, B every K * ldb, out every M * ldo floats) in one
+// launch of the single-CTA kernel; FULL step s advances ep_bstride[s] floats
+// per product.  The caller passes it only for shapes that launch_gemm would
+// run on the tensor-core kernels.
+struct BatchSpec {
+    long long count = 1;
+    const long long* ep_bstride = nullptr;
+};
 int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long long ldb, float* out, long long ldo,
                 int M, int N, int K, const EpStepDev* steps, int n_steps, int precision, cudaStream_t stream,
                 const float* B_small_pre = nullptr, long long row_base = 0, const Product* prod = nullptr,
-                int choice_rows = 0, PeerRows* peers = nullptr);
+                int choice_rows = 0, PeerRows* peers = nullptr, const BatchSpec* batch = nullptr);
+// Whether run_gemm_node runs `batch` products of M x N x K in one launch.
+bool batched_in_one_launch(const GpuCtx* ctx, long long batch, int M, int N, int K, int precision);
 int build_epilogue(const Node* n, int M, int N, long long batch, long long bt,
                    const std::unordered_map<const Node*, const float*>& dev_of,
                    const std::unordered_map<const Node*, long long>& size_of, EpStepDev* out,

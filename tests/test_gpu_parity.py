@@ -466,6 +466,48 @@ def test_skinny_rows_path(lib, gpu_ctx, M, form, NK, precision, monkeypatch, hos
     check(got, want, X3, f"skinny M={M}")
 
 
+@pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
+@pytest.mark.parametrize("bmnk", [(16, 250, 130, 300), (5, 384, 256, 1000), (64, 128, 128, 128)])
+def test_batched_one_launch(lib, gpu_ctx, bmnk, precision, monkeypatch):
+    """A rank-3 fused node whose products are small runs all of them in one
+    launch (3-D tensor maps: a partial row tile or k-block of one product
+    reads zeros, not the next product): ADD operands holding every product,
+    one shared M x N block, a [N] row and an odd size read by the modulo rule
+    over the flat batched index (graph.c:100-105), ragged M, N and K.  The
+    result matches the oracle and the one-launch-per-product loop
+    (MINIXLA_BATCH_LAUNCH=0), and in TF32 mode the whole batch is one kernel
+    launch."""
+    from tests.graph_eval import host_graph, oracle_eval
+
+    bt, M, N, K = bmnk
+    g = np.random.default_rng(bt * 1000 + M)
+    inputs = {"A": g.uniform(-1, 1, (bt, M, K)).astype(np.float32),
+              "B": g.uniform(-1, 1, (bt, K, N)).astype(np.float32),
+              "C": g.normal(0, 1, (bt, M, N)).astype(np.float32),
+              "blk": g.uniform(-1, 1, (M, N)).astype(np.float32),
+              "bias": g.normal(0, 0.5, (N,)).astype(np.float32),
+              "odd": g.uniform(-1, 1, (11,)).astype(np.float32)}
+
+    def build(b, t):
+        return b.fused(t["A"], t["B"], [("add", t["C"]), ("relu", None), ("add", t["blk"]), ("add", t["bias"]),
+                                        ("add", t["odd"])])
+
+    hg, root = host_graph(inputs, build)
+    want = oracle_eval(inputs, build)
+    n0 = lib.mxb_launch_count()
+    got = run_execute(lib, gpu_ctx, root, precision)
+    launches = lib.mxb_launch_count() - n0
+    check(got, want, precision, f"batched {bmnk}")
+    if precision == TF32:
+        assert launches == 1, f"{launches} launches for {bt} products"
+    monkeypatch.setenv("MINIXLA_BATCH_LAUNCH", "0")
+    n0 = lib.mxb_launch_count()
+    looped = run_execute(lib, gpu_ctx, root, precision)
+    if precision == TF32:
+        assert lib.mxb_launch_count() - n0 == bt
+    check(got, looped, precision, f"batched {bmnk} one launch vs loop")
+
+
 @pytest.mark.parametrize("M", [9, 16])
 @pytest.mark.parametrize("NK", [(1000, 777), (2501, 8000)], ids=["short_k", "k_split"])
 def test_few_rows_tensor_path(lib, gpu_ctx, M, NK, host_threads):
