@@ -95,6 +95,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // K split: the reduce kernel, launched next as a programmatic dependent,
+    // may be scheduled now; it waits for this grid's completion itself.
+    if (KSPLIT) asm volatile("griddepcontrol.launch_dependents;");
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -432,6 +435,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // the node's epilogue.  Thread i takes four consecutive columns of one row,
 // so a warp reads 512 contiguous bytes of a slice row; every SM takes part.
 __global__ void __launch_bounds__(256) ksplit_reduce_kernel(const __grid_constant__ FusedParams p) {
+    // Launched as a programmatic dependent of the split GEMM: its CTAs are
+    // resident early, and this wait returns once that grid has finished and
+    // its slices are visible.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int groups = (p.N + 3) / 4;
     const long long total = static_cast<long long>(p.M) * groups;
     for (long long i = blockIdx.x * 256ll + threadIdx.x; i < total; i += static_cast<long long>(gridDim.x) * 256) {
@@ -445,6 +452,14 @@ __global__ void __launch_bounds__(256) ksplit_reduce_kernel(const __grid_constan
 }
 
 // ------------------------------------------------------------------ host side
+
+// The reduce kernel of a K split is launched as a programmatic dependent of
+// the GEMM (it starts early and waits on griddepcontrol.wait);
+// MINIXLA_KSPLIT_PDL=0 launches it in plain stream order.
+bool ksplit_pdl_enabled() {
+    const char* v = getenv("MINIXLA_KSPLIT_PDL");
+    return !(v && v[0] == '0');
+}
 
 template <int BN, int STAGES, bool SPLIT3, bool SEG, bool KSPLIT = false, bool BATCHED = false>
 cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
@@ -544,7 +559,17 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         const long long items = static_cast<long long>(g.M) * ((g.N + 3) / 4);
         const long long blocks = std::min<long long>((items + 255) / 256, 8ll * g.num_sms);
-        ksplit_reduce_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(p);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+        cfg.blockDim = dim3(256);
+        cfg.stream = stream;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr.val.programmaticStreamSerializationAllowed = ksplit_pdl_enabled() ? 1 : 0;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, ksplit_reduce_kernel, p);
+        if (e != cudaSuccess) return e;
         note_launch();
     }
     return cudaGetLastError();
