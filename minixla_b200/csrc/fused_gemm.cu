@@ -456,6 +456,12 @@ __global__ void __launch_bounds__(256) ksplit_reduce_kernel(const __grid_constan
 // The reduce kernel of a K split is launched as a programmatic dependent of
 // the GEMM (it starts early and waits on griddepcontrol.wait);
 // MINIXLA_KSPLIT_PDL=0 launches it in plain stream order.
+// MINIXLA_BATCH_WIDE=0 keeps batched TF32 launches on 128-wide tiles.
+bool batch_wide_tiles() {
+    const char* v = getenv("MINIXLA_BATCH_WIDE");
+    return !(v && v[0] == '0');
+}
+
 bool ksplit_pdl_enabled() {
     const char* v = getenv("MINIXLA_KSPLIT_PDL");
     return !(v && v[0] == '0');
@@ -686,9 +692,11 @@ GemmPlan plan_fused_gemm(const GemmLaunch& g, int k_splits) {
     pl.kernel = MXB_KERNEL_SINGLE_CTA;
     pl.tile_rows = kBM;
     if (g.batch > 1) {
-        // All products in one launch on 128 x 128 tiles (the caller batches
-        // only products too small to fill the GPU alone).
-        pl.tile_cols = 128;
+        // All products in one launch (the caller batches only products too
+        // small to fill the GPU alone): 128 x 256 tiles in TF32 mode from
+        // N = 512 (32 x 1024^3: 197 -> 162 us; at N = 256 they were no
+        // faster), else 128 x 128.
+        pl.tile_cols = g.precision == GPU_PRECISION_TF32 && g.N >= 512 && batch_wide_tiles() ? 256 : 128;
         return pl;
     }
     if (k_splits > 1) {
@@ -714,8 +722,9 @@ cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
     }
     if (g.batch > 1) {
         if (g.A2 || g.k_splits > 1 || g.n_peers > 0) return cudaErrorInvalidValue;
-        return x3 ? run_variant<128, 3, true, true, false, true>(g, stream)
-                  : run_variant<128, 6, false, false, false, true>(g, stream);
+        if (x3) return run_variant<128, 3, true, true, false, true>(g, stream);
+        return pl.tile_cols == 256 ? run_variant<256, 4, false, false, false, true>(g, stream)
+                                   : run_variant<128, 6, false, false, false, true>(g, stream);
     }
     if (pl.k_splits > 1)
         return x3 ? run_variant<128, 3, true, true, true>(g, stream) : run_variant<128, 6, false, false, true>(g, stream);
