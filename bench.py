@@ -65,6 +65,9 @@ def parse():
     p.add_argument("--shape", type=int, default=0,
                    help="per-GPU M = N = K override (profiling on a smaller case); 0 = 8192")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--batched", default="",
+                   help="time a rank-3 fused node relu(A.B + C) of 'B,M,N,K' through gpu_time_kernel_ms, both modes, "
+                        "one launch for the batch and one launch per product (one JSON line each)")
     p.add_argument("--mnk", default="",
                    help="with --sweep: time only this product, 'M,N,K' (no config-4 MLP; for profiling one kernel)")
     return p.parse_args()
@@ -1014,9 +1017,59 @@ def run_mlp(args):
     return 0
 
 
+def run_batched(args):
+    """A rank-3 fused node relu(A.B + C) -- `batch` products of M x N x K,
+    eval_fused's batch loop (graph.c:80-113) -- timed kernel-only through
+    gpu_time_kernel_ms: every product in one launch, and one launch per
+    product (MINIXLA_BATCH_LAUNCH=0; that form's time includes the host's
+    preparation of each launch, as a caller would see it).  Checked against
+    the oracle on the first and last products."""
+    import numpy as np
+
+    from minixla_b200 import datagen
+    from minixla_b200 import lib as mlib
+    from minixla_b200.abi import OP_ADD, OP_RELU, HostGraph, free_host_tensor, tensor_to_numpy
+    from oracle.bindings import fused_oracle
+
+    bt, M, N, K = (int(v) for v in args.batched.split(","))
+    lib = mlib.load()
+    ctx = lib.gpu_ctx_create_on(0)
+    A = datagen.uniform((bt, M, K), 0)
+    B = datagen.uniform((bt, K, N), 1)
+    Cm = datagen.normal((bt, M, N), 2)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A), hg.input_node(B), [(OP_ADD, hg.input_node(Cm)), (OP_RELU, None)])
+    flops = 2.0 * bt * M * N * K
+    for prec_name, prec in (("tf32", mlib.GPU_PRECISION_TF32), ("3xtf32", mlib.GPU_PRECISION_3XTF32)):
+        lib.gpu_ctx_set_precision(ctx, prec)
+        t = lib.gpu_execute(root, ctx)
+        if not t:
+            raise RuntimeError(mlib.last_error())
+        got = tensor_to_numpy(t)
+        free_host_tensor(t)
+        err = 0.0
+        for b in (0, bt - 1):
+            want = fused_oracle(A[b], B[b], [("add", Cm[b]), ("relu",)])
+            err = max(err, float(np.linalg.norm(got[b] - want) / np.linalg.norm(want)))
+        line = {"batched": "fused relu(A.B+C), rank 3", "batch": bt, "M": M, "N": N, "K": K,
+                "precision": prec_name, "rel_err_first_last": err}
+        for form, env in (("one_launch", "1"), ("launch_per_product", "0")):
+            os.environ["MINIXLA_BATCH_LAUNCH"] = env
+            ms = lib.gpu_time_kernel_ms(root, ctx, 3, 10)
+            if ms <= 0:
+                raise RuntimeError(mlib.last_error())
+            line[form] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12}
+        os.environ.pop("MINIXLA_BATCH_LAUNCH", None)
+        print(json.dumps(line), flush=True)
+    lib.gpu_ctx_destroy(ctx)
+    return 0
+
+
 def main():
     args = parse()
     rank, local_rank, world = env_rank()
+    if args.batched:
+        return run_batched(args)
     if args.sweep:
         return run_sweep(args)
     if args.kernels:
