@@ -65,12 +65,15 @@ struct PairCfg {
 // PUSH: the epilogue also writes each tile's rows into the peers' copies
 // (FusedParams::peer_out), a separate instance so the other launches keep
 // their registers.
-template <int STAGES, int BN, bool DUAL, int EPI, bool PUSH>
+// BATCHED: p.batch products of one shape in one launch, A and B as 3-D tensor
+// maps (third coordinate: the product), as in the single-CTA kernel.
+template <int STAGES, int BN, bool DUAL, int EPI, bool PUSH, bool BATCHED = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, DUAL, EPI>::kThreadsPerCta, 1)
     fused_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                            const __grid_constant__ FusedParams p) {
     using C = PairCfg<STAGES, BN, DUAL, EPI>;
+    static_assert(!(BATCHED && (DUAL || PUSH)), "a batched launch has one product and no peer rows");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -129,7 +132,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             bool ok = true;
             for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
                 int mb, nb;
-                tile_coords(t, p, mb, nb);
+                int b = 0;
+                if (BATCHED) {
+                    b = t / p.tiles_per_batch;
+                    tile_coords(t - b * p.tiles_per_batch, p, mb, nb);
+                } else {
+                    tile_coords(t, p, mb, nb);
+                }
                 const int m0 = mb * 256 + static_cast<int>(rank) * 128;
                 // CTA r stages, for sub-MMA h, B columns nb*BN + h*kSubN + r*kSubN/2 ..
                 // + kSubN/2, so accumulator column c is output column nb*BN + c.
@@ -145,11 +154,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                     if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * C::kStageBytes);
                     const uint32_t fb = mapa_shared(full_bar(stage), 0);
                     const int k0 = kb * kBK;
-                    tma_load_2d_pair(smem_addr(st), &tmA, fb, k0, m0);
+                    if (BATCHED) {
+                        tma_load_3d_pair(smem_addr(st), &tmA, fb, k0, m0, b);
 #pragma unroll
-                    for (int j = 0; j < BN / 64; ++j)
-                        tma_load_2d_pair(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb,
-                                         n0 + (j / C::kSubBoxes) * C::kSubN + 32 * (j % C::kSubBoxes), k0);
+                        for (int j = 0; j < BN / 64; ++j)
+                            tma_load_3d_pair(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb,
+                                             n0 + (j / C::kSubBoxes) * C::kSubN + 32 * (j % C::kSubBoxes), k0, b);
+                    } else {
+                        tma_load_2d_pair(smem_addr(st), &tmA, fb, k0, m0);
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j)
+                            tma_load_2d_pair(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb,
+                                             n0 + (j / C::kSubBoxes) * C::kSubN + 32 * (j % C::kSubBoxes), k0);
+                    }
                     if (DUAL) {
 #pragma unroll
                         for (int j = 0; j < BN / 64; ++j)
@@ -239,7 +256,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
         uint32_t acc_phase = 0;
         for (int t = pair; t < p.num_tiles; t += num_pairs) {
             int mb, nb;
-            tile_coords(t, p, mb, nb);
+            int b = 0;
+            if (BATCHED) {
+                b = t / p.tiles_per_batch;
+                tile_coords(t - b * p.tiles_per_batch, p, mb, nb);
+            } else {
+                tile_coords(t, p, mb, nb);
+            }
+            const long long out_off = BATCHED ? b * p.out_bstride : 0;
             const int row = mb * 256 + row_in_tile;
             const bool row_ok = row < p.M;
             const int col0 = nb * BN;
@@ -248,7 +272,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             // C rows into L2: during the k-loop when it is short, else once the accumulator is ready.
             const bool fetch = row_ok && chunks > c_first;
             if (fetch && p.num_kb <= kShortKb)
-                prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p);
+                prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p, b);
             const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
             const bool got = !stop && mbar_wait_cluster(tfull_bar(acc), acc_phase, p.timeout_ns);
             if (!__all_sync(0xffffffffu, got)) {
@@ -257,7 +281,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             }
             tc_fence_after();
             if (fetch && p.num_kb > kShortKb)
-                prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p);
+                prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p, b);
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                    static_cast<uint32_t>(acc * C::kAccCols);
             if (chunks <= c_first) {
@@ -292,8 +316,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                 if (DUAL)
                     apply_epilogue(v, row, col, row_ok, p, w);
                 else
-                    apply_epilogue(v, row, col, row_ok, p);
-                if (row_ok) store_row_chunk(v, row, col, p);
+                    apply_epilogue(v, row, col, row_ok, p, nullptr, b);
+                if (row_ok) store_row_chunk(v, row, col, p, out_off);
             }
             if (PUSH) {
                 // The accumulator is already released: these copies overlap the next tile's k-loop.
@@ -318,10 +342,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
 
 // ------------------------------------------------------------------ host side
 
-template <int STAGES, int BN, bool DUAL, int EPI = 4, bool PUSH = false>
+template <int STAGES, int BN, bool DUAL, int EPI = 4, bool PUSH = false, bool BATCHED = false>
 cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
     using C = PairCfg<STAGES, BN, DUAL, EPI>;
-    auto kernel = fused_gemm_pair_kernel<STAGES, BN, DUAL, EPI, PUSH>;
+    auto kernel = fused_gemm_pair_kernel<STAGES, BN, DUAL, EPI, PUSH, BATCHED>;
+    if (BATCHED != (g.batch > 1)) return cudaErrorInvalidValue;
     static std::mutex mu;
     static uint64_t configured = 0;
     static int max_clusters[64] = {0};
@@ -364,8 +389,14 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
     constexpr CUtensorMapSwizzle kSwA = CU_TENSOR_MAP_SWIZZLE_128B;
     constexpr CUtensorMapSwizzle kSwB = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
     CUtensorMap mA, mB, mA2, mB2;
-    if (!make_map(&mA, g.A, g.M, g.K, g.lda, kBK, 128, kSwA) || !make_map(&mB, g.B, g.K, g.N, g.ldb, 32, kBK, kSwB))
+    if (BATCHED) {
+        if (!make_map_3d(&mA, g.A, g.batch, g.M, g.K, g.lda, g.a_bstride, kBK, 128, kSwA) ||
+            !make_map_3d(&mB, g.B, g.batch, g.K, g.N, g.ldb, g.b_bstride, 32, kBK, kSwB))
+            return cudaErrorInvalidValue;
+    } else if (!make_map(&mA, g.A, g.M, g.K, g.lda, kBK, 128, kSwA) ||
+               !make_map(&mB, g.B, g.K, g.N, g.ldb, 32, kBK, kSwB)) {
         return cudaErrorInvalidValue;
+    }
     if (DUAL) {
         // The second product shares A (same rows, K and pitch); only B2 has a map of its own.
         if (g.A2 != g.A || g.K2 != g.K || g.lda2 != g.lda || !g.B2 ||
@@ -407,6 +438,17 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
         p.push_vec = vec ? 1 : 0;
     }
 
+    p.batch = 1;
+    if (BATCHED) {
+        const long long tiles = static_cast<long long>(p.num_tiles) * g.batch;
+        if (tiles >= (1ll << 31) || !g.ep_bstride) return cudaErrorInvalidValue;
+        p.batch = static_cast<int>(g.batch);
+        p.tiles_per_batch = p.num_tiles;
+        p.num_tiles = static_cast<int>(tiles);
+        p.out_bstride = g.out_bstride;
+        for (int i = 0; i < g.n_steps; ++i) p.ep_bstride[i] = g.ep_bstride[i];
+    }
+
     const int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;
     kernel<<<2 * pairs, C::kThreadsPerCta, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p);
     note_launch();
@@ -416,6 +458,10 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_pair_tf32(const GemmLaunch& g, bool wide_tiles, cudaStream_t stream) {
+    if (g.batch > 1) {
+        if (g.n_peers > 0 || g.A2) return cudaErrorInvalidValue;
+        return run_pair_variant<6, 256, false, 4, false, true>(g, stream);
+    }
     if (g.n_peers > 0)
         return wide_tiles ? run_pair_variant<4, 512, false, 4, true>(g, stream)
                           : run_pair_variant<6, 256, false, 4, true>(g, stream);
