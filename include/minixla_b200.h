@@ -325,10 +325,16 @@ typedef struct {
     int kernel;                /* MXB_KERNEL_*                                                */
     int tile_rows, tile_cols;  /* output tile of one CTA (pair: of the two CTAs)              */
     int k_splits;              /* CTAs sharing one tile's K range (1: none)                   */
-    int products;              /* 1 (mxb_gemm_plan_for reports single products)               */
+    int products;              /* products per launch: 1, or the batch when a rank-3 node's  */
+                               /* products all run in one launch                             */
     int reserved[3];
 } mxb_gemm_plan;
 MXB_API int mxb_gemm_plan_for(int M, int N, int K, int precision, int num_sms, mxb_gemm_plan* plan);
+/* The same for a rank-3 node of `batch` products of M x N x K (eval_fused's
+ * batch loop, graph.c:80-113): products = batch when they all run in one
+ * launch, else the single-product plan (one launch per product). */
+MXB_API int mxb_gemm_plan_batch_for(long long batch, int M, int N, int K, int precision, int num_sms,
+                                    mxb_gemm_plan* plan);
 
 /* Standalone element-wise nodes (tensor.c:64-86 and 110-120 semantics):
  * out[i] = a[i] + b[i % b_size]  and  out[i] = x[i] > 0 ? x[i] : 0. */

@@ -236,7 +236,7 @@ int build_epilogue(const Node* n, int M, int N, long long batch, long long bt,
 // (skinny kernels) and, in 3xTF32 mode, batches small enough in total for the
 // one-launch CUDA-core kernel.  MINIXLA_BATCH_LAUNCH=0 keeps one launch per
 // product.
-bool batched_in_one_launch(const GpuCtx* ctx, long long batch, int M, int N, int K, int precision) {
+bool batched_in_one_launch(int num_sms, long long batch, int M, int N, int K, int precision) {
     if (batch < 2) return false;
     if (const char* v = getenv("MINIXLA_BATCH_LAUNCH"))
         if (v[0] == '0') return false;
@@ -244,7 +244,7 @@ bool batched_in_one_launch(const GpuCtx* ctx, long long batch, int M, int N, int
     const long long rows_total = batch * M;
     if (rows_total < (1ll << 31) && use_tiny_gemm(static_cast<int>(rows_total), N, K, precision)) return false;
     const long long tiles = static_cast<long long>((M + 127) / 128) * ((N + 127) / 128);
-    return tiles < ctx->num_sms;
+    return tiles < num_sms;
 }
 
 // Runs one matmul-anchored node on device buffers: `batch` products of
@@ -260,7 +260,7 @@ int run_gemm_node(GpuCtx* ctx, const Node* n, const float* dA, int M, int K, con
     if (!tma_operand(ctx, dA, batch * M, K, a, stream) || !tma_operand(ctx, dB, batch * K, N, b, stream)) {
         rc = MXB_E_NOMEM;
     }
-    if (rc == MXB_OK && !prod && batched_in_one_launch(ctx, batch, M, N, K, precision)) {
+    if (rc == MXB_OK && !prod && batched_in_one_launch(ctx->num_sms, batch, M, N, K, precision)) {
         // Every product in one launch.  A FULL operand's step for product 1
         // differs from product 0's by its batch stride (M * N for an operand
         // holding every product, 0 for one M x N block); the modulo rule's

@@ -529,6 +529,30 @@ int mxb_fused_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, l
                               stream, nullptr);
 }
 
+int mxb_gemm_plan_batch_for(long long batch, int M, int N, int K, int precision, int num_sms, mxb_gemm_plan* plan) {
+    if (!plan || batch < 1 || M < 1 || N < 1 || K < 1 || num_sms < 2 || !mxb::valid_precision(precision)) {
+        set_error("mxb_gemm_plan_batch_for: invalid arguments");
+        return MXB_E_ARG;
+    }
+    if (!mxb::batched_in_one_launch(num_sms, batch, M, N, K, precision)) return mxb_gemm_plan_for(M, N, K, precision, num_sms, plan);
+    memset(plan, 0, sizeof(*plan));
+    mxb::GemmLaunch g{};
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.precision = precision;
+    g.num_sms = num_sms;
+    g.choice_rows = M;
+    g.batch = batch;
+    const mxb::GemmPlan pl = mxb::plan_fused_gemm(g, 1);
+    plan->kernel = pl.kernel;
+    plan->tile_rows = pl.tile_rows;
+    plan->tile_cols = pl.tile_cols;
+    plan->k_splits = 1;
+    plan->products = static_cast<int>(std::min<long long>(batch, 1ll << 30));
+    return MXB_OK;
+}
+
 int mxb_gemm_plan_for(int M, int N, int K, int precision, int num_sms, mxb_gemm_plan* plan) {
     if (!plan || M < 1 || N < 1 || K < 1 || num_sms < 2 || !mxb::valid_precision(precision)) {
         set_error("mxb_gemm_plan_for: invalid arguments");

@@ -304,7 +304,7 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
                 const float* B_small_pre = nullptr, long long row_base = 0, const Product* prod = nullptr,
                 int choice_rows = 0, PeerRows* peers = nullptr, const BatchSpec* batch = nullptr);
 // Whether run_gemm_node runs `batch` products of M x N x K in one launch.
-bool batched_in_one_launch(const GpuCtx* ctx, long long batch, int M, int N, int K, int precision);
+bool batched_in_one_launch(int num_sms, long long batch, int M, int N, int K, int precision);
 int build_epilogue(const Node* n, int M, int N, long long batch, long long bt,
                    const std::unordered_map<const Node*, const float*>& dev_of,
                    const std::unordered_map<const Node*, long long>& size_of, EpStepDev* out,

@@ -69,6 +69,7 @@ PROTOTYPES = {
     "mxb_ipc_free": (C.c_int, [C.c_int, C.c_void_p]),
     "mxb_gather_push_count": (C.c_ulonglong, []),
     "mxb_gemm_plan_for": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "mxb_gemm_plan_batch_for": (C.c_int, [C.c_longlong, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p]),
     "mxb_add": (C.c_int, [C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]),
     "mxb_relu": (C.c_int, [C.c_void_p, C.c_void_p, C.c_longlong, C.c_void_p, C.c_void_p]),
     "mxb_check_device_error": (C.c_int, [C.c_void_p]),
@@ -94,10 +95,14 @@ class GemmPlan(C.Structure):
     ]
 
 
-def gemm_plan(M: int, N: int, K: int, precision: int, num_sms: int = 148) -> GemmPlan:
-    """What mxb_gemm_plan_for reports for an M x N x K product (host-only)."""
+def gemm_plan(M: int, N: int, K: int, precision: int, num_sms: int = 148, batch: int = 0) -> GemmPlan:
+    """What mxb_gemm_plan_for (batch = 0) or mxb_gemm_plan_batch_for reports
+    for M x N x K products (host-only)."""
     plan = GemmPlan()
-    rc = load().mxb_gemm_plan_for(M, N, K, precision, num_sms, C.byref(plan))
+    if batch:
+        rc = load().mxb_gemm_plan_batch_for(batch, M, N, K, precision, num_sms, C.byref(plan))
+    else:
+        rc = load().mxb_gemm_plan_for(M, N, K, precision, num_sms, C.byref(plan))
     if rc != 0:
         raise ValueError(f"mxb_gemm_plan_for: {last_error()}")
     return plan

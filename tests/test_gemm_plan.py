@@ -82,3 +82,31 @@ def test_plan_depends_on_sm_count():
 def test_plan_rejects_bad_arguments(args):
     with pytest.raises(ValueError):
         mlib.gemm_plan(*args)
+
+
+# (batch, M, N, K, precision) -> (kernel, tile_rows, tile_cols, products per launch)
+BATCH_CASES = [
+    ((64, 256, 256, 256, TF32), (SINGLE, 128, 128, 64)),     # small products: one launch
+    ((64, 256, 256, 256, X3), (SINGLE, 128, 128, 64)),
+    ((16, 250, 130, 300, TF32), (SINGLE, 128, 128, 16)),
+    ((5, 384, 520, 1000, TF32), (SINGLE, 128, 256, 5)),      # N >= 512: 128 x 256 tiles
+    ((32, 1024, 1024, 1024, TF32), (PAIR, 256, 256, 32)),    # from 1024 x 1024: CTA pairs
+    ((32, 1024, 1024, 1024, X3), (SINGLE, 128, 128, 32)),
+    ((8, 2048, 2048, 2048, TF32), (PAIR, 256, 256, 1)),      # fills the GPU: one launch per product
+    ((4, 8, 4096, 4096, TF32), (SKINNY, 8, 128, 1)),         # few rows: skinny kernel per product
+    ((4, 64, 64, 64, X3), (TINY, 32, 32, 1)),                # tiny in total (3xTF32)
+]
+
+
+@pytest.mark.parametrize("shape,want", BATCH_CASES, ids=[f"{b}x{m}x{n}x{k}-{'tf32' if p == TF32 else '3x'}"
+                                                         for (b, m, n, k, p), _ in BATCH_CASES])
+def test_plan_batched(shape, want, monkeypatch):
+    for var in ("MINIXLA_BATCH_LAUNCH", "MINIXLA_BATCH_PAIR", "MINIXLA_BATCH_WIDE", "MINIXLA_SKINNY_MAX_ROWS",
+                "MINIXLA_TINY_MAX_MNK", "MINIXLA_GEMM_VARIANT"):
+        monkeypatch.delenv(var, raising=False)
+    b, m, n, k, prec = shape
+    p = mlib.gemm_plan(m, n, k, prec, batch=b)
+    assert (p.kernel, p.tile_rows, p.tile_cols, p.products) == want
+    monkeypatch.setenv("MINIXLA_BATCH_LAUNCH", "0")
+    assert mlib.gemm_plan(m, n, k, prec, batch=b).products == 1
+
