@@ -279,7 +279,9 @@ int run_gemm_node(GpuCtx* ctx, const Node* n, const float* dA, int M, int K, con
         bs.ep_bstride = bstride;
         rc = launch_gemm(ctx, a.ptr, a.ld, b.ptr, b.ld, dOut, N, M, N, K, steps, n_steps, precision, stream, nullptr,
                          0, nullptr, 0, nullptr, &bs);
-        batch = 0;  // done
+        ctx->pool->release(a.owned, stream);
+        ctx->pool->release(b.owned, stream);
+        return rc;
     }
     for (long long bt = 0; bt < batch && rc == MXB_OK; ++bt) {
         EpStepDev steps[MXB_MAX_EPILOGUE];
