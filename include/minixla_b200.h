@@ -273,8 +273,8 @@ MXB_API int mxb_fused_gemm_noalloc(const float* A, long long lda,
  * GPU's rows like mxb_fused_gemm into `out` (its rows of its own copy of the
  * full output) and writes the same rows into every peer GPU's copy:
  * peer_out[i] is where those rows start in peer i's copy (same ldo), a
- * device pointer opened with mxb_ipc_open.  In TF32 mode on the CTA-pair
- * kernel (M >= 256 with enough tiles to occupy the GPU) the epilogue warps
+ * device pointer opened with mxb_ipc_open.  On the CTA-pair kernels (either
+ * mode; M >= 256 with enough tiles to occupy the GPU) the epilogue warps
  * store each finished tile to the peers over NVLink while the tensor cores
  * run the next tile; every other kernel is followed by one strided copy per
  * peer on the same stream.  Values are identical either way.  Peer rows are

@@ -535,7 +535,7 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.row_base = g.row_base;
     p.timeout_ns = g.timeout_ns;
     p.err = g.err;
-    if (g.n_peers > 0) return cudaErrorInvalidValue;  // only the TF32 CTA-pair kernel writes peer rows
+    if (g.n_peers > 0) return cudaErrorInvalidValue;  // only the CTA-pair kernels write peer rows
     for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
     p.splits = 1;
     p.kb_per_split = p.num_kb;
@@ -672,7 +672,7 @@ int fused_gemm_k_splits(const GemmLaunch& g) {
 bool fused_gemm_pushes_rows(const GemmLaunch& g) {
     const char* v = getenv("MINIXLA_GATHER_PUSH");
     if (v && v[0] == '0') return false;
-    return !g.A2 && g.precision == GPU_PRECISION_TF32 && use_pair_kernel(g);
+    return !g.A2 && g.batch <= 1 && use_pair_kernel(g);
 }
 
 GemmPlan plan_fused_gemm(const GemmLaunch& g, int k_splits) {

@@ -48,7 +48,16 @@ struct Pair3Cfg {
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-template <int STAGES, bool DUAL>
+// The peer copies as a call of their own: this kernel runs at 168 registers
+// a thread, and inlined they pushed the segment sums into local memory.
+__device__ __noinline__ void push_rows_apart(const FusedParams& p, int row0, int c0, int c1) {
+    push_rows<2>(p, row0, c0, c1);
+}
+
+// PUSH: after a tile's last segment each epilogue warp also copies its 32
+// rows x 128 columns into the peers' copies (FusedParams::peer_out), with the
+// accumulator already released; a separate instance keeps the others' code.
+template <int STAGES, bool DUAL, bool PUSH = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
     fused_gemm_pair3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmAs, const __grid_constant__ CUtensorMap tmBs,
@@ -56,6 +65,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
                             const __grid_constant__ FusedParams p) {
     using C = Pair3Cfg<STAGES, DUAL>;
     constexpr int BN = C::kBN;
+    static_assert(!(PUSH && DUAL), "peer rows are written for one product");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -312,8 +322,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
                 if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
                 acc ^= 1;
                 if (acc == 0) acc_phase ^= 1u;
+                if (PUSH && last) {
+                    // Overlaps the next tile's MMAs: the accumulator is released.
+                    const int c_end = col0 + 128 < p.N ? col0 + 128 : p.N;
+                    push_rows_apart(p, mb * 256 + row_in_tile - lane, col0, c_end);
+                }
             }
         }
+        // Peer stores performed before the kernel counts as finished.
+        if (PUSH) __threadfence_system();
     }
 
     __syncwarp();
@@ -327,10 +344,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
 
 // ------------------------------------------------------------------ host side
 
-template <int STAGES, bool DUAL>
+template <int STAGES, bool DUAL, bool PUSH = false>
 cudaError_t run_pair3_variant(const GemmLaunch& g, cudaStream_t stream) {
     using C = Pair3Cfg<STAGES, DUAL>;
-    auto kernel = fused_gemm_pair3_kernel<STAGES, DUAL>;
+    auto kernel = fused_gemm_pair3_kernel<STAGES, DUAL, PUSH>;
     static std::mutex mu;
     static uint64_t configured = 0;
     static int max_clusters[64] = {0};
@@ -404,8 +421,19 @@ cudaError_t run_pair3_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.row_base = g.row_base;
     p.timeout_ns = g.timeout_ns;
     p.err = g.err;
-    if (g.n_peers > 0) return cudaErrorInvalidValue;  // only the TF32 CTA-pair kernel writes peer rows
     for (int i = 0; i < g.n_steps; ++i) p.steps[i] = g.steps[i];
+    if (PUSH != (g.n_peers > 0)) return cudaErrorInvalidValue;
+    if (PUSH) {
+        if (DUAL || g.n_peers > kMaxPeers || !g.peer_out) return cudaErrorInvalidValue;
+        bool vec = (g.ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(g.out) & 15) == 0;
+        for (int i = 0; i < g.n_peers; ++i) {
+            if (!g.peer_out[i]) return cudaErrorInvalidValue;
+            p.peer_out[i] = g.peer_out[i];
+            vec = vec && (reinterpret_cast<uintptr_t>(g.peer_out[i]) & 15) == 0;
+        }
+        p.n_peers = g.n_peers;
+        p.push_vec = vec ? 1 : 0;
+    }
 
     const int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;
     kernel<<<2 * pairs, kPair3Threads, C::kSmemBytes, stream>>>(mA, mB, mAs, mBs, mB2, mB2s, p);
@@ -416,6 +444,7 @@ cudaError_t run_pair3_variant(const GemmLaunch& g, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_pair_3xtf32(const GemmLaunch& g, bool dual, cudaStream_t stream) {
+    if (g.n_peers > 0) return dual ? cudaErrorInvalidValue : run_pair3_variant<3, false, true>(g, stream);
     return dual ? run_pair3_variant<3, true>(g, stream) : run_pair3_variant<3, false>(g, stream);
 }
 

@@ -48,7 +48,7 @@ struct FusedParams {
     unsigned long long timeout_ns;
     int* err;
     EpStepDev steps[MXB_MAX_EPILOGUE];
-    // Row all-gather (TF32 CTA-pair kernel only): the same rows of `out` in
+    // Row all-gather (CTA-pair kernels only): the same rows of `out` in
     // each peer GPU's copy of the full output (same ldo), written by the
     // epilogue warps once their tile is stored locally.
     float* peer_out[kMaxPeers];
@@ -241,15 +241,15 @@ __device__ __forceinline__ void store_row_chunk(const float (&v)[W], int row, in
 // output into every peer's copy.  The calling warp stored these rows just
 // before (lane i row row0 + i), so __syncwarp orders those stores before the
 // loads, which hit L2.  One instruction moves 512 contiguous bytes of a row;
-// four rows are in flight at a time.  The stores are plain global stores to
+// kU rows are in flight at a time.  The stores are plain global stores to
 // peer addresses (NVLink), so this warp's cost is issue only while the link
 // drains, and it runs while the MMA warp is already on the next tile.
+template <int kU = 4>
 __device__ __forceinline__ void push_rows(const FusedParams& p, int row0, int c0, int c1) {
     __syncwarp();
     const int lane = threadIdx.x & 31;
     const int rows = min(32, p.M - row0);
     if (rows <= 0 || c0 >= c1) return;
-    constexpr int kU = 4;
     if (p.push_vec) {
         // c0 is a multiple of 32, so every float4 below is 16-byte aligned.
         const int segs = (c1 - c0 + 127) / 128;  // 128-column segments per row

@@ -42,7 +42,7 @@ struct GemmLaunch {
     int* err;                          // device error word
     unsigned long long timeout_ns;
     int num_sms;
-    float* const* peer_out;            // n_peers > 0: also write the rows here (TF32 CTA-pair kernel only)
+    float* const* peer_out;            // n_peers > 0: also write the rows here (CTA-pair kernels only)
     int n_peers;
     int choice_rows;                   // rows the K split is chosen for (0: M)
     int k_splits;                      // > 1: single-CTA TF32 kernel with K split this many ways
@@ -88,8 +88,9 @@ cudaError_t launch_tiny_gemm(const float* A, long long lda, const float* B, long
 
 // Kernel launchers (fused_gemm.cu, elementwise.cu).  Return cudaError_t.
 cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream);
-// Whether launch_fused_gemm(g) runs the TF32 CTA-pair kernel for one product,
-// the kernel that writes peer rows itself (MINIXLA_GATHER_PUSH=0: never).
+// Whether launch_fused_gemm(g) runs a CTA-pair kernel (TF32 or 3xTF32) for one
+// product, the kernels that write peer rows themselves (MINIXLA_GATHER_PUSH=0:
+// never).
 bool fused_gemm_pushes_rows(const GemmLaunch& g);
 // Kernel family (MXB_KERNEL_*), tile and K split that launch_fused_gemm runs
 // for g when the caller provides workspace for `k_splits` slices (0 or 1:

@@ -8,9 +8,9 @@ unmap-before-free on close.
 GPU (one process per visible GPU, up to eight, NCCL): every rank's full buffer after the
 fused gather must equal, bit for bit, the NCCL all-gather of the same
 shards computed by mxb_fused_gemm, and sampled rows must match the oracle.
-Covers the in-kernel push (256 x 256 and 256 x 512 pair tiles, float4 and
-odd-pitch scalar copies, uneven shards) and the copy form (3xTF32, the
-single-CTA and skinny kernels, MINIXLA_GATHER_PUSH=0)."""
+Covers the in-kernel push (TF32 256 x 256 and 256 x 512 pair tiles, the
+3xTF32 pair kernel, float4 and odd-pitch scalar copies, uneven shards) and
+the copy form (the single-CTA and skinny kernels, MINIXLA_GATHER_PUSH=0)."""
 import ctypes as C
 import os
 import socket
@@ -133,7 +133,8 @@ GPU_CASES = [
     (4096, 0, 4096, 128, 1, "1", True),    # 256 x 512 pair tiles
     (2048, 1, 2047, 200, 1, "1", True),    # uneven shards, odd pitch: scalar copies, K tail
     (2048, 0, 2048, 256, 1, "0", False),   # copy form forced
-    (2048, 0, 2048, 256, 3, "1", False),   # 3xTF32: copy form
+    (2048, 0, 2048, 256, 3, "1", True),    # 3xTF32 CTA-pair kernel pushes too
+    (2048, 1, 2047, 200, 3, "1", True),    # ... with uneven shards and an odd pitch
     (100, 0, 96, 64, 1, "1", False),       # single-CTA kernel
     (8, 0, 512, 256, 1, "1", False),       # skinny kernel
 ]
