@@ -55,7 +55,7 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     p.add_argument("--sweep", action="store_true",
-                   help="time every BASELINE shape (kernel only, operands resident); one JSON line per shape")
+                   help="time every benchmark shape (kernel only, operands resident); one JSON line per shape")
     p.add_argument("--kernels", action="store_true",
                    help="HBM-bound kernels alone (standalone add / relu, skinny GEMM) on operands larger than L2: "
                         "GB/s against the measured copy rate; one JSON line per kernel")
@@ -632,7 +632,7 @@ def ours_arm(args, rank, local_rank, world):
     return 0
 
 
-SWEEP_SHAPES = [  # (M, N, K, C distribution) -- BASELINE configs 1-3 and config 5 on one GPU
+SWEEP_SHAPES = [  # (M, N, K, C distribution) -- the benchmark workloads: 128^3, the square sweep, the ragged shapes, 32768 x 8192 x 8192 on one GPU
     (128, 128, 128, "uniform"),
     (512, 512, 512, "normal"), (1024, 1024, 1024, "normal"), (2048, 2048, 2048, "normal"),
     (4096, 4096, 4096, "normal"), (8192, 8192, 8192, "normal"),
@@ -669,7 +669,7 @@ def cpu_reference_ms(build, rows_total: int, flops_per_row: float):
 
 
 def run_sweep(args):
-    """Kernel-only time of relu(A.B + C) for every BASELINE shape, both
+    """Kernel-only time of relu(A.B + C) for every benchmark shape, both
     precision modes, operands resident (min and median of CUDA-event-timed
     launches after warm-up; each behind a ~50 us spin on the stream so the
     host's launch preparation stays outside the events), plus the 3-layer

@@ -12,7 +12,7 @@ Sources of the cases (gouthamk16/miniXLA):
   tests.c:48-65    relu(AB + bias[N])    expects {0, 0, 19, 4}
   tests.c:191-220  diamond epilogue      expects {5, 4, 11, 10}
   gpu_test.c:83-126, 132-188, 201-249  diamond / two-layer / deep-chain fills
-plus seeded cases at the BASELINE shapes scaled down, ragged tile edges, the
+plus seeded cases at the benchmark shapes scaled down, ragged tile edges, the
 modulo-operand rule of graph.c:100-105, and the 3-layer MLP DAG.
 """
 from __future__ import annotations
@@ -142,7 +142,7 @@ def case_mlp_small(M=64, D=32, H=64):
     b1, b2, b3 = _n((H,), 55, 0.0, 0.1), _n((H,), 56, 0.0, 0.1), _n((D,), 57, 0.0, 0.1)
 
     def build(g, t):
-        # The structure optimize() gives the 3-layer MLP of the BASELINE
+        # The structure optimize() gives the 3-layer MLP of the benchmark
         # configs: F1 = [ADD b1, RELU]; F2 = [ADD b2, RELU, ADD (h W2')] with
         # h W2' left as a bare matmul; F3 = [ADD b3].
         h = g.fused(t["X"], t["W1"], [("add", t["b1"]), ("relu", None)])
@@ -177,7 +177,7 @@ def all_cases():
     ]
 
 
-# Longest chain of GEMMs from an input to the root.  The BASELINE tolerances
+# Longest chain of GEMMs from an input to the root.  The tolerances
 # are per fused op; rounding error compounds through chained layers, so
 # graph-level checks scale the tolerance by this depth.
 DEPTH = {"tests_diamond": 2, "gpu_two_layer": 2, "gpu_deep_chain": 8, "mlp_small": 3}

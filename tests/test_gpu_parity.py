@@ -1,6 +1,6 @@
 """GPU parity tests: the sm_100a path against the oracle, through the C ABI.
 
-Tolerances:
+Tolerances (the accuracy targets of the fused path):
   3xTF32 mode: relative Frobenius error <= 1e-5 against MiniXLA's fp32 execute();
   TF32 mode:   relative Frobenius error <= 2e-3;
   both:        no NaN, and no sign flip after relu beyond what the tolerance
@@ -234,7 +234,7 @@ def test_kernel_timers(lib, gpu_ctx):
     assert lib.gpu_time_kernel_ms(mm, gpu_ctx, 1, 1) == -1.0
 
 
-# ---------------------------------------------------------------- BASELINE configs
+# ---------------------------------------------------------------- benchmark workloads
 
 
 def _relu_abc(M, N, K, c_normal):
