@@ -9,7 +9,7 @@ B (weak scaling: the single-GPU case is the 8192^3 headline shape; at 4 GPUs
 the job is the 32768 x 8192 x 8192 row-sharded shape).  Output rows stay on
 their GPU; no collective runs on the data path (at N > 1 an NCCL all-gather of
 the output rows is timed after the kernel steps and reported apart, as
-`allgather`).  `--workload config5` runs the
+`allgather`).  `--workload strong` runs the
 fixed 32768 x 8192 x 8192 job split over N GPUs instead (strong scaling).
 
 ours:      `value` = whole-job TFLOP/s with inputs resident in HBM, K launches of
@@ -41,7 +41,7 @@ sys.path.insert(0, str(ROOT))
 
 NDIM = 8192       # N = K = 8192
 ROWS_PER_GPU = 8192
-CONFIG5_M = 32768
+STRONG_M = 32768
 
 
 def parse():
@@ -51,7 +51,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--precision", choices=["tf32", "3xtf32"], default="tf32")
-    p.add_argument("--workload", choices=["weak", "config5"], default="weak")
+    # "config5" is the earlier name of "strong", still accepted.
+    p.add_argument("--workload", choices=["weak", "strong", "config5"], default="weak")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
     p.add_argument("--sweep", action="store_true",
@@ -60,7 +61,8 @@ def parse():
                    help="HBM-bound kernels alone (standalone add / relu, skinny GEMM) on operands larger than L2: "
                         "GB/s against the measured copy rate; one JSON line per kernel")
     p.add_argument("--mlp", action="store_true",
-                   help="config 4 end to end: the 3-layer MLP built with the reference's g_* API and optimize(), "
+                   help="the 3-layer MLP (X 4096 x 1024, hidden 4096) end to end, built with the reference's g_* API "
+                        "and optimize(), "
                         "run through gpu_execute_into, weights uploaded or kept resident; one JSON line per run")
     p.add_argument("--shape", type=int, default=0,
                    help="per-GPU M = N = K override (profiling on a smaller case); 0 = 8192")
@@ -69,7 +71,7 @@ def parse():
                    help="time a rank-3 fused node relu(A.B + C) of 'B,M,N,K' through gpu_time_kernel_ms, both modes, "
                         "one launch for the batch and one launch per product (one JSON line each)")
     p.add_argument("--mnk", default="",
-                   help="with --sweep: time only this product, 'M,N,K' (no config-4 MLP; for profiling one kernel)")
+                   help="with --sweep: time only this product, 'M,N,K' (no MLP; for profiling one kernel)")
     return p.parse_args()
 
 
@@ -82,8 +84,8 @@ def shard_rows(world: int, rank: int, workload: str, rows_per_gpu: int = 0):
     """Row range [r0, r1) of this rank and the job's total M."""
     if rows_per_gpu:
         return rank * rows_per_gpu, (rank + 1) * rows_per_gpu, rows_per_gpu * world
-    if workload == "config5":
-        m_total = CONFIG5_M
+    if workload in ("strong", "config5"):
+        m_total = STRONG_M
         base, extra = divmod(m_total, world)
         r0 = rank * base + min(rank, extra)
         return r0, r0 + base + (1 if rank < extra else 0), m_total
@@ -599,11 +601,11 @@ def ours_arm(args, rank, local_rank, world):
             "metric": "fused relu(A.B+C) TFLOP/s (fp32 in/out)",
             "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-            "scaling": "strong" if args.workload == "config5" else "weak",
+            "scaling": "strong" if args.workload in ("strong", "config5") else "weak",
             "vs_baseline": None, "dtype": args.precision,
             "data": "synthetic (seeded splitmix64: A,B ~ U[-1,1], C ~ N(0,1))",
             "config": {
-                "workload": ("relu(A.B+C) 32768x8192x8192 split over N GPUs" if args.workload == "config5"
+                "workload": ("relu(A.B+C) 32768x8192x8192 split over N GPUs" if args.workload in ("strong", "config5")
                              else "relu(A.B+C) 8192x8192x8192 per GPU (8192-row shard each)"),
                 "M_total": m_total, "N": N, "K": K, "rows_per_gpu": M, "precision": args.precision,
                 "parallelism": f"row-shard x{world}",
@@ -673,7 +675,8 @@ def run_sweep(args):
     precision modes, operands resident (min and median of CUDA-event-timed
     launches after warm-up; each behind a ~50 us spin on the stream so the
     host's launch preparation stays outside the events), plus the 3-layer
-    MLP DAG of config 4 through the device API (one launch per fused node)."""
+    3-layer MLP DAG (X 4096 x 1024, hidden 4096) through the device API (one
+    launch per fused node)."""
     import numpy as np
     import torch
 
@@ -760,7 +763,7 @@ def run_sweep(args):
     if args.mnk:
         lib.gpu_ctx_destroy(ctx)
         return 0
-    # config 4: 3-layer MLP, one launch per fused node (+ the bare matmul)
+    # the 3-layer MLP, one launch per fused node (+ the bare matmul)
     Mx, D, H = 4096, 1024, 4096
     X = torch.from_numpy(datagen.uniform((Mx, D), 70)).to(dev)
     W1 = torch.from_numpy(datagen.normal((D, H), 71, 0.0, 1.0 / np.sqrt(D))).to(dev)
@@ -929,7 +932,7 @@ def run_kernels(args):
 
 
 def run_mlp(args):
-    """Config 4 through the reference-facing path: the 3-layer MLP (X 4096 x
+    """The 3-layer MLP through the reference-facing path (X 4096 x
     1024; W1 1024 x 4096, W2 and W2' 4096 x 4096, W3 4096 x 1024; bias rows)
     built with MiniXLA's own g_matmul / g_add / g_relu and optimize()
     (oracle/_ref), then handed to gpu_execute_into.  Each step is one
@@ -948,7 +951,7 @@ def run_mlp(args):
     from oracle.bindings import RefGraph, fused_oracle, ref_available
 
     if not ref_available():
-        print(json.dumps({"workload": "config 4 MLP", "unavailable": "oracle/_ref not built"}))
+        print(json.dumps({"workload": "3-layer MLP 4096x1024 -> 4096 -> 4096 -> 1024", "unavailable": "oracle/_ref not built"}))
         return 0
     lib = mlib.load()
     ctx = lib.gpu_ctx_create_on(0)
@@ -1001,11 +1004,11 @@ def run_mlp(args):
                 got = out_h.numpy()[rows]
                 rel = float(np.linalg.norm(got - want) / np.linalg.norm(want))
                 tol = 3 * (2e-3 if prec == mlib.GPU_PRECISION_TF32 else 1e-5)
-                assert rel <= tol, f"config 4 check failed: {rel:.3g} > {tol}"
+                assert rel <= tol, f"MLP check failed: {rel:.3g} > {tol}"
                 ms = min(ts) * 1e3
                 h2d = 4 * Mx * D + (0 if resident else 4 * sum(host[k].size for k in weights))
                 print(json.dumps({
-                    "workload": "config 4 MLP via optimize() + gpu_execute_into", "precision": prec_name,
+                    "workload": "3-layer MLP 4096x1024 -> 4096 -> 4096 -> 1024 via optimize() + gpu_execute_into", "precision": prec_name,
                     "nodes_after_optimize": n_nodes, "weights": "resident" if resident else "uploaded each call",
                     "executor": "row-streamed (8 chunks)" if chunks == "8" else "one-stream (multi-stream DAG)",
                     "ms_min": ms, "ms_median": statistics.median(ts) * 1e3, "tflops": flops / (ms * 1e-3) / 1e12,

@@ -23,7 +23,7 @@ namespace {
 //
 // DUAL: the node's epilogue holds one step that adds a second product
 // A @ B2 with the same A (a bare matmul on the same left operand whose only
-// consumer is this node: config 4's relu(h W2 + b2) + h W2').  Each k-block
+// consumer is this node, as in the 3-layer MLP's relu(h W2 + b2) + h W2').  Each k-block
 // stages A once with the B and B2 halves; the MMA warp issues A.B into
 // accumulator 0 and A.B2 into accumulator 1 next to it in TMEM; the epilogue
 // reads both and adds the second where the step stands.  The second product

@@ -188,7 +188,7 @@ bool dual_kernel_enabled() {
 //
 // optimize() never fuses a bare matmul (optimizer.c:94-132), so a matmul that
 // feeds a fused node's ADD step stays a node of its own and eval_fused adds
-// its stored result (graph.c:98-105) -- config 4's F2 = relu(h W2 + b2) +
+// its stored result (graph.c:98-105) -- the 3-layer MLP's F2 = relu(h W2 + b2) +
 // h W2'.  When that fused node is the matmul's only reader and both products
 // share the left operand, they run in one kernel (the pair kernels' DUAL
 // forms, TF32 and 3xTF32): A is staged once for both and the matmul's value

@@ -316,7 +316,7 @@ def _mlp_inputs(M=4096, D=1024, H=4096):
 
 
 @pytest.mark.parametrize("precision", [X3, TF32], ids=["3xtf32", "tf32"])
-def test_config4_mlp_dag(lib, gpu_ctx, precision, host_threads):
+def test_three_layer_mlp_dag(lib, gpu_ctx, precision, host_threads):
     """3-layer MLP with a shared node (h feeds W2 and W2'), at full size.
     Rows are independent through every layer, so the oracle evaluates a row sample of X."""
     inp = _mlp_inputs()
