@@ -1,4 +1,7 @@
 // Skinny fused GEMM for few output rows (M <= 16): out = epi(A[M,K] @ B[K,N]).
+// use_skinny_gemm routes up to 8 rows here in TF32 mode and up to 16 in
+// 3xTF32 mode; 9 to 16 TF32 rows run faster on the tensor-core kernel with
+// its K split.
 //
 // With one to a few rows the work is reading B (4*K*N bytes); a 128-row
 // tensor-core tile would idle most of the MMA and cover too few SMs.  This
