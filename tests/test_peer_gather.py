@@ -123,6 +123,56 @@ def test_gather_buffers_host_logic_gloo():
         assert calls[4] == ("free", rank, own_addr)
 
 
+def _cpu_checks_worker(port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=0, world_size=1, timeout=timedelta(seconds=60))
+        import sys
+        sys.path.insert(0, os.getcwd())
+        from minixla_b200.peer_gather import GatherBuffers
+
+        errors = []
+        try:
+            GatherBuffers(_FakeLib(0), device=0, rows_total=10, cols=8, ldo=4)
+        except ValueError as e:
+            errors.append(("ldo", str(e)))
+        lib = _FakeLib(0)
+        gb = GatherBuffers(lib, device=0, rows_total=100, cols=8)
+        for row0, M, N in ((-1, 10, 8), (95, 10, 8), (0, 10, 9)):
+            try:
+                gb.gemm(None, 1, 4, 2, 8, row0, M, N, 4, None, 0, 1, 0)
+            except ValueError as e:
+                errors.append(("rows", str(e)))
+        ptrs, n = gb.peer_rows(7)
+        launched = [c for c in lib.calls if c[0] == "gemm"]
+        gb.close()
+        gb.close()  # a second close is a no-op
+        q.put((errors, n, len(launched), [c[0] for c in lib.calls]))
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent
+        q.put(repr(e))
+
+
+def test_gather_buffers_argument_checks():
+    """One rank (gloo): a pitch narrower than the rows, rows outside the
+    buffer and a column count other than the buffer's are refused before any
+    launch; with no peers the launch gets an empty peer list; close is
+    idempotent and frees the buffer once."""
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_cpu_checks_worker, args=(port, q))
+    p.start()
+    res = q.get(timeout=120)
+    p.join(timeout=60)
+    assert p.exitcode == 0
+    assert isinstance(res, tuple), res
+    errors, n_peers, launched, calls = res
+    assert [k for k, _ in errors] == ["ldo", "rows", "rows", "rows"]
+    assert n_peers == 0 and launched == 0
+    assert calls == ["alloc", "free"]
+
+
 # ---------------------------------------------------------------- GPU: one process per GPU
 
 # (rows per rank, extra rows, N, K, precision, MINIXLA_GATHER_PUSH, expect the
