@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(256) ksplit_reduce_kernel(const __grid_constan
 // The reduce kernel of a K split is launched as a programmatic dependent of
 // the GEMM (it starts early and waits on griddepcontrol.wait);
 // MINIXLA_KSPLIT_PDL=0 launches it in plain stream order.
-// MINIXLA_BATCH_PAIR=0 keeps batched TF32 launches on the single-CTA kernel.
+// MINIXLA_BATCH_PAIR=0 keeps batched launches on the single-CTA kernel.
 bool batch_pair_tiles() {
     const char* v = getenv("MINIXLA_BATCH_PAIR");
     return !(v && v[0] == '0');
@@ -697,11 +697,12 @@ GemmPlan plan_fused_gemm(const GemmLaunch& g, int k_splits) {
     }
     pl.kernel = MXB_KERNEL_SINGLE_CTA;
     pl.tile_rows = kBM;
-    if (g.batch > 1 && g.precision == GPU_PRECISION_TF32 && g.M >= 1024 && g.N >= 1024 && batch_pair_tiles()) {
-        // TF32 products from 1024 x 1024 on 256 x 256 CTA-pair tiles once the
-        // batch gives every CTA pair a tile (32 x 1024^3: 162 -> 152 us; at
-        // 512^3 and on ragged 300-row products the single-CTA tiles were
-        // faster, 84 vs 88 and 21 vs 26 us).
+    if (g.batch > 1 && g.M >= 1024 && g.N >= 1024 && g.K >= 1024 && batch_pair_tiles()) {
+        // Products from 1024^3 on 256 x 256 CTA-pair tiles once the batch
+        // gives every CTA pair a tile (32 x 1024^3: TF32 162 -> 152 us, 3xTF32
+        // 441 -> 411 us).  The single-CTA tiles stayed faster at 512^3 (84 vs
+        // 88 us), on ragged 300-row products (21 vs 26 us) and with a short K
+        // (8 x (1100, 1030, 300), 3xTF32: 108 vs 118 us).
         const long long pair_tiles = g.batch * ((g.M + 255) / 256) * ((g.N + 255) / 256);
         if (pair_tiles >= g.num_sms / 2) {
             pl.kernel = MXB_KERNEL_CTA_PAIR;
@@ -736,7 +737,7 @@ cudaError_t launch_fused_gemm(const GemmLaunch& g, cudaStream_t stream) {
     const bool x3 = g.precision == GPU_PRECISION_3XTF32;
     const GemmPlan pl = plan_fused_gemm(g, g.k_splits);
     if (pl.kernel == MXB_KERNEL_CTA_PAIR) {
-        if (g.batch > 1) return x3 ? cudaErrorInvalidValue : launch_pair_tf32(g, false, stream);
+        if (g.batch > 1) return x3 ? launch_pair_3xtf32(g, false, stream) : launch_pair_tf32(g, false, stream);
         if (pl.products == 2) return x3 ? launch_pair_3xtf32(g, true, stream) : launch_pair_tf32_dual(g, stream);
         return x3 ? launch_pair_3xtf32(g, false, stream) : launch_pair_tf32(g, pl.tile_cols == 512, stream);
     }

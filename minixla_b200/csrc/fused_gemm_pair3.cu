@@ -57,7 +57,9 @@ __device__ __noinline__ void push_rows_apart(const FusedParams& p, int row0, int
 // PUSH: after a tile's last segment each epilogue warp also copies its 32
 // rows x 128 columns into the peers' copies (FusedParams::peer_out), with the
 // accumulator already released; a separate instance keeps the others' code.
-template <int STAGES, bool DUAL, bool PUSH = false>
+// BATCHED: p.batch products of one shape, A, B and their low parts as 3-D
+// tensor maps (third coordinate: the product).
+template <int STAGES, bool DUAL, bool PUSH = false, bool BATCHED = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
     fused_gemm_pair3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                             const __grid_constant__ CUtensorMap tmAs, const __grid_constant__ CUtensorMap tmBs,
@@ -66,6 +68,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
     using C = Pair3Cfg<STAGES, DUAL>;
     constexpr int BN = C::kBN;
     static_assert(!(PUSH && DUAL), "peer rows are written for one product");
+    static_assert(!(BATCHED && (DUAL || PUSH)), "a batched launch has one product and no peer rows");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -126,7 +129,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
             bool ok = true;
             for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
                 int mb, nb;
-                tile_coords(t, p, mb, nb);
+                int b = 0;
+                if (BATCHED) {
+                    b = t / p.tiles_per_batch;
+                    tile_coords(t - b * p.tiles_per_batch, p, mb, nb);
+                } else {
+                    tile_coords(t, p, mb, nb);
+                }
                 const int m0 = mb * 256 + static_cast<int>(rank) * 128;
                 const int n0 = nb * BN + static_cast<int>(rank) * (BN / 2);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
@@ -141,17 +150,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
                     if (rank == 0) mbar_arrive_expect_tx(full_bar(stage), 2 * C::kStageBytes);
                     const uint32_t fb = mapa_shared(full_bar(stage), 0);
                     const int k0 = kb * kBK;
-                    tma_load_2d_pair(smem_addr(st), &tmA, fb, k0, m0);
-                    tma_load_2d_pair(smem_addr(st2), &tmAs, fb, k0, m0);
+                    if (BATCHED) {
+                        tma_load_3d_pair(smem_addr(st), &tmA, fb, k0, m0, b);
+                        tma_load_3d_pair(smem_addr(st2), &tmAs, fb, k0, m0, b);
 #pragma unroll
-                    for (int j = 0; j < BN / 64; ++j) {
-                        tma_load_2d_pair(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb, n0 + 32 * j, k0);
-                        tma_load_2d_pair(smem_addr(st2 + C::kABytes + j * kBoxBytes), &tmBs, fb, n0 + 32 * j, k0);
-                        if (DUAL) {
-                            tma_load_2d_pair(smem_addr(st + C::kABytes + C::kBBytes + j * kBoxBytes), &tmB2, fb,
-                                             n0 + 32 * j, k0);
-                            tma_load_2d_pair(smem_addr(st2 + C::kABytes + C::kBBytes + j * kBoxBytes), &tmB2s, fb,
-                                             n0 + 32 * j, k0);
+                        for (int j = 0; j < BN / 64; ++j) {
+                            tma_load_3d_pair(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb, n0 + 32 * j, k0, b);
+                            tma_load_3d_pair(smem_addr(st2 + C::kABytes + j * kBoxBytes), &tmBs, fb, n0 + 32 * j, k0,
+                                             b);
+                        }
+                    } else {
+                        tma_load_2d_pair(smem_addr(st), &tmA, fb, k0, m0);
+                        tma_load_2d_pair(smem_addr(st2), &tmAs, fb, k0, m0);
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j) {
+                            tma_load_2d_pair(smem_addr(st + C::kABytes + j * kBoxBytes), &tmB, fb, n0 + 32 * j, k0);
+                            tma_load_2d_pair(smem_addr(st2 + C::kABytes + j * kBoxBytes), &tmBs, fb, n0 + 32 * j,
+                                             k0);
+                            if (DUAL) {
+                                tma_load_2d_pair(smem_addr(st + C::kABytes + C::kBBytes + j * kBoxBytes), &tmB2, fb,
+                                                 n0 + 32 * j, k0);
+                                tma_load_2d_pair(smem_addr(st2 + C::kABytes + C::kBBytes + j * kBoxBytes), &tmB2s,
+                                                 fb, n0 + 32 * j, k0);
+                            }
                         }
                     }
                     ++issued;
@@ -248,7 +269,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
         bool failed = false;
         for (int t = pair; t < p.num_tiles && !failed; t += num_pairs) {
             int mb, nb;
-            tile_coords(t, p, mb, nb);
+            int b = 0;
+            if (BATCHED) {
+                b = t / p.tiles_per_batch;
+                tile_coords(t - b * p.tiles_per_batch, p, mb, nb);
+            } else {
+                tile_coords(t, p, mb, nb);
+            }
+            const long long out_off = BATCHED ? b * p.out_bstride : 0;
             const int row = mb * 256 + row_in_tile;
             const bool row_ok = row < p.M;
             const int col0 = nb * BN + half * (DUAL ? 64 : 128);  // first output column of this thread
@@ -312,8 +340,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
                             float v[32];
 #pragma unroll
                             for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-                            apply_epilogue(v, row, col, row_ok, p);
-                            if (row_ok) store_row_chunk(v, row, col, p);
+                            apply_epilogue(v, row, col, row_ok, p, nullptr, b);
+                            if (row_ok) store_row_chunk(v, row, col, p, out_off);
                         }
                     }
                 }
@@ -344,10 +372,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPair3Threads, 1)
 
 // ------------------------------------------------------------------ host side
 
-template <int STAGES, bool DUAL, bool PUSH = false>
+template <int STAGES, bool DUAL, bool PUSH = false, bool BATCHED = false>
 cudaError_t run_pair3_variant(const GemmLaunch& g, cudaStream_t stream) {
     using C = Pair3Cfg<STAGES, DUAL>;
-    auto kernel = fused_gemm_pair3_kernel<STAGES, DUAL, PUSH>;
+    auto kernel = fused_gemm_pair3_kernel<STAGES, DUAL, PUSH, BATCHED>;
+    if (BATCHED != (g.batch > 1)) return cudaErrorInvalidValue;
     static std::mutex mu;
     static uint64_t configured = 0;
     static int max_clusters[64] = {0};
@@ -390,10 +419,18 @@ cudaError_t run_pair3_variant(const GemmLaunch& g, cudaStream_t stream) {
     constexpr CUtensorMapSwizzle kSwA = CU_TENSOR_MAP_SWIZZLE_128B;
     constexpr CUtensorMapSwizzle kSwB = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
     CUtensorMap mA, mB, mAs, mBs, mB2, mB2s;
-    if (!make_map(&mA, g.A, g.M, g.K, g.lda, kBK, 128, kSwA) || !make_map(&mB, g.B, g.K, g.N, g.ldb, 32, kBK, kSwB) ||
-        !make_map(&mAs, g.A_small, g.M, g.K, g.lda, kBK, 128, kSwA) ||
-        !make_map(&mBs, g.B_small, g.K, g.N, g.ldb, 32, kBK, kSwB))
+    if (BATCHED) {
+        if (!make_map_3d(&mA, g.A, g.batch, g.M, g.K, g.lda, g.a_bstride, kBK, 128, kSwA) ||
+            !make_map_3d(&mB, g.B, g.batch, g.K, g.N, g.ldb, g.b_bstride, 32, kBK, kSwB) ||
+            !make_map_3d(&mAs, g.A_small, g.batch, g.M, g.K, g.lda, g.a_bstride, kBK, 128, kSwA) ||
+            !make_map_3d(&mBs, g.B_small, g.batch, g.K, g.N, g.ldb, g.b_bstride, 32, kBK, kSwB))
+            return cudaErrorInvalidValue;
+    } else if (!make_map(&mA, g.A, g.M, g.K, g.lda, kBK, 128, kSwA) ||
+               !make_map(&mB, g.B, g.K, g.N, g.ldb, 32, kBK, kSwB) ||
+               !make_map(&mAs, g.A_small, g.M, g.K, g.lda, kBK, 128, kSwA) ||
+               !make_map(&mBs, g.B_small, g.K, g.N, g.ldb, 32, kBK, kSwB)) {
         return cudaErrorInvalidValue;
+    }
     if (DUAL) {
         // The second product shares A (same rows, K and pitch); B2 and its low part have maps of their own.
         if (g.A2 != g.A || g.K2 != g.K || g.lda2 != g.lda || !g.B2 || !g.B2_small ||
@@ -435,6 +472,17 @@ cudaError_t run_pair3_variant(const GemmLaunch& g, cudaStream_t stream) {
         p.push_vec = vec ? 1 : 0;
     }
 
+    p.batch = 1;
+    if (BATCHED) {
+        const long long tiles = static_cast<long long>(p.num_tiles) * g.batch;
+        if (tiles >= (1ll << 31) || !g.ep_bstride) return cudaErrorInvalidValue;
+        p.batch = static_cast<int>(g.batch);
+        p.tiles_per_batch = p.num_tiles;
+        p.num_tiles = static_cast<int>(tiles);
+        p.out_bstride = g.out_bstride;
+        for (int i = 0; i < g.n_steps; ++i) p.ep_bstride[i] = g.ep_bstride[i];
+    }
+
     const int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;
     kernel<<<2 * pairs, kPair3Threads, C::kSmemBytes, stream>>>(mA, mB, mAs, mBs, mB2, mB2s, p);
     note_launch();
@@ -444,6 +492,10 @@ cudaError_t run_pair3_variant(const GemmLaunch& g, cudaStream_t stream) {
 }  // namespace
 
 cudaError_t launch_pair_3xtf32(const GemmLaunch& g, bool dual, cudaStream_t stream) {
+    if (g.batch > 1) {
+        if (dual || g.n_peers > 0) return cudaErrorInvalidValue;
+        return run_pair3_variant<3, false, false, true>(g, stream);
+    }
     if (g.n_peers > 0) return dual ? cudaErrorInvalidValue : run_pair3_variant<3, false, true>(g, stream);
     return dual ? run_pair3_variant<3, true>(g, stream) : run_pair3_variant<3, false>(g, stream);
 }

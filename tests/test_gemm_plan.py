@@ -91,7 +91,9 @@ BATCH_CASES = [
     ((16, 250, 130, 300, TF32), (SINGLE, 128, 128, 16)),
     ((5, 384, 520, 1000, TF32), (SINGLE, 128, 256, 5)),      # N >= 512: 128 x 256 tiles
     ((32, 1024, 1024, 1024, TF32), (PAIR, 256, 256, 32)),    # from 1024 x 1024: CTA pairs
-    ((32, 1024, 1024, 1024, X3), (SINGLE, 128, 128, 32)),
+    ((32, 1024, 1024, 1024, X3), (PAIR, 256, 256, 32)),
+    ((3, 1100, 1030, 1056, X3), (PAIR, 256, 256, 3)),        # ragged, 75 pair tiles
+    ((8, 1100, 1030, 300, X3), (SINGLE, 128, 128, 8)),       # short K: single-CTA tiles
     ((8, 2048, 2048, 2048, TF32), (PAIR, 256, 256, 1)),      # fills the GPU: one launch per product
     ((4, 8, 4096, 4096, TF32), (SKINNY, 8, 128, 1)),         # few rows: skinny kernel per product
     ((4, 64, 64, 64, X3), (TINY, 32, 32, 1)),                # tiny in total (3xTF32)

@@ -468,15 +468,15 @@ def test_skinny_rows_path(lib, gpu_ctx, M, form, NK, precision, monkeypatch, hos
 
 @pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
 @pytest.mark.parametrize("bmnk", [(16, 250, 130, 300), (5, 384, 520, 1000), (64, 128, 128, 128),
-                                  (4, 1100, 1030, 300)])
+                                  (3, 1100, 1030, 1056)])
 def test_batched_one_launch(lib, gpu_ctx, bmnk, precision, monkeypatch):
     """A rank-3 fused node whose products are small runs all of them in one
     launch (3-D tensor maps: a partial row tile or k-block of one product
     reads zeros, not the next product): ADD operands holding every product,
     one shared M x N block, a [N] row and an odd size read by the modulo rule
     over the flat batched index (graph.c:100-105), ragged M, N and K, on
-    128- and (N >= 512, TF32) 256-wide tiles and, for 4 x (1100, 1030, 300)
-    in TF32 mode, 256 x 256 CTA-pair tiles.  The
+    128- and (N >= 512, TF32) 256-wide tiles and, for 3 x (1100, 1030, 1056),
+    the 256 x 256 tiles of the CTA-pair kernels of both modes.  The
     result matches the oracle and the one-launch-per-product loop
     (MINIXLA_BATCH_LAUNCH=0), and in TF32 mode the whole batch is one kernel
     launch."""
