@@ -256,8 +256,11 @@ MXB_API int mxb_fused_gemm2(GpuCtx* ctx,
  * layout rules and epilogue steps as mxb_fused_gemm; runs on the current
  * device and on `stream` (NULL = the legacy default stream), and returns once
  * the work on that stream is finished.  The first call on a device looks up
- * the array's device address; make it before any stream capture.  Calls share
- * the array, so calls that overlap on the GPU race and must be serialised. */
+ * the array's device address; make it before any stream capture.  As every
+ * call synchronises its stream, a call on a stream that is being captured is
+ * refused with MXB_E_ARG.  Device-side waits are bounded by
+ * $MINIXLA_WAIT_TIMEOUT_MS (else 5 s).  Calls share the array, so calls that
+ * overlap on the GPU race and must be serialised. */
 MXB_API int mxb_fused_gemm_noalloc(const float* A, long long lda,
                                    const float* B, long long ldb,
                                    float* out, long long ldo,

@@ -13,11 +13,17 @@
 //
 // Set-up: the first call on each device looks up the device addresses of the
 // array and of an error word (cudaGetSymbolAddress, with that device current)
-// and caches them; make that first call before any stream capture.  Calls
-// share the array: calls that overlap on the GPU (other host threads, other
-// streams) race on it and must be serialised by the caller.
+// and caches them; make that first call before any stream capture.  Every
+// call reads the error word back and synchronises its stream before it
+// returns, so a call on a stream that is being captured is refused
+// (MXB_E_ARG) before anything is enqueued.  Calls share the array: calls that
+// overlap on the GPU (other host threads, other streams) race on it and must
+// be serialised by the caller.  Device-side waits are bounded by
+// $MINIXLA_WAIT_TIMEOUT_MS (read once per process, as gpu_ctx_create reads
+// it), else 5 s.
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -43,6 +49,19 @@ struct DeviceSlots {
 constexpr int kMaxDevices = 64;
 std::mutex g_slots_mu;
 DeviceSlots g_slots[kMaxDevices];
+
+// The bound on every device-side wait: $MINIXLA_WAIT_TIMEOUT_MS, else 5 s.
+unsigned long long wait_timeout_ns() {
+    static const unsigned long long ns = [] {
+        unsigned long long v = 5ull * 1000 * 1000 * 1000;
+        if (const char* t = getenv("MINIXLA_WAIT_TIMEOUT_MS")) {
+            const long long ms = atoll(t);
+            if (ms > 0) v = static_cast<unsigned long long>(ms) * 1000000ull;
+        }
+        return v;
+    }();
+    return ns;
+}
 
 // Once per device, with that device current.
 int device_slots(int dev, DeviceSlots& out) {
@@ -114,11 +133,17 @@ extern "C" int mxb_fused_gemm_noalloc(const float* A, long long lda, const float
         set_error("mxb_fused_gemm_noalloc: no current CUDA device");
         return MXB_E_CUDA;
     }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &capturing) != cudaSuccess || capturing != cudaStreamCaptureStatusNone) {
+        set_error("mxb_fused_gemm_noalloc: the stream is being captured (or cannot be queried); this call reads "
+                  "its error word back and synchronises the stream, which a capture does not allow");
+        return MXB_E_ARG;
+    }
     DeviceSlots slots;
     int rc = device_slots(dev, slots);
     if (rc != MXB_OK) return rc;
 
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     float* a_small = slots.scratch;
     float* b_small = slots.scratch + static_cast<long long>(M) * lda;  // lda % 4 == 0 keeps 16-byte alignment
     cudaError_t e = cudaMemsetAsync(slots.err, 0, sizeof(int), st);
@@ -141,7 +166,7 @@ extern "C" int mxb_fused_gemm_noalloc(const float* A, long long lda, const float
         g.n_steps = n_steps;
         g.precision = GPU_PRECISION_3XTF32;
         g.err = slots.err;
-        g.timeout_ns = 5ull * 1000 * 1000 * 1000;
+        g.timeout_ns = wait_timeout_ns();
         g.num_sms = slots.num_sms;
         e = launch_fused_gemm(g, st);
     }

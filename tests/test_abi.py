@@ -9,10 +9,12 @@ import pytest
 
 from minixla_b200 import abi
 from minixla_b200 import lib as mlib
+from oracle.refdir import ref_dir
 
 ROOT = Path(__file__).resolve().parents[1]
 HEADER = ROOT / "include" / "minixla_b200.h"
-REF = Path("/root/reference")
+REF = ref_dir() or ROOT / "baseline" / "_ref"
+DROPIN_APP = ROOT / "oracle" / "_ref" / "dropin_app"
 
 
 def declared_symbols():
@@ -101,39 +103,16 @@ def test_header_compiles_after_reference_headers(tmp_path):
                    check=True)
 
 
-_DROPIN_APP = r"""
-#include <stdio.h>
-#include "gpu_exec.h"
-#include "optimizer.h"
-int main(void) {
-    Tensor* a = create_tensor((float[]){1, 2, 3, 4, 5, 6}, (int[]){2, 3}, 2);
-    Tensor* b = create_tensor((float[]){1, 2, 3, 4, 5, 6}, (int[]){3, 2}, 2);
-    Tensor* c = create_tensor((float[]){-100, 0, 0, -100}, (int[]){2, 2}, 2);
-    Node* root = optimize(g_relu(g_add(g_matmul(input_node(a), input_node(b)), input_node(c))));
-    GpuCtx* ctx = gpu_ctx_create();
-    if (!ctx) { printf("no GPU context\n"); return 2; }
-    Tensor* out = gpu_execute(root, ctx);
-    int ok = out && out->data[0] == 0 && out->data[1] == 28 && out->data[2] == 49 && out->data[3] == 0;
-    printf("%s\n", ok ? "OK" : "MISMATCH");
-    free_tensor(out); gpu_ctx_destroy(ctx); free_graph(root);
-    free_tensor(a); free_tensor(b); free_tensor(c);
-    return ok ? 0 : 1;
-}
-"""
-
-
 @pytest.mark.skipif(not (REF / "graph.c").exists(), reason="reference sources not present")
 def test_reference_c_program_links_as_drop_in(tmp_path):
-    """A MiniXLA C program, unchanged headers and graph code, links against
-    libminixla_b200.so in place of gpu_exec.c / runtime.c / ptx.c (the link
-    line of INTEGRATION.md) and fails gracefully where no GPU exists."""
-    src = tmp_path / "app.c"
-    src.write_text(_DROPIN_APP)
+    """A MiniXLA C program (tests/dropin/dropin_app.c), unchanged headers and
+    graph code, links against libminixla_b200.so in place of gpu_exec.c /
+    runtime.c / ptx.c and, where no GPU exists, fails gracefully."""
     exe = tmp_path / "app"
     lib_dir = mlib.LIB_PATH.parent
-    subprocess.run(["gcc", "-O2", "-I", str(REF), "-o", str(exe), str(src), str(REF / "graph.c"),
-                    str(REF / "tensor.c"), str(REF / "optimizer.c"), "-L", str(lib_dir), "-lminixla_b200",
-                    f"-Wl,-rpath,{lib_dir}", "-lm"], check=True)
+    subprocess.run(["gcc", "-O2", "-I", str(REF), "-o", str(exe), str(ROOT / "tests" / "dropin" / "dropin_app.c"),
+                    str(REF / "graph.c"), str(REF / "tensor.c"), str(REF / "optimizer.c"), "-L", str(lib_dir),
+                    "-lminixla_b200", f"-Wl,-rpath,{lib_dir}", "-lm"], check=True)
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     import torch
 
@@ -141,3 +120,14 @@ def test_reference_c_program_links_as_drop_in(tmp_path):
         assert r.returncode == 0 and "OK" in r.stdout, r.stdout + r.stderr
     else:
         assert r.returncode == 2 and "no GPU context" in r.stdout
+
+
+@pytest.mark.gpu
+def test_reference_c_program_runs_on_gpu():
+    """The same C program, prebuilt against the library by the oracle recipe
+    (`make -C oracle dropin`), run on the GPU: gpu_execute gives tests.c's
+    answer {0, 28, 49, 0}."""
+    if not DROPIN_APP.exists():
+        pytest.skip("oracle/_ref/dropin_app not built (needs the reference sources at build time)")
+    r = subprocess.run([str(DROPIN_APP)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "OK" in r.stdout, r.stdout + r.stderr
