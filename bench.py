@@ -55,6 +55,8 @@ def parse():
     p.add_argument("--workload", choices=["weak", "strong", "config5"], default="weak")
     p.add_argument("--e2e-steps", type=int, default=10)
     p.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg (profiling runs)")
+    p.add_argument("--no-strong", action="store_true",
+                   help="skip the 32768 x 8192 x 8192 strong-scaling and multi-GPU executor legs")
     p.add_argument("--sweep", action="store_true",
                    help="time every benchmark shape (kernel only, operands resident); one JSON line per shape")
     p.add_argument("--kernels", action="store_true",
@@ -360,7 +362,9 @@ def time_fused_allgather(lib, ctx, local_rank, A_d, B_d, steps_arr, r0, M, N, K,
         exact = max_over_ranks(0.0 if torch.equal(gb.tensor(), ref_full) else 1.0) == 0.0
     finally:
         gb.close()
+    world = dist.get_world_size()
     return {"ms_per_step": ms, "rows_written_by_kernel": in_kernel, "bit_equal_to_nccl_gather": exact,
+            "peer_GBs_per_direction": 4.0 * M * N * (world - 1) / (ms * 1e-3) / 1e9,
             "form": "mxb_fused_gemm_allgather: epilogue stores to CUDA-IPC peer buffers over NVLink, "
                     "+ one-element NCCL all-reduce per step"}
 
@@ -374,6 +378,193 @@ def traffic_from_profile(precision: str, m: int):
         return None
 
 
+def check_rows(M: int, r0: int, n_random: int = 48, seed: int = 0):
+    """Rows of a shard [r0, r0 + M) to check against the oracle: the shard's
+    edges, the CTA-pair tile edges (every 256 rows of the job, and the first
+    ones inside the shard), and random rows."""
+    import numpy as np
+
+    rows = {0, 1, M // 2, M - 2, M - 1, 127, 128, 255, 256, 257}
+    first = (r0 + 255) // 256 * 256
+    for g in range(first, r0 + M, 256 * max(1, M // (256 * 8))):
+        rows.update({g - r0 - 1, g - r0})
+    rng = np.random.default_rng(seed + r0)
+    rows.update(rng.integers(0, M, n_random).tolist())
+    return sorted(r for r in rows if 0 <= r < M)
+
+
+def time_steps(launch, stream, warmup: int, steps: int) -> float:
+    """Mean CUDA-event time of `steps` back-to-back launches on `stream`, after `warmup`."""
+    import torch
+
+    for _ in range(warmup):
+        launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        launch()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def strong_leg(args, lib, ctx, dev, stream, rank, local_rank, world, prec, B_h, B_d, max_over_ranks, barrier, tol):
+    """The fixed 32768 x 8192 x 8192 relu(A.B + C) job split by rows over the
+    N GPUs: kernel-only time (max over ranks), the same with the row
+    all-gather -- fused into the epilogue (mxb_fused_gemm_allgather) and as an
+    NCCL all-gather after the kernel -- and the 1-GPU time of the whole job
+    (rank 0 alone, the others waiting), from which speed-up and efficiency
+    follow.  Every rank checks >= 64 rows of its shard against the oracle."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from minixla_b200 import datagen
+    from minixla_b200 import lib as mlib
+    from oracle.bindings import fused_oracle
+
+    N = K = NDIM
+    m_total = STRONG_M
+    r0, r1, _ = shard_rows(world, rank, "strong")
+    M = r1 - r0
+    flops_job = 2.0 * m_total * N * K
+
+    def steps_for(C_dev):
+        st = (mlib.EpStepDev * 2)()
+        st[0] = mlib.EpStepDev(mlib.MXB_EP_ADD_FULL, 0, C_dev.data_ptr(), N, 0.0, 0)
+        st[1] = mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0)
+        return st
+
+    def gemm_launcher(A_dev, C_dev, out_dev, rows):
+        st = steps_for(C_dev)
+
+        def launch():
+            rc = lib.mxb_fused_gemm(ctx, A_dev.data_ptr(), K, B_d.data_ptr(), N, out_dev.data_ptr(), N, rows, N, K,
+                                    st, 2, prec, stream.cuda_stream)
+            if rc != 0:
+                raise RuntimeError(f"mxb_fused_gemm failed: {mlib.last_error()}")
+        return launch, st
+
+    # The whole job on one GPU (rank 0; at N = 1 this is the shard itself).
+    one_gpu_ms = None
+    if world > 1:
+        if rank == 0:
+            A_f = torch.from_numpy(datagen.uniform((m_total, K), 0)).to(dev)
+            C_f = torch.from_numpy(datagen.normal((m_total, N), 2)).to(dev)
+            O_f = torch.empty((m_total, N), device=dev)
+            launch_f, _ = gemm_launcher(A_f, C_f, O_f, m_total)
+            one_gpu_ms = time_steps(launch_f, stream, max(3, args.warmup), args.steps)
+            del A_f, C_f, O_f
+            torch.cuda.empty_cache()
+        barrier()
+        t = torch.tensor([one_gpu_ms or 0.0], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        one_gpu_ms = float(t.item())
+
+    A_h = datagen.uniform((M, K), 0, row_offset=r0)
+    C_h = datagen.normal((M, N), 2, row_offset=r0)
+    A_s, C_s = torch.from_numpy(A_h).to(dev), torch.from_numpy(C_h).to(dev)
+    out_s = torch.empty((M, N), device=dev)
+    launch_s, st_s = gemm_launcher(A_s, C_s, out_s, M)
+    barrier()
+    shard_ms = max_over_ranks(time_steps(launch_s, stream, max(3, args.warmup), args.steps))
+    if world == 1:
+        one_gpu_ms = shard_ms
+
+    rows = check_rows(M, r0)
+    want = fused_oracle(A_h, B_h, [("add", C_h), ("relu",)], rows=rows)
+    got = out_s[rows].cpu().numpy()
+    rel = max_over_ranks(float(np.linalg.norm(got - want) / np.linalg.norm(want)))
+    if not rel <= tol:
+        raise RuntimeError(f"strong-scaling result check failed: relative error {rel:.3g} > {tol}")
+    n_rows = int(max_over_ranks(-len(rows)) * -1)  # fewest rows checked on any rank
+
+    def entry(ms):
+        return {"ms_per_step": ms, "tflops": flops_job / (ms * 1e-3) / 1e12,
+                "speedup_vs_1gpu": one_gpu_ms / ms, "efficiency": one_gpu_ms / ms / world}
+
+    out = {
+        "workload": "relu(A.B+C) 32768x8192x8192 split by rows over N GPUs (mxb_shard_rows)",
+        "rows_per_gpu": M, "one_gpu_ms": one_gpu_ms,
+        "one_gpu_tflops": flops_job / (one_gpu_ms * 1e-3) / 1e12,
+        "kernel": entry(shard_ms),
+        "kernel_efficiency": one_gpu_ms / shard_ms / world,
+        "speedup_vs_1gpu": one_gpu_ms / shard_ms,
+        "streamk_tiles_per_gpu": mlib.gemm_plan(M, N, K, prec, torch.cuda.get_device_properties(dev)
+                                                .multi_processor_count).streamk_tiles,
+        "check": {"rows_per_rank": n_rows, "rel_err_max_over_ranks": rel, "tol": tol,
+                  "rows": "shard edges, 256-row tile edges, 48 random rows per rank; oracle (eval_fused restated)"},
+        "gather_nccl": None, "gather_fused": None,
+    }
+    if world > 1:
+        ag, gathered = time_allgather(out_s, world, m_total, stream, args.warmup, args.steps, max_over_ranks)
+        out["gather_nccl"] = entry(shard_ms + ag["ms_per_step"])
+        out["gather_nccl"].update({"allgather_ms": ag["ms_per_step"], "busbw_GBs": ag["busbw_GBs"],
+                                   "form": "kernel, then torch.distributed all_gather (NCCL)"})
+        fused = time_fused_allgather(lib, ctx, local_rank, A_s, B_d, st_s, r0, M, N, K, m_total, prec, stream,
+                                     args.warmup, args.steps, max_over_ranks, gathered)
+        out["gather_fused"] = entry(fused["ms_per_step"])
+        out["gather_fused"].update({k: fused[k] for k in ("rows_written_by_kernel", "bit_equal_to_nccl_gather",
+                                                          "form", "peer_GBs_per_direction")})
+        del gathered
+    del A_s, C_s, out_s
+    torch.cuda.empty_cache()
+    return out
+
+
+def sharded_executor_leg(lib, world, prec, tol, reps: int = 2):
+    """One process driving all N GPUs through the product's own multi-GPU
+    executor (gpu_ctx_create_multi + gpu_execute): the 32768 x 8192 x 8192
+    relu(A.B + C) node on pageable host buffers, rows split over the GPUs,
+    B replicated by peer copies; host-clock time per call (inputs up, result
+    down, as a MiniXLA caller sees it) and sampled rows against the oracle."""
+    import numpy as np
+
+    from minixla_b200 import datagen
+    from minixla_b200 import lib as mlib
+    from minixla_b200.abi import OP_ADD, OP_RELU, HostGraph, free_host_tensor
+    from oracle.bindings import fused_oracle
+
+    N = K = NDIM
+    M = STRONG_M
+    A = datagen.uniform((M, K), 0)
+    B = datagen.uniform((K, N), 1)
+    Cm = datagen.normal((M, N), 2)
+    ctx = lib.gpu_ctx_create_multi(world)
+    if not ctx:
+        raise RuntimeError(f"gpu_ctx_create_multi({world}) failed: {mlib.last_error()}")
+    try:
+        lib.gpu_ctx_set_precision(ctx, prec)
+        hg = HostGraph()
+        root = hg.fused_node(hg.input_node(A), hg.input_node(B), [(OP_ADD, hg.input_node(Cm)), (OP_RELU, None)])
+        ts = []
+        got = None
+        for i in range(reps + 1):
+            t0 = time.perf_counter()
+            t = lib.gpu_execute(root, ctx)
+            if not t:
+                raise RuntimeError(f"sharded gpu_execute failed: {mlib.last_error()}")
+            if i == reps:
+                got = np.ctypeslib.as_array(t.contents.data, shape=(M * N,)).reshape(M, N).copy()
+            free_host_tensor(t)
+            if i > 0:
+                ts.append(time.perf_counter() - t0)
+        ngpu = lib.gpu_ctx_ngpu(ctx)
+    finally:
+        lib.gpu_ctx_destroy(ctx)
+    rows = sorted(set(check_rows(M, 0, 40)) | {g * (M // world) + d for g in range(1, world) for d in (-1, 0)})
+    want = fused_oracle(A, B, [("add", Cm), ("relu",)], rows=rows)
+    rel = float(np.linalg.norm(got[rows] - want) / np.linalg.norm(want))
+    if not rel <= tol:
+        raise RuntimeError(f"sharded executor check failed: relative error {rel:.3g} > {tol}")
+    ms = 1e3 * min(ts)
+    return {"entry_point": "gpu_ctx_create_multi + gpu_execute (pageable host buffers)", "gpus": ngpu,
+            "workload": "relu(A.B+C) 32768x8192x8192", "ms": ms, "ms_all": [1e3 * x for x in ts],
+            "tflops_end_to_end": 2.0 * M * N * K / (ms * 1e-3) / 1e12, "rel_err": rel, "tol": tol,
+            "rows_checked": len(rows), "h2d_bytes": 4 * (M * K + K * N + M * N), "d2h_bytes": 4 * M * N}
+
+
 def ours_arm(args, rank, local_rank, world):
     import numpy as np
     import torch
@@ -381,7 +572,7 @@ def ours_arm(args, rank, local_rank, world):
 
     from minixla_b200 import datagen
     from minixla_b200 import lib as mlib
-    from minixla_b200.abi import OP_ADD, OP_RELU, HostGraph
+    from minixla_b200.abi import OP_ADD, OP_RELU, HostGraph, free_host_tensor
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -413,6 +604,7 @@ def ours_arm(args, rank, local_rank, world):
     A = datagen.uniform((M, K), 0, row_offset=r0)
     B = datagen.uniform((K, N), 1)
     Cm = datagen.normal((M, N), 2, row_offset=r0)
+    tol = 2e-3 if prec == mlib.GPU_PRECISION_TF32 else 1e-5
 
     ctx = lib.gpu_ctx_create_on(local_rank)
     if not ctx:
@@ -430,9 +622,9 @@ def ours_arm(args, rank, local_rank, world):
     # stream the kernels run on.
     stream = torch.cuda.Stream(dev)
 
-    def launch():
+    def launch(p=prec):
         rc = lib.mxb_fused_gemm(ctx, A_d.data_ptr(), K, B_d.data_ptr(), N, out_d.data_ptr(), N, M, N, K, steps, 2,
-                                prec, stream.cuda_stream)
+                                p, stream.cuda_stream)
         if rc != 0:
             raise RuntimeError(f"mxb_fused_gemm failed: {mlib.last_error()}")
 
@@ -472,6 +664,16 @@ def ours_arm(args, rank, local_rank, world):
     flops_job = 2.0 * m_total * N * K
     value = flops_job * args.steps / (total_ms * 1e-3) / 1e12
 
+    # spot check of this rank's result against the oracle on a few rows
+    from oracle.bindings import fused_oracle
+
+    rows = [0, M // 2, M - 1]
+    want = fused_oracle(A, B, [("add", Cm), ("relu",)], rows=rows)
+    got = out_d[rows].cpu().numpy()
+    rel = float(np.linalg.norm(got - want) / np.linalg.norm(want))
+    if not rel <= tol:
+        raise RuntimeError(f"bench result check failed: relative error {rel:.3g} > {tol}")
+
     # All-gather of the output rows over NVLink (N > 1): timed separately, as
     # the row-sharded job only needs it when a consumer wants the full tensor.
     allgather = None
@@ -485,20 +687,29 @@ def ours_arm(args, rank, local_rank, world):
         allgather["fused"] = fused
         del gathered
 
-    # spot check of this rank's result against the oracle on a few rows
-    from oracle.bindings import fused_oracle
-
-    rows = [0, M // 2, M - 1]
-    want = fused_oracle(A, B, [("add", Cm), ("relu",)], rows=rows)
-    got = out_d[rows].cpu().numpy()
-    rel = float(np.linalg.norm(got - want) / np.linalg.norm(want))
-    tol = 2e-3 if prec == mlib.GPU_PRECISION_TF32 else 1e-5
-    if not rel <= tol:
-        raise RuntimeError(f"bench result check failed: relative error {rel:.3g} > {tol}")
+    # ---- the default precision (3xTF32, fp32-faithful) through the same timed loop
+    x3 = None
+    if prec == mlib.GPU_PRECISION_TF32 and not args.shape:
+        ms3 = max_over_ranks(time_steps(lambda: launch(mlib.GPU_PRECISION_3XTF32), stream, max(3, args.warmup),
+                                        args.steps))
+        rows3 = check_rows(M, r0, 13)
+        want3 = fused_oracle(A, B, [("add", Cm), ("relu",)], rows=rows3)
+        rel3 = max_over_ranks(float(np.linalg.norm(out_d[rows3].cpu().numpy() - want3) / np.linalg.norm(want3)))
+        if not rel3 <= 1e-5:
+            raise RuntimeError(f"3xTF32 result check failed: relative error {rel3:.3g} > 1e-5")
+        pk3, pk3_src = measured_tf32_peak()
+        ach3 = flops_rank / (ms3 * 1e-3) / 1e12
+        x3 = {"value": flops_job / (ms3 * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms3,
+              "steps": args.steps, "rel_err_rows": rel3, "rows_checked": len(rows3), "tol": 1e-5,
+              "roofline": {"bound": "tensor", "achieved": ach3, "peak": pk3 / 3.0, "unit": "TFLOP/s",
+                           "frac": ach3 / (pk3 / 3.0),
+                           "peak_source": pk3_src + " / 3 (three TF32 products per multiply-add)"},
+              "note": "gpu_execute's default mode: x = big + small, three TF32 products, segment sums in fp32"}
 
     # cuBLAS TF32 on the same shape, for context only (not on the product path):
-    # the same number of back-to-back steps, so both run under the same power cap.
-    cublas = None
+    # the same number of back-to-back steps, so both run under the same power
+    # cap, and the best of 10 single launches as the measured TF32 peak.
+    cublas = cublas_best = None
     if rank == 0:
         torch.backends.cuda.matmul.allow_tf32 = True
         with torch.cuda.stream(stream):
@@ -510,16 +721,68 @@ def ours_arm(args, rank, local_rank, world):
             for _ in range(args.steps):
                 torch.matmul(A_d, B_d, out=ref_out)
             c1.record(stream)
-        torch.cuda.synchronize()
-        cublas = flops_rank * args.steps / (c0.elapsed_time(c1) * 1e-3) / 1e12
+            torch.cuda.synchronize()
+            cublas = flops_rank * args.steps / (c0.elapsed_time(c1) * 1e-3) / 1e12
+            singles = []
+            for _ in range(10):
+                c0.record(stream)
+                torch.matmul(A_d, B_d, out=ref_out)
+                c1.record(stream)
+                torch.cuda.synchronize()
+                singles.append(c0.elapsed_time(c1))
+            cublas_best = flops_rank / (min(singles) * 1e-3) / 1e12
         torch.backends.cuda.matmul.allow_tf32 = False
         del ref_out
+
+    # ---- the fixed 32768 x 8192 x 8192 job split over the N GPUs (strong scaling)
+    strong = None
+    if not args.shape and not args.no_strong:
+        strong = strong_leg(args, lib, ctx, dev, stream, rank, local_rank, world, prec, B, B_d, max_over_ranks,
+                            barrier, tol)
     del out_d
     torch.cuda.empty_cache()
 
-    # ---- end to end through the reference-facing C ABI with pinned host buffers
+    # ---- end to end through the reference-facing C ABI
     e2e = None
     if not args.no_e2e:
+        h2d = 4 * (M * K + K * N + M * N)
+        d2h = 4 * M * N
+        # Headline: gpu_execute, exactly as a MiniXLA program calls it -- the
+        # inputs in pageable (malloc'd) host memory as create_tensor leaves
+        # them, a fresh result tensor returned and released with free_tensor's
+        # frees, every step.
+        hp = HostGraph()
+        root_p = hp.fused_node(hp.input_node(A), hp.input_node(B), [(OP_ADD, hp.input_node(Cm)), (OP_RELU, None)])
+
+        def execute_once():
+            t = lib.gpu_execute(root_p, ctx)
+            if not t:
+                raise RuntimeError(f"gpu_execute failed: {mlib.last_error()}")
+            return t
+
+        for _ in range(2):
+            free_host_tensor(execute_once())
+        barrier()
+        ts = []
+        last = None
+        for i in range(args.e2e_steps):
+            t0 = time.perf_counter()
+            t = execute_once()
+            if i == args.e2e_steps - 1:
+                last = np.ctypeslib.as_array(t.contents.data, shape=(M * N,)).reshape(M, N)[rows].copy()
+            free_host_tensor(t)
+            ts.append(time.perf_counter() - t0)
+        g_ms = max_over_ranks(1e3 * statistics.mean(ts))
+        rel_e2e = float(np.linalg.norm(last - want) / np.linalg.norm(want))
+        if not rel_e2e <= tol:
+            raise RuntimeError(f"e2e result check failed: relative error {rel_e2e:.3g} > {tol}")
+        e2e = {"value": flops_job / (g_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": g_ms,
+               "steps": args.e2e_steps, "entry_point": "gpu_execute (pageable malloc'd host buffers; the returned "
+                                                       "tensor freed inside the step)",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+        # The additive gpu_execute_into with pinned host buffers (the copies at
+        # full link speed).
         A_h = torch.from_numpy(A).pin_memory()
         B_h = torch.from_numpy(B).pin_memory()
         C_h = torch.from_numpy(Cm).pin_memory()
@@ -528,67 +791,53 @@ def ours_arm(args, rank, local_rank, world):
         root = hg.fused_node(hg.input_node(A_h), hg.input_node(B_h),
                              [(OP_ADD, hg.input_node(C_h)), (OP_RELU, None)])
         out_t = hg.tensor(O_h)
-        for _ in range(2):
-            if lib.gpu_execute_into(root, ctx, out_t) != 0:
-                raise RuntimeError(mlib.last_error())
-        barrier()
-        e0 = time.perf_counter()
-        for _ in range(args.e2e_steps):
-            if lib.gpu_execute_into(root, ctx, out_t) != 0:
-                raise RuntimeError(mlib.last_error())
-        e_ms = max_over_ranks((time.perf_counter() - e0) * 1e3 / args.e2e_steps)
-        rel_e2e = float(np.linalg.norm(O_h[rows].numpy() - want) / np.linalg.norm(want))
-        if not rel_e2e <= tol:
-            raise RuntimeError(f"e2e result check failed: relative error {rel_e2e:.3g} > {tol}")
-        e2e = {"value": flops_job / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e_ms,
-               "steps": args.e2e_steps, "entry_point": "gpu_execute_into (pinned host buffers)",
-               "h2d_bytes_per_step": 4 * (M * K + K * N + M * N), "d2h_bytes_per_step": 4 * M * N}
+
+        def timed_into(r, o):
+            for _ in range(2):
+                if lib.gpu_execute_into(r, ctx, o) != 0:
+                    raise RuntimeError(mlib.last_error())
+            barrier()
+            e0 = time.perf_counter()
+            for _ in range(args.e2e_steps):
+                if lib.gpu_execute_into(r, ctx, o) != 0:
+                    raise RuntimeError(mlib.last_error())
+            return max_over_ranks((time.perf_counter() - e0) * 1e3 / args.e2e_steps)
+
+        e_ms = timed_into(root, out_t)
+        rel_into = float(np.linalg.norm(O_h[rows].numpy() - want) / np.linalg.norm(want))
+        if not rel_into <= tol:
+            raise RuntimeError(f"e2e (pinned) result check failed: relative error {rel_into:.3g} > {tol}")
+        e2e["pinned_into"] = {"value": flops_job / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e_ms,
+                              "entry_point": "gpu_execute_into (pinned host buffers)",
+                              "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
         # Same, with B kept resident on the GPU (weights that stay between calls):
         # A and C still go up and the result comes down every step.
         b_tensor = root.contents.inputs[1].contents.output
         if lib.gpu_ctx_keep_resident(ctx, b_tensor) != 0:
             raise RuntimeError(mlib.last_error())
-        for _ in range(2):
-            if lib.gpu_execute_into(root, ctx, out_t) != 0:
-                raise RuntimeError(mlib.last_error())
-        barrier()
-        e0 = time.perf_counter()
-        for _ in range(args.e2e_steps):
-            if lib.gpu_execute_into(root, ctx, out_t) != 0:
-                raise RuntimeError(mlib.last_error())
-        r_ms = max_over_ranks((time.perf_counter() - e0) * 1e3 / args.e2e_steps)
+        r_ms = timed_into(root, out_t)
         lib.gpu_ctx_release_resident(ctx, None)
+        e2e["b_resident"] = {"value": flops_job / (r_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": r_ms,
+                             "h2d_bytes_per_step": 4 * (M * K + M * N), "d2h_bytes_per_step": d2h,
+                             "note": "gpu_execute_into, pinned, B kept resident with gpu_ctx_keep_resident"}
 
-        # The same call with pageable host buffers (numpy arrays, as MiniXLA's
-        # malloc'd tensors are): through the context's pinned staging slots,
-        # and with staging off (the driver's own pageable copy path).
-        hp = HostGraph()
+        # gpu_execute_into with pageable buffers: through the context's pinned
+        # staging slots, and with staging off (the driver's own pageable path).
         out_p = np.empty((M, N), dtype=np.float32)
-        root_p = hp.fused_node(hp.input_node(A), hp.input_node(B), [(OP_ADD, hp.input_node(Cm)), (OP_RELU, None)])
         out_pt = hp.tensor(out_p)
         pageable = {}
         for label, staged in (("staged", "1"), ("driver_copy", "0")):
             os.environ["MINIXLA_STAGED_COPY"] = staged
-            for _ in range(2):
-                if lib.gpu_execute_into(root_p, ctx, out_pt) != 0:
-                    raise RuntimeError(mlib.last_error())
-            barrier()
-            e0 = time.perf_counter()
-            for _ in range(args.e2e_steps):
-                if lib.gpu_execute_into(root_p, ctx, out_pt) != 0:
-                    raise RuntimeError(mlib.last_error())
-            p_ms = max_over_ranks((time.perf_counter() - e0) * 1e3 / args.e2e_steps)
+            p_ms = timed_into(root_p, out_pt)
             pageable[label] = {"value": flops_job / (p_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": p_ms}
         os.environ.pop("MINIXLA_STAGED_COPY", None)
         if not np.array_equal(out_p, O_h.numpy()):
             raise RuntimeError("pageable e2e result differs from the pinned one")
-        pageable["note"] = ("pageable host buffers (as create_tensor's malloc'd data): 'staged' copies through the "
-                            "context's pinned slots filled by several host threads; 'driver_copy' is the CUDA "
-                            "driver's own pageable path (MINIXLA_STAGED_COPY=0)")
-        e2e["b_resident"] = {"value": flops_job / (r_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": r_ms,
-                             "h2d_bytes_per_step": 4 * (M * K + M * N), "d2h_bytes_per_step": 4 * M * N,
-                             "note": "B kept resident with gpu_ctx_keep_resident; not the headline e2e"}
-        e2e["pageable"] = pageable
+        pageable["note"] = ("gpu_execute_into on pageable host buffers: 'staged' copies through the context's "
+                            "pinned slots filled by several host threads; 'driver_copy' is the CUDA driver's own "
+                            "pageable path (MINIXLA_STAGED_COPY=0)")
+        e2e["pageable_into"] = pageable
+        e2e["vs_pinned_into"] = g_ms / e_ms
 
     peak, peak_src = measured_tf32_peak()
     if prec == mlib.GPU_PRECISION_3XTF32:
@@ -596,41 +845,54 @@ def ours_arm(args, rank, local_rank, world):
     achieved = flops_rank / (per_launch_ms * 1e-3) / 1e12
     lib.gpu_ctx_destroy(ctx)
 
-    if rank == 0:
-        line = {
-            "metric": "fused relu(A.B+C) TFLOP/s (fp32 in/out)",
-            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-            "scaling": "strong" if args.workload in ("strong", "config5") else "weak",
-            "vs_baseline": None, "dtype": args.precision,
-            "data": "synthetic (seeded splitmix64: A,B ~ U[-1,1], C ~ N(0,1))",
-            "config": {
-                "workload": ("relu(A.B+C) 32768x8192x8192 split over N GPUs" if args.workload in ("strong", "config5")
-                             else "relu(A.B+C) 8192x8192x8192 per GPU (8192-row shard each)"),
-                "M_total": m_total, "N": N, "K": K, "rows_per_gpu": M, "precision": args.precision,
-                "parallelism": f"row-shard x{world}",
-                "l2": "inputs larger than L2 (A+B+C = 768 MiB per GPU step), no flush",
-            },
-            "gpu_launches": int(launches),
-            "e2e": e2e,
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": traffic_from_profile(args.precision, M),
-                         "peak_source": peak_src, "kernel_ms": per_launch_ms,
-                         "frac_of_spec": achieved / (SPEC_TF32_TFLOPS / (3.0 if prec == mlib.GPU_PRECISION_3XTF32
-                                                                         else 1.0)),
-                         "spec_peak": "1125 TFLOP/s dense TF32 (B200 nominal)",
-                         "frac_of_cublas_tf32": (achieved / cublas) if cublas and prec == mlib.GPU_PRECISION_TF32
-                         else None},
-            "allgather": allgather,
-            "cpu_baseline": cpu,
-            "clocks": clocks,
-            "cublas_tf32_matmul_tflops_same_shape_same_steps": cublas,
-            "result_check_rel_err": rel,
-        }
-        print(json.dumps(line), flush=True)
+    # Ranks meet once more, then leave; rank 0 alone drives all N GPUs
+    # through the product's multi-GPU executor.
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    sharded = None
+    if world > 1 and not args.shape and not args.no_strong:
+        torch.cuda.synchronize()
+        sharded = sharded_executor_leg(lib, world, prec, tol)
+
+    spec = SPEC_TF32_TFLOPS / (3.0 if prec == mlib.GPU_PRECISION_3XTF32 else 1.0)
+    line = {
+        "metric": "fused relu(A.B+C) TFLOP/s (fp32 in/out)",
+        "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": "strong" if args.workload in ("strong", "config5") else "weak",
+        "vs_baseline": None, "dtype": args.precision,
+        "data": "synthetic (seeded splitmix64: A,B ~ U[-1,1], C ~ N(0,1))",
+        "config": {
+            "workload": ("relu(A.B+C) 32768x8192x8192 split over N GPUs" if args.workload in ("strong", "config5")
+                         else "relu(A.B+C) 8192x8192x8192 per GPU (8192-row shard each)"),
+            "M_total": m_total, "N": N, "K": K, "rows_per_gpu": M, "precision": args.precision,
+            "parallelism": f"row-shard x{world}",
+            "l2": "inputs larger than L2 (A+B+C = 768 MiB per GPU step), no flush",
+        },
+        "gpu_launches": int(launches),
+        "e2e": e2e,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": traffic_from_profile(args.precision, M),
+                     "peak_source": peak_src, "kernel_ms": per_launch_ms,
+                     "frac_of_spec": achieved / spec, "spec_peak": "1125 TFLOP/s dense TF32 (B200 nominal)",
+                     "peak_cublas_tf32_best_of_10": cublas_best if prec == mlib.GPU_PRECISION_TF32 else None,
+                     "frac_of_cublas_tf32_best_of_10": (achieved / cublas_best)
+                     if cublas_best and prec == mlib.GPU_PRECISION_TF32 else None,
+                     "frac_of_cublas_tf32": (achieved / cublas) if cublas and prec == mlib.GPU_PRECISION_TF32
+                     else None},
+        "precision_3xtf32": x3,
+        "strong": strong,
+        "sharded_executor": sharded,
+        "allgather": allgather,
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "cublas_tf32_matmul_tflops_same_shape_same_steps": cublas,
+        "result_check_rel_err": rel,
+    }
+    print(json.dumps(line), flush=True)
     return 0
 
 

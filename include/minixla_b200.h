@@ -330,7 +330,10 @@ typedef struct {
     int k_splits;              /* CTAs sharing one tile's K range (1: none)                   */
     int products;              /* products per launch: 1, or the batch when a rank-3 node's  */
                                /* products all run in one launch                             */
-    int reserved[3];
+    int streamk_tiles;         /* CTA pair (TF32): tiles whose k-blocks are shared out evenly */
+                               /* over the pairs because they do not fill the last waves     */
+                               /* (0: every tile runs whole on one pair)                     */
+    int reserved[2];
 } mxb_gemm_plan;
 MXB_API int mxb_gemm_plan_for(int M, int N, int K, int precision, int num_sms, mxb_gemm_plan* plan);
 /* The same for a rank-3 node of `batch` products of M x N x K (eval_fused's

@@ -669,6 +669,29 @@ int fused_gemm_k_splits(const GemmLaunch& g) {
     return std::max(1, std::min(s, num_kb));
 }
 
+// Stream-K on the TF32 CTA-pair kernels (single products): the tiles of the
+// last one to two waves are shared out by k-blocks over every pair when the
+// tile count is not a multiple of the pairs (streamk_split), with a split
+// tile's accumulator handed from one pair to the next through global memory.
+// Reported for num_sms / 2 pairs; the launch uses the pairs that fit.
+int fused_gemm_streamk_tiles(const GemmLaunch& g) {
+    if (g.precision != GPU_PRECISION_TF32 || g.A2 || g.batch > 1) return 0;
+    const GemmPlan pl = plan_fused_gemm(g, 1);
+    if (pl.kernel != MXB_KERNEL_CTA_PAIR || pl.products != 1) return 0;
+    const long long tiles = static_cast<long long>((g.M + 255) / 256) * ((g.N + pl.tile_cols - 1) / pl.tile_cols);
+    if (tiles >= (1ll << 31)) return 0;
+    const StreamKSplit sk = streamk_split(static_cast<int>(tiles), (g.K + kBK - 1) / kBK, g.num_sms / 2);
+    return sk.q > 0 ? static_cast<int>(tiles) - sk.dp_tiles : 0;
+}
+
+size_t fused_gemm_streamk_bytes(const GemmLaunch& g) {
+    if (fused_gemm_streamk_tiles(g) == 0) return 0;
+    const int pairs = g.num_sms / 2;
+    const int cols = plan_fused_gemm(g, 1).tile_cols;
+    // Raw accumulators (2 CTAs x 128 rows x tile columns per pair), then the flags.
+    return static_cast<size_t>(pairs) * 2 * 128 * cols * sizeof(float) + static_cast<size_t>(pairs) * 2 * 8 * sizeof(int);
+}
+
 bool fused_gemm_pushes_rows(const GemmLaunch& g) {
     const char* v = getenv("MINIXLA_GATHER_PUSH");
     if (v && v[0] == '0') return false;

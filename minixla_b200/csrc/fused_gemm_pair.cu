@@ -35,7 +35,16 @@ namespace {
 // Barriers: full[s] lives in the leader and counts both CTAs' TMA bytes (the
 // peer's loads signal it through its cluster address); empty[s] and tfull[a]
 // live in both CTAs and receive the leader's multicast commits; tempty[a]
-// lives in the leader and takes one arrival per epilogue warp of either CTA.
+// lives in the leader and takes one arrival per epilogue warp of either CTA;
+// so does tload, which tells the MMA warp that a stream-K tail's accumulator
+// has been loaded back into TMEM.
+//
+// Stream-K (FusedParams::sk_q > 0, single-product instances): when the tiles
+// are not a multiple of the CTA pairs, the last one to two waves' k-blocks are
+// spread evenly over all pairs (pair_work); a tile split between two pairs
+// is handed from the pair running its first k-blocks to the pair running the
+// rest as the raw fp32 accumulator, through global memory, so the MMA chain
+// of every output element is unchanged.
 
 template <int STAGES, int BN, bool DUAL, int EPI = 4>
 struct PairCfg {
@@ -53,7 +62,7 @@ struct PairCfg {
     static constexpr int kBufs = kAccCols <= 256 ? 2 : 1;        // accumulator buffers in TMEM
     static constexpr int kTmemCols = kBufs * kAccCols;
     static constexpr int kBarOffset = STAGES * kStageBytes;
-    static constexpr int kNumBars = 2 * STAGES + 5;
+    static constexpr int kNumBars = 2 * STAGES + 6;
     static constexpr int kSmemBytes = 1024 + kBarOffset + kNumBars * 8 + 16;
     static_assert(BN == 128 || BN == 256 || BN == 512, "pair tile width");
     static_assert(!(DUAL && BN == 512), "two products use 128- or 256-column tiles");
@@ -87,6 +96,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
     auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
     auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
     const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+    const uint32_t tload_bar = bar0 + 8u * (2 * STAGES + 5);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -104,6 +114,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             mbar_init(tempty_bar(a), 2 * EPI);  // every epilogue warp of the two CTAs
         }
         mbar_init(drain_bar, 1);
+        mbar_init(tload_bar, 2 * EPI);  // every epilogue warp of the two CTAs, once per launch
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
@@ -130,7 +141,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             uint32_t phase = 0;
             long long issued = 0;
             bool ok = true;
-            for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+            PairWork wk;
+            for (int idx = 0; ok && pair_work(p, pair, num_pairs, idx, wk); ++idx) {
+                const int t = wk.t;
                 int mb, nb;
                 int b = 0;
                 if (BATCHED) {
@@ -143,7 +156,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                 // CTA r stages, for sub-MMA h, B columns nb*BN + h*kSubN + r*kSubN/2 ..
                 // + kSubN/2, so accumulator column c is output column nb*BN + c.
                 const int n0 = nb * BN + static_cast<int>(rank) * (C::kSubN / 2);
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb = wk.kb0; kb < wk.kb1; ++kb) {
                     if (*abort_flag) { ok = false; break; }
                     if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1u, p.timeout_ns)) {
                         raise_error(p, abort_flag, kErrProducer);
@@ -196,15 +209,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             int acc = 0;
             uint32_t acc_phase = 0;
             bool ok = true;
-            for (int t = pair; t < p.num_tiles && ok; t += num_pairs) {
+            PairWork wk;
+            for (int idx = 0; ok && pair_work(p, pair, num_pairs, idx, wk); ++idx) {
                 if (*abort_flag) break;
                 if (!mbar_wait_cluster(tempty_bar(acc), acc_phase ^ 1u, p.timeout_ns)) {
                     raise_error(p, abort_flag, kErrMma);
                     break;
                 }
+                // A stream-K tail starts from the accumulator its head pair
+                // left, once the epilogue warps have loaded it into TMEM.
+                if (wk.kind == kWorkTail && (*abort_flag || !mbar_wait_cluster(tload_bar, 0, p.timeout_ns))) {
+                    raise_error(p, abort_flag, kErrMma);
+                    break;
+                }
                 tc_fence_after();
                 const uint32_t d_tile = tmem_base + static_cast<uint32_t>(acc * C::kAccCols);
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb = wk.kb0; kb < wk.kb1; ++kb) {
                     if (!mbar_wait_cluster(full_bar(stage), phase, p.timeout_ns)) {
                         raise_error(p, abort_flag, kErrMma);
                         ok = false;
@@ -217,7 +237,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                     for (int kk = 0; kk < kBK / 8; ++kk) {
                         const uint64_t da = smem_desc(a_addr + kk * 32, 16, 1024, kLayoutSW128);
                         const uint64_t db = smem_desc(b_addr + kk * 1024, kBoxBytes, 512, kLayoutSW128Base32B);
-                        const uint32_t accumulate = (kb | kk) != 0 ? 1u : 0u;
+                        const uint32_t accumulate = (wk.kind == kWorkTail || kb != wk.kb0 || kk != 0) ? 1u : 0u;
                         mma_tf32_pair(d_tile, da, db, idesc, accumulate);
 #pragma unroll
                         for (int h = 1; h < C::kSubs; ++h) {
@@ -254,7 +274,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
         const uint32_t tempty_leader1 = mapa_shared(tempty_bar(1), 0);
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int t = pair; t < p.num_tiles; t += num_pairs) {
+        // Stream-K hand-off: this warp's rows of the tile (lane quadrant,
+        // column range) in the head pair's slot and the flag it sets.
+        const int sk_warp = (static_cast<int>(rank) * EPI + (warp - 2));
+        PairWork wk;
+        for (int idx = 0; pair_work(p, pair, num_pairs, idx, wk); ++idx) {
+            const int t = wk.t;
             int mb, nb;
             int b = 0;
             if (BATCHED) {
@@ -269,8 +294,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             const int col0 = nb * BN;
             int chunks = (p.N - col0 + 31) / 32;
             if (chunks > c_first + kChunksPerWarp) chunks = c_first + kChunksPerWarp;
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                   static_cast<uint32_t>(acc * C::kAccCols);
+            const bool head = !BATCHED && !DUAL && wk.kind == kWorkHead;
+            if (!BATCHED && !DUAL && wk.kind == kWorkTail) {
+                // Load the head pair's accumulator into this (free) TMEM buffer,
+                // then let the MMA warp continue the chain.
+                const int src_pair = pair - 1;
+                const bool ready = __all_sync(0xffffffffu, *abort_flag == 0) &&
+                                   wait_flag_gpu(p.sk_flags + src_pair * 2 * EPI + sk_warp, 1, p.timeout_ns);
+                if (!__all_sync(0xffffffffu, ready)) {
+                    if (lane == 0) raise_error(p, abort_flag, kErrEpilogue);
+                    break;
+                }
+                const float* src = p.sk_ws + (static_cast<long long>(src_pair) * 2 + rank) * (BN * 128) +
+                                   (quad * 32 + lane) * 4;
+                for (int c = c_first; c < chunks; ++c) {
+                    uint32_t r[32];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 x = ld_global_cg_v4(src + (8 * c + j) * 512);
+                        r[4 * j + 0] = __float_as_uint(x.x);
+                        r[4 * j + 1] = __float_as_uint(x.y);
+                        r[4 * j + 2] = __float_as_uint(x.z);
+                        r[4 * j + 3] = __float_as_uint(x.w);
+                    }
+                    tmem_st_32x32b_x32(taddr + 32 * c, r);
+                }
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(tload_bar, 0));
+            }
             // C rows into L2: during the k-loop when it is short, else once the accumulator is ready.
-            const bool fetch = row_ok && chunks > c_first;
+            const bool fetch = !head && row_ok && chunks > c_first;
             if (fetch && p.num_kb <= kShortKb)
                 prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p, b);
             const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
@@ -282,13 +339,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             tc_fence_after();
             if (fetch && p.num_kb > kShortKb)
                 prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p, b);
-            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                                   static_cast<uint32_t>(acc * C::kAccCols);
             if (chunks <= c_first) {
                 // No columns of this tile for this warp: release the accumulator at once.
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+            }
+            if (head) {
+                // A stream-K head: the raw accumulator goes to this pair's slot
+                // ([column / 4][row][4], 512 contiguous bytes per instruction),
+                // kept in L2 for the tail pair; no epilogue.
+                float* dst = p.sk_ws + (static_cast<long long>(pair) * 2 + rank) * (BN * 128) + (quad * 32 + lane) * 4;
+                const uint64_t pol = l2_policy_evict_last();
+                for (int c = c_first; c < chunks; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + 32 * c, r);
+                    tmem_ld_wait();
+                    if (c == chunks - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        st_global_v4_hint(dst + (8 * c + j) * 512, __uint_as_float(r[4 * j]),
+                                          __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                                          __uint_as_float(r[4 * j + 3]), pol);
+                }
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) st_release_gpu(p.sk_flags + pair * 2 * EPI + sk_warp, 1);
+                if (C::kBufs == 2) acc ^= 1;
+                if (acc == 0) acc_phase ^= 1u;
+                continue;
             }
             for (int c = c_first; c < chunks; ++c) {
                 uint32_t r[32];
@@ -450,6 +533,21 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
     }
 
     const int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;
+    if (!BATCHED && !DUAL && g.sk_ws && g.sk_flags && pairs <= g.sk_pairs && BN <= g.sk_cols) {
+        // Stream-K over the last one to two waves when the tiles are not a
+        // multiple of the pairs: every pair then gets the same number of
+        // k-blocks (within one), where the last wave would leave some idle.
+        const StreamKSplit sk = streamk_split(p.num_tiles, p.num_kb, pairs);
+        if (sk.q > 0) {
+            p.sk_dp_tiles = sk.dp_tiles;
+            p.sk_q = sk.q;
+            p.sk_extra = sk.extra;
+            p.sk_ws = g.sk_ws;
+            p.sk_flags = g.sk_flags;
+            const cudaError_t e2 = cudaMemsetAsync(g.sk_flags, 0, sizeof(int) * pairs * 2 * EPI, stream);
+            if (e2 != cudaSuccess) return e2;
+        }
+    }
     kernel<<<2 * pairs, C::kThreadsPerCta, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p);
     note_launch();
     return cudaGetLastError();

@@ -70,7 +70,111 @@ struct FusedParams {
     int tiles_per_batch;
     long long out_bstride;
     long long ep_bstride[MXB_MAX_EPILOGUE];
+    // Stream-K tail (TF32 CTA-pair kernels; sk_q == 0: off).  Tiles
+    // [0, sk_dp_tiles) go one per pair in turn, a multiple of the pair count;
+    // the k-blocks of the remaining tiles, taken as one run of
+    // (num_tiles - sk_dp_tiles) * num_kb iterations, are dealt out in
+    // contiguous ranges of sk_q (sk_q + 1 for the first sk_extra pairs).
+    // sk_q >= num_kb, so a tile is shared by at most two pairs: the one that
+    // runs its first k-blocks (the head, first on its list) stores the raw
+    // accumulator to sk_ws and sets its flags; the other (the tail, last on
+    // its list) loads that accumulator back into TMEM and continues
+    // accumulating, so each output is the same chain of MMAs into one fp32
+    // accumulator as without the split: the bits do not change.
+    int sk_dp_tiles;
+    int sk_q, sk_extra;
+    float* sk_ws;                   // [pair][cta][BN / 4][128 rows][4]: raw accumulators of heads
+    int* sk_flags;                  // [pair][cta][epilogue warp]: 1 once that warp's rows are stored
 };
+
+// Host side of the stream-K schedule: with `tiles` tiles of `num_kb`
+// k-blocks on `pairs` pairs, whole waves but the last run one tile per pair
+// (dp_tiles), and the remaining tiles (more than one wave, less than two) are
+// shared out by k-blocks: q each, q + 1 for the first `extra` pairs.  q = 0
+// when the tiles are a multiple of the pairs (or fewer), or when
+// MINIXLA_STREAMK=0.
+struct StreamKSplit {
+    int dp_tiles = 0, q = 0, extra = 0;
+};
+
+inline bool streamk_enabled() {
+    const char* v = getenv("MINIXLA_STREAMK");
+    return !(v && v[0] == '0');
+}
+
+inline StreamKSplit streamk_split(int tiles, int num_kb, int pairs) {
+    StreamKSplit s;
+    if (!streamk_enabled() || pairs < 2 || tiles <= pairs || tiles % pairs == 0) return s;
+    s.dp_tiles = (tiles / pairs - 1) * pairs;
+    const long long iters = static_cast<long long>(tiles - s.dp_tiles) * num_kb;
+    s.q = static_cast<int>(iters / pairs);
+    s.extra = static_cast<int>(iters % pairs);
+    return s;
+}
+
+// One unit of a CTA pair's work: k-blocks [kb0, kb1) of tile t.
+enum : int { kWorkFull = 0, kWorkHead = 1, kWorkTail = 2 };
+struct PairWork {
+    int t, kb0, kb1, kind;
+};
+
+// Item `idx` of pair `pair`'s list, in execution order: its stream-K head
+// (if any), its whole tiles (one per pair in turn, then whole tiles inside
+// its stream-K range), its stream-K tail (if any).  False past the end.
+__host__ __device__ __forceinline__ bool pair_work(const FusedParams& p, int pair, int num_pairs, int idx,
+                                                   PairWork& w) {
+    const int nk = p.num_kb;
+    if (p.sk_q == 0) {
+        w.t = pair + idx * num_pairs;
+        w.kb0 = 0;
+        w.kb1 = nk;
+        w.kind = kWorkFull;
+        return w.t < p.num_tiles;
+    }
+    const long long s = static_cast<long long>(pair) * p.sk_q + (pair < p.sk_extra ? pair : p.sk_extra);
+    const long long e = s + p.sk_q + (pair < p.sk_extra ? 1 : 0);
+    const int tile_lo = static_cast<int>(s / nk), tile_hi = static_cast<int>((e - 1) / nk);
+    const int tail_kb = static_cast<int>(s - static_cast<long long>(tile_lo) * nk);      // > 0: tail of tile_lo
+    const int head_kb = static_cast<int>(e - static_cast<long long>(tile_hi) * nk);      // < nk: head of tile_hi
+    const bool has_tail = tail_kb > 0, has_head = head_kb < nk;
+    int i = idx;
+    if (has_head) {
+        if (i == 0) {
+            w.t = p.sk_dp_tiles + tile_hi;
+            w.kb0 = 0;
+            w.kb1 = head_kb;
+            w.kind = kWorkHead;
+            return true;
+        }
+        --i;
+    }
+    const int n_dp = p.sk_dp_tiles / num_pairs;
+    if (i < n_dp) {
+        w.t = pair + i * num_pairs;
+        w.kb0 = 0;
+        w.kb1 = nk;
+        w.kind = kWorkFull;
+        return true;
+    }
+    i -= n_dp;
+    const int f_lo = has_tail ? tile_lo + 1 : tile_lo, f_hi = has_head ? tile_hi - 1 : tile_hi;
+    if (i <= f_hi - f_lo) {
+        w.t = p.sk_dp_tiles + f_lo + i;
+        w.kb0 = 0;
+        w.kb1 = nk;
+        w.kind = kWorkFull;
+        return true;
+    }
+    i -= f_hi >= f_lo ? f_hi - f_lo + 1 : 0;
+    if (has_tail && i == 0) {
+        w.t = p.sk_dp_tiles + tile_lo;
+        w.kb0 = tail_kb;
+        w.kb1 = nk;
+        w.kind = kWorkTail;
+        return true;
+    }
+    return false;
+}
 
 // Error bits written to the device error word.
 enum : int { kErrProducer = 1, kErrMma = 2, kErrEpilogue = 4, kErrProbe = 8 };

@@ -145,7 +145,8 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
         g.out_bstride = static_cast<long long>(M) * ldo;
         g.ep_bstride = batch->ep_bstride;
     }
-    float* ws[4] = {nullptr, nullptr, nullptr, nullptr};  // 3xTF32 low parts of A, B, B2; K-split slices
+    // 3xTF32 low parts of A, B, B2; K-split slices; stream-K accumulators and flags
+    float* ws[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
     int rc = MXB_OK;
     g.k_splits = fused_gemm_k_splits(g);
     if (g.k_splits > 1) {
@@ -154,6 +155,19 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
         ws[3] = static_cast<float*>(ctx->pool->alloc(g.k_splits * slice * sizeof(float), stream));
         if (!ws[3]) rc = MXB_E_NOMEM;
         g.ks_ws = ws[3];
+    }
+    if (const size_t skb = rc == MXB_OK ? fused_gemm_streamk_bytes(g) : 0) {
+        // The CTA-pair kernel's stream-K hand-off: accumulators of the pairs
+        // that run a split tile's first k-blocks, then one flag per epilogue warp.
+        const int pairs = ctx->num_sms / 2;
+        ws[4] = static_cast<float*>(ctx->pool->alloc(skb, stream));
+        if (!ws[4]) rc = MXB_E_NOMEM;
+        g.sk_ws = ws[4];
+        g.sk_flags = ws[4] ? reinterpret_cast<int*>(ws[4] + (skb - static_cast<size_t>(pairs) * 16 * sizeof(int)) /
+                                                                sizeof(float))
+                           : nullptr;
+        g.sk_pairs = pairs;
+        g.sk_cols = plan_fused_gemm(g, 1).tile_cols;
     }
     if (rc == MXB_OK && precision == GPU_PRECISION_3XTF32) {
         // Low parts of every product of a batch (stored back to back like A and B).

@@ -53,7 +53,20 @@ struct GemmLaunch {
     long long batch;
     long long a_bstride, b_bstride, out_bstride;
     const long long* ep_bstride;
+    // Stream-K workspace of the TF32 CTA-pair kernels (nullptr: none, every
+    // tile whole on one pair): room for sk_pairs pairs' raw accumulators
+    // (pairs x 2 x 128 x tile columns floats) and flags (pairs x 2 x 8 ints).
+    float* sk_ws;
+    int* sk_flags;
+    int sk_pairs;
+    int sk_cols;                       // tile columns sk_ws was sized for
 };
+
+// Stream-K workspace a launch of g needs (0: it runs no stream-K tail); the
+// caller passes it as GemmLaunch::sk_ws / sk_flags with sk_pairs = num_sms / 2.
+size_t fused_gemm_streamk_bytes(const GemmLaunch& g);
+// Tiles of g run as stream-K work on num_sms / 2 pairs (0: none).
+int fused_gemm_streamk_tiles(const GemmLaunch& g);
 
 // Skinny GEMM (skinny_gemm.cu): few output rows, CUDA-core fp32, split over
 // column blocks x K ranges; workspace holds splits * M * N floats.

@@ -587,6 +587,7 @@ int mxb_gemm_plan_for(int M, int N, int K, int precision, int num_sms, mxb_gemm_
     plan->tile_rows = pl.tile_rows;
     plan->tile_cols = pl.tile_cols;
     plan->k_splits = pl.k_splits;
+    plan->streamk_tiles = mxb::fused_gemm_streamk_tiles(g);
     return MXB_OK;
 }
 

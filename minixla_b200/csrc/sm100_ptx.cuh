@@ -176,12 +176,76 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
         : "memory");
 }
 
+// Store 32 consecutive columns (two x16 stores).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+        "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+        "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- flags and L2 hints between CTAs
+//
+// A flag in global memory that one CTA sets once its data is stored and
+// another CTA of the same grid polls before reading the data: a release
+// store and acquire loads at GPU scope.
+
+__device__ __forceinline__ void st_release_gpu(int* ptr, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
+
+// Bounded poll until *flag == want (every lane of the warp polls; the
+// acquire orders the lane's later loads after the writer's release).
+__device__ __forceinline__ bool wait_flag_gpu(const int* flag, int want, uint64_t timeout_ns) {
+    if (ld_acquire_gpu(flag) == want) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 1; it < (1u << 30); ++it) {
+        if (ld_acquire_gpu(flag) == want) return true;
+        if ((it & 15u) == 0 && global_timer_ns() - t0 > timeout_ns) return false;
+        __nanosleep(64);
+    }
+    return false;
+}
+
+// L2 cache policy that keeps lines resident ahead of others (evict_last).
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ void st_global_v4_hint(float* ptr, float a, float b, float c, float d, uint64_t pol) {
+    asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "f"(a), "f"(b), "f"(c),
+                 "f"(d), "l"(pol)
+                 : "memory");
+}
+
+__device__ __forceinline__ float4 ld_global_cg_v4(const float* ptr) {
+    float4 v;
+    asm volatile("ld.global.cg.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(ptr)
+                 : "memory");
+    return v;
 }
 
 // ---------------------------------------------------------------- CTA pairs (cta_group::2)

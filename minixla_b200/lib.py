@@ -91,7 +91,8 @@ class GemmPlan(C.Structure):
         ("tile_cols", C.c_int),
         ("k_splits", C.c_int),
         ("products", C.c_int),
-        ("reserved", C.c_int * 3),
+        ("streamk_tiles", C.c_int),
+        ("reserved", C.c_int * 2),
     ]
 
 

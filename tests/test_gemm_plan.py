@@ -2,6 +2,8 @@
 dispatcher follows, on a 148-SM GPU, without a GPU.  The same plan function
 drives the launches (launch_fused_gemm dispatches on it), so these cases pin
 what the GPU runs."""
+from pathlib import Path
+
 import pytest
 
 from minixla_b200 import lib as mlib
@@ -112,3 +114,49 @@ def test_plan_batched(shape, want, monkeypatch):
     monkeypatch.setenv("MINIXLA_BATCH_LAUNCH", "0")
     assert mlib.gemm_plan(m, n, k, prec, batch=b).products == 1
 
+
+
+# (M, N, K) -> stream-K tiles on 74 CTA pairs (TF32): tiles that do not make a
+# whole last wave are shared out by k-blocks over every pair.
+STREAMK = [
+    ((8192, 8192, 8192), 142),    # 512 tiles of 256 x 512 = 6 x 74 + 68: the last two waves' tiles
+    ((4096, 4096, 4096), 128),    # 128 tiles: all of them (1.73 waves)
+    ((4096, 8192, 8192), 108),    # the 8-way split of 32768 x 8192 x 8192: 256 tiles = 3 x 74 + 34
+    ((32768, 8192, 8192), 124),   # 2048 tiles = 27 x 74 + 50
+    ((2048, 2048, 2048), 0),      # 64 tiles of 256 x 256: fewer than the pairs
+    ((9472, 8192, 8192), 0),      # 592 tiles = 8 x 74 exactly
+]
+
+
+@pytest.mark.parametrize("shape,want", STREAMK, ids=[f"{m}x{n}x{k}" for (m, n, k), _ in STREAMK])
+def test_streamk_tiles(shape, want, monkeypatch):
+    for var in ("MINIXLA_STREAMK", "MINIXLA_GEMM_VARIANT"):
+        monkeypatch.delenv(var, raising=False)
+    assert mlib.gemm_plan(*shape, TF32).streamk_tiles == want
+    assert mlib.gemm_plan(*shape, X3).streamk_tiles == 0   # 3xTF32 pair kernel: whole tiles
+    monkeypatch.setenv("MINIXLA_STREAMK", "0")
+    assert mlib.gemm_plan(*shape, TF32).streamk_tiles == 0
+
+
+def test_streamk_schedule_covers_every_kblock_once(tmp_path):
+    """The stream-K work lists themselves (pair_work / streamk_split from
+    gemm_common.cuh, compiled for the host): every k-block of every tile runs
+    on exactly one pair; a split tile is shared by two neighbouring pairs, as
+    the first item of one and the last of the next (the accumulator hand-off
+    the kernel implements); the pairs' stream-K k-blocks differ by at most one."""
+    import random
+    import shutil
+    import subprocess
+
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    root = Path(__file__).resolve().parents[1]
+    exe = tmp_path / "streamk_schedule"
+    subprocess.run([nvcc, "-std=c++17", "-O1", "-gencode", "arch=compute_100a,code=sm_100a", "-I",
+                    str(root / "include"), "--expt-relaxed-constexpr", "-o", str(exe),
+                    str(root / "tests" / "native" / "streamk_schedule.cu")], check=True, capture_output=True)
+    rng = random.Random(7)
+    cases = [(128, 128, 74), (512, 256, 74), (256, 256, 74), (2048, 256, 74), (75, 1, 74), (149, 3, 74),
+             (64, 64, 74), (74, 9, 74), (1000, 33, 73), (3, 5, 2)]
+    cases += [(rng.randint(1, 3000), rng.randint(1, 300), rng.randint(2, 80)) for _ in range(300)]
+    out = subprocess.run([str(exe)] + [str(x) for c in cases for x in c], capture_output=True, text=True)
+    assert out.returncode == 0 and out.stdout.strip() == f"OK {len(cases)}", out.stdout

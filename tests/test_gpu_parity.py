@@ -895,3 +895,61 @@ def test_allocation_failure_injection(fail_at):
     r = subprocess.run([sys.executable, "-c", _OOM_CHILD, str(ROOT)], env=env, capture_output=True, text=True,
                        timeout=300)
     assert r.returncode == 0 and "OK" in r.stdout, r.stdout + r.stderr
+
+
+# (M, N, K) whose TF32 CTA-pair tiles do not fill a whole number of waves on
+# 74 pairs: 80 wide tiles (all stream-K), 96 tiles of 256 x 256 with a ragged
+# M, N and K, 128 wide tiles (4096^3), and the 8-way split of config 5
+# (256 wide tiles: 148 run whole, 108 stream-K).
+STREAMK_SHAPES = [(2560, 4096, 1024), (2000, 3001, 997), (4096, 4096, 4096), (4096, 8192, 8192)]
+
+
+@pytest.mark.parametrize("mnk", STREAMK_SHAPES, ids=[f"{m}x{n}x{k}" for m, n, k in STREAMK_SHAPES])
+def test_stream_k_keeps_the_bits(lib, gpu_ctx, mnk, monkeypatch, host_threads):
+    """Stream-K hands a split tile's raw fp32 accumulator from one CTA pair to
+    the next and continues the same MMA chain, so the output must be bit-equal
+    to the launch that runs every tile whole (MINIXLA_STREAMK=0) -- and match
+    the oracle on sampled rows (tile edges, shard-like edges, random rows)
+    within the TF32 tolerance, for relu(A.B + C) + bias."""
+    import torch
+
+    M, N, K = mnk
+    sms = torch.cuda.get_device_properties(lib.gpu_ctx_device(gpu_ctx)).multi_processor_count
+    plan = mlib.gemm_plan(M, N, K, TF32, sms)
+    if plan.kernel != mlib.MXB_KERNEL_CTA_PAIR or plan.streamk_tiles == 0:
+        pytest.skip(f"{sms} SMs: {mnk} runs no stream-K tail")
+    dev = torch.device("cuda", lib.gpu_ctx_device(gpu_ctx))
+    A_h = datagen.uniform((M, K), 30)
+    B_h = datagen.uniform((K, N), 31)
+    C_h = datagen.normal((M, N), 32)
+    bias_h = datagen.normal((N,), 33, 0.0, 0.5)
+    Kp, Np = (K + 3) // 4 * 4, (N + 3) // 4 * 4
+
+    def padded(x, cols):
+        t = torch.zeros((x.shape[0], cols), device=dev)
+        t[:, :x.shape[1]] = torch.from_numpy(x).to(dev)
+        return t
+
+    A, B = padded(A_h, Kp), padded(B_h, Np)
+    C = torch.from_numpy(C_h).to(dev)
+    bias = torch.from_numpy(bias_h).to(dev)
+    steps = (mlib.EpStepDev * 3)()
+    steps[0] = mlib.EpStepDev(mlib.MXB_EP_ADD_FULL, 0, C.data_ptr(), N, 0.0, 0)
+    steps[1] = mlib.EpStepDev(mlib.MXB_EP_RELU, 0, None, 0, 0.0, 0)
+    steps[2] = mlib.EpStepDev(mlib.MXB_EP_ADD_ROW, 0, bias.data_ptr(), N, 0.0, 0)
+    outs = {}
+    for sk in ("1", "0"):
+        monkeypatch.setenv("MINIXLA_STREAMK", sk)
+        out = torch.full((M, N), float("nan"), device=dev)
+        for _ in range(2):  # twice: flags and accumulators of one launch do not leak into the next
+            rc = lib.mxb_fused_gemm(gpu_ctx, A.data_ptr(), Kp, B.data_ptr(), Np, out.data_ptr(), N, M, N, K,
+                                    steps, 3, TF32, None)
+            assert rc == 0, mlib.last_error()
+        assert lib.mxb_check_device_error(gpu_ctx) == 0
+        outs[sk] = out.cpu().numpy()
+    assert not np.isnan(outs["1"]).any()
+    assert np.array_equal(outs["1"], outs["0"]), "stream-K changed the bits"
+    rng = np.random.default_rng(M + N)
+    rows = sorted({0, 1, 127, 128, 255, 256, 257, M // 2, M - 2, M - 1, *rng.integers(0, M, 48).tolist()})
+    want = bindings.fused_oracle(A_h, B_h, [("add", C_h), ("relu",), ("add", bias_h)], rows=rows, threads=host_threads)
+    check(outs["1"][rows], want, TF32, f"stream-K {mnk}")
