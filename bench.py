@@ -4,23 +4,32 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 One step = one fused relu(A.B + C) over one batch of rows, fp32 in and out.
-Workload: every GPU owns an 8192-row shard of A and C with the full 8192 x 8192
-B (weak scaling: the single-GPU case is the 8192^3 headline shape; at 4 GPUs
-the job is the 32768 x 8192 x 8192 row-sharded shape).  Output rows stay on
-their GPU; no collective runs on the data path (at N > 1 an NCCL all-gather of
-the output rows is timed after the kernel steps and reported apart, as
-`allgather`).  `--workload strong` runs the
-fixed 32768 x 8192 x 8192 job split over N GPUs instead (strong scaling).
+Workload of `value`: every GPU owns an 8192-row shard of A and C with the
+full 8192 x 8192 B (weak scaling: the single-GPU case is the 8192^3 headline
+shape).  Output rows stay on their GPU; no collective runs on the data path.
+`--workload strong` makes `value` the fixed 32768 x 8192 x 8192 job instead.
 
 ours:      `value` = whole-job TFLOP/s with inputs resident in HBM, K launches of
            the fused kernel through the device-pointer C ABI, timed with CUDA
-           events on the launch stream, max over ranks.  `e2e` = the same metric
-           through gpu_execute_into() (the reference-facing entry point) with
-           pinned host buffers, uploads and the download inside the timed region.
+           events on the launch stream, max over ranks.
+           `e2e` = the same metric through gpu_execute() -- the reference's own
+           entry point -- on pageable (malloc'd) host buffers, the returned
+           tensor freed inside the step; `e2e.pinned_into` is the additive
+           gpu_execute_into() with pinned buffers.
+           `precision_3xtf32` = the default (fp32-faithful) mode, same loop.
+           `strong` = the fixed 32768 x 8192 x 8192 job split by rows over the
+           N GPUs: kernel only, with the row all-gather fused into the
+           epilogue and with an NCCL all-gather after the kernel; speed-up and
+           efficiency against the whole job on one GPU of the same run; >= 64
+           rows per rank checked against the oracle.
+           `sharded_executor` (N > 1) = the same job through the product's
+           one-process multi-GPU executor (gpu_ctx_create_multi + gpu_execute).
+           `allgather` = the all-gathers on the 8192-row shards of `value`.
 reference: MiniXLA's own CPU execute() (eval_fused, graph.c:64-115), compiled
            unmodified from the reference sources into oracle/_ref, on a bounded
            row sample of the same workload using all host cores (one process per
-           core, row-parallel), rank 0 only.
+           core, row-parallel), rank 0 only.  The reference has no multi-GPU
+           path, so its value does not depend on N.
 """
 from __future__ import annotations
 
@@ -247,7 +256,9 @@ def reference_arm(args, rank, world):
         "ms_per_step": 1e3 * total / len(timed), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded splitmix64: A,B ~ U[-1,1], C ~ N(0,1))",
         "config": {"workload": "relu(A.B+C) 8192x8192x8192 per shard, row sample per step",
-                   "rows_per_step": rows, "N": NDIM, "K": NDIM, "parallelism": f"{workers} host processes"},
+                   "rows_per_step": rows, "N": NDIM, "K": NDIM, "parallelism": f"{workers} host processes",
+                   "note": "host CPU cores only: the reference's execute() has no GPU or multi-GPU path, so this "
+                           "value is the same at every N"},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": workers, "kind": kind,
                          "sample": f"{rows} output rows per step ({workers} processes x 1 row) through "
                                    "MiniXLA's execute()"},

@@ -3,9 +3,12 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <condition_variable>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
+#include <thread>
 #include <unordered_map>
 #include <unordered_set>
 #include <vector>
@@ -176,6 +179,40 @@ int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
         }
     }
     std::vector<cudaEvent_t> computed(n_chunks, nullptr);
+    // Result rows come back on their own host thread (with their own pinned
+    // ring), chunk by chunk as soon as each chunk's kernels are enqueued, so
+    // a pageable destination is filled while later chunks are still being
+    // staged up: the two directions of the link and of the host copies run
+    // side by side.
+    const Info& root = info.back();
+    const long long out_cols = root.size / M;
+    std::mutex dl_mu;
+    std::condition_variable dl_cv;
+    int enqueued = 0;        // chunks whose computed event is recorded
+    bool abandon = false;    // the main thread stopped early
+    int dl_rc = MXB_OK;
+    std::thread downloader([&] {
+        if (!cuda_ok(cudaSetDevice(ctx->device), "download thread device")) {
+            dl_rc = MXB_E_CUDA;
+            return;
+        }
+        for (int c = 0; c < n_chunks; ++c) {
+            {
+                std::unique_lock<std::mutex> lk(dl_mu);
+                dl_cv.wait(lk, [&] { return enqueued > c || abandon; });
+                if (enqueued <= c) return;
+            }
+            const long long r0 = static_cast<long long>(c) * rows_per;
+            const long long r1 = std::min<long long>(M, r0 + rows_per);
+            if (cudaStreamWaitEvent(ds, computed[c], 0) != cudaSuccess ||
+                !cuda_ok(copy_d2h(ctx->stager_dl, host_dst + r0 * out_cols, root.dev + r0 * out_cols,
+                                  static_cast<size_t>((r1 - r0) * out_cols) * 4, ds),
+                         "chunk download")) {
+                dl_rc = MXB_E_CUDA;
+                return;
+            }
+        }
+    });
     for (int c = 0; c < n_chunks && rc == MXB_OK; ++c) {
         const long long r0 = static_cast<long long>(c) * rows_per;
         const long long r1 = std::min<long long>(M, r0 + rows_per);
@@ -244,22 +281,28 @@ int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
             }
         }
         if (rc == MXB_OK) {
-            computed[c] = sync_event(ctx, next_event++);
-            if (!computed[c] || cudaEventRecord(computed[c], cs) != cudaSuccess) rc = MXB_E_CUDA;
+            // computed[] is filled before the download thread may read it
+            // (sync_event grows ctx->sync_events only on this thread).
+            cudaEvent_t e = sync_event(ctx, next_event++);
+            if (!e || cudaEventRecord(e, cs) != cudaSuccess) {
+                rc = MXB_E_CUDA;
+            } else {
+                std::lock_guard<std::mutex> lk(dl_mu);
+                computed[c] = e;
+                enqueued = c + 1;
+            }
+            dl_cv.notify_one();
         }
     }
-    // Downloads are enqueued after all uploads and kernels: with a pageable
-    // destination each copy blocks the host until it is done.
-    const Info& root = info.back();
-    const long long out_cols = root.size / M;
-    for (int c = 0; c < n_chunks && rc == MXB_OK; ++c) {
-        const long long r0 = static_cast<long long>(c) * rows_per;
-        const long long r1 = std::min<long long>(M, r0 + rows_per);
-        if (cudaStreamWaitEvent(ds, computed[c], 0) != cudaSuccess ||
-            !cuda_ok(copy_d2h(ctx->stager, host_dst + r0 * out_cols, root.dev + r0 * out_cols,
-                              static_cast<size_t>((r1 - r0) * out_cols) * 4, ds),
-                     "chunk download"))
-            rc = MXB_E_CUDA;
+    {
+        std::lock_guard<std::mutex> lk(dl_mu);
+        abandon = true;
+    }
+    dl_cv.notify_one();
+    downloader.join();
+    if (rc == MXB_OK && dl_rc != MXB_OK) {
+        set_error("row streaming: a result download failed");
+        rc = dl_rc;
     }
     // The pool reuses blocks in compute-stream order: join both copy streams first.
     order_after(cs, ds);

@@ -309,17 +309,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                 }
                 const float* src = p.sk_ws + (static_cast<long long>(src_pair) * 2 + rank) * (BN * 128) +
                                    (quad * 32 + lane) * 4;
-                for (int c = c_first; c < chunks; ++c) {
-                    uint32_t r[32];
+                // Four chunks' loads in flight per round trip (the MMA warp
+                // waits for this buffer meanwhile).
+                for (int c0 = c_first; c0 < chunks; c0 += 4) {
+                    uint32_t r[4][32];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float4 x = ld_global_cg_v4(src + (8 * c + j) * 512);
-                        r[4 * j + 0] = __float_as_uint(x.x);
-                        r[4 * j + 1] = __float_as_uint(x.y);
-                        r[4 * j + 2] = __float_as_uint(x.z);
-                        r[4 * j + 3] = __float_as_uint(x.w);
+                    for (int u = 0; u < 4; ++u) {
+                        if (c0 + u < chunks) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                const float4 x = ld_global_cg_v4(src + (8 * (c0 + u) + j) * 512);
+                                r[u][4 * j + 0] = __float_as_uint(x.x);
+                                r[u][4 * j + 1] = __float_as_uint(x.y);
+                                r[u][4 * j + 2] = __float_as_uint(x.z);
+                                r[u][4 * j + 3] = __float_as_uint(x.w);
+                            }
+                        }
                     }
-                    tmem_st_32x32b_x32(taddr + 32 * c, r);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        if (c0 + u < chunks) tmem_st_32x32b_x32(taddr + 32 * (c0 + u), r[u]);
                 }
                 tmem_st_wait();
                 tc_fence_before();

@@ -102,9 +102,16 @@ inline bool streamk_enabled() {
     return !(v && v[0] == '0');
 }
 
+// Used when the idle share of the last wave is at least 1/kStreamKMinLoss of
+// the job (one idle pair-tile in 25): below that the hand-offs cost about
+// what they win back.
+constexpr int kStreamKMinLoss = 25;
+
 inline StreamKSplit streamk_split(int tiles, int num_kb, int pairs) {
     StreamKSplit s;
     if (!streamk_enabled() || pairs < 2 || tiles <= pairs || tiles % pairs == 0) return s;
+    const long long idle = static_cast<long long>(pairs - tiles % pairs);
+    if (idle * kStreamKMinLoss < tiles) return s;
     s.dp_tiles = (tiles / pairs - 1) * pairs;
     const long long iters = static_cast<long long>(tiles - s.dp_tiles) * num_kb;
     s.q = static_cast<int>(iters / pairs);
@@ -118,9 +125,12 @@ struct PairWork {
     int t, kb0, kb1, kind;
 };
 
-// Item `idx` of pair `pair`'s list, in execution order: its stream-K head
-// (if any), its whole tiles (one per pair in turn, then whole tiles inside
-// its stream-K range), its stream-K tail (if any).  False past the end.
+// Item `idx` of pair `pair`'s list, in execution order: its whole tiles of
+// the first waves (one per pair in turn, so the pairs keep step through them
+// and share A and B in L2 as without stream-K), then its stream-K head (if
+// any), the whole tiles inside its stream-K range, and its stream-K tail (if
+// any), which comes last so that the neighbouring pair's head is long done.
+// False past the end.
 __host__ __device__ __forceinline__ bool pair_work(const FusedParams& p, int pair, int num_pairs, int idx,
                                                    PairWork& w) {
     const int nk = p.num_kb;
@@ -138,6 +148,15 @@ __host__ __device__ __forceinline__ bool pair_work(const FusedParams& p, int pai
     const int head_kb = static_cast<int>(e - static_cast<long long>(tile_hi) * nk);      // < nk: head of tile_hi
     const bool has_tail = tail_kb > 0, has_head = head_kb < nk;
     int i = idx;
+    const int n_dp = p.sk_dp_tiles / num_pairs;
+    if (i < n_dp) {
+        w.t = pair + i * num_pairs;
+        w.kb0 = 0;
+        w.kb1 = nk;
+        w.kind = kWorkFull;
+        return true;
+    }
+    i -= n_dp;
     if (has_head) {
         if (i == 0) {
             w.t = p.sk_dp_tiles + tile_hi;
@@ -148,15 +167,6 @@ __host__ __device__ __forceinline__ bool pair_work(const FusedParams& p, int pai
         }
         --i;
     }
-    const int n_dp = p.sk_dp_tiles / num_pairs;
-    if (i < n_dp) {
-        w.t = pair + i * num_pairs;
-        w.kb0 = 0;
-        w.kb1 = nk;
-        w.kind = kWorkFull;
-        return true;
-    }
-    i -= n_dp;
     const int f_lo = has_tail ? tile_lo + 1 : tile_lo, f_hi = has_head ? tile_hi - 1 : tile_hi;
     if (i <= f_hi - f_lo) {
         w.t = p.sk_dp_tiles + f_lo + i;
@@ -347,13 +357,17 @@ __device__ __forceinline__ void store_row_chunk(const float (&v)[W], int row, in
 // loads, which hit L2.  One instruction moves 512 contiguous bytes of a row;
 // kU rows are in flight at a time.  The stores are plain global stores to
 // peer addresses (NVLink), so this warp's cost is issue only while the link
-// drains, and it runs while the MMA warp is already on the next tile.
+// drains, and it runs while the MMA warp is already on the next tile.  Each
+// warp starts its round of peers at a different one (by its 32-row block),
+// so the warps of a GPU spread their stores over every peer's ingress at
+// once instead of all writing to the same GPU first.
 template <int kU = 4>
 __device__ __forceinline__ void push_rows(const FusedParams& p, int row0, int c0, int c1) {
     __syncwarp();
     const int lane = threadIdx.x & 31;
     const int rows = min(32, p.M - row0);
     if (rows <= 0 || c0 >= c1) return;
+    const int q0 = (row0 >> 5) % p.n_peers;
     if (p.push_vec) {
         // c0 is a multiple of 32, so every float4 below is 16-byte aligned.
         const int segs = (c1 - c0 + 127) / 128;  // 128-column segments per row
@@ -374,7 +388,11 @@ __device__ __forceinline__ void push_rows(const FusedParams& p, int row0, int c0
 #pragma unroll
             for (int u = 0; u < kU; ++u) {
                 if (col[u] + 4 <= c1) {
-                    for (int q = 0; q < p.n_peers; ++q) *reinterpret_cast<float4*>(p.peer_out[q] + off[u]) = v[u];
+                    int q = q0;
+                    for (int j = 0; j < p.n_peers; ++j) {
+                        *reinterpret_cast<float4*>(p.peer_out[q] + off[u]) = v[u];
+                        q = q + 1 == p.n_peers ? 0 : q + 1;
+                    }
                 } else {
                     // Row tail when N % 4 != 0: at most three scalars.
                     for (int j = 0; col[u] + j < c1; ++j) {

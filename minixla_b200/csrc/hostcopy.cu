@@ -29,12 +29,22 @@ constexpr size_t kStageMinBytes = 2u << 20;  // smaller copies: the driver's own
 
 // A small pool of host threads that split one memcpy between them (one
 // thread moves about 10 GB/s).  One copy at a time; the caller takes part 0.
+// Each Stager owns one, so uploads and downloads staged at the same time (on
+// two host threads) do not queue behind each other.
 class CopyThreads {
   public:
-    static CopyThreads& get() {
-        static CopyThreads t;
-        return t;
+    CopyThreads() = default;
+    // Starts the helpers (once): a quarter of the cores per pool, as two
+    // pools may run at once, at most seven.
+    void start() {
+        if (started_) return;
+        started_ = true;
+        const unsigned hw = std::thread::hardware_concurrency();
+        const unsigned n = hw >= 8 ? std::min(7u, hw / 4) : 0;
+        for (unsigned i = 0; i < n; ++i) workers_.emplace_back([this, i] { run(i + 1); });
     }
+    CopyThreads(const CopyThreads&) = delete;
+    CopyThreads& operator=(const CopyThreads&) = delete;
 
     void copy(void* dst, const void* src, size_t bytes) {
         if (workers_.empty() || bytes < (1u << 20)) {
@@ -59,13 +69,6 @@ class CopyThreads {
         done_.wait(lk, [&] { return pending_ == 0; });
     }
 
-  private:
-    CopyThreads() {
-        const unsigned hw = std::thread::hardware_concurrency();
-        const unsigned n = hw >= 4 ? std::min(7u, hw / 2) : 0;
-        for (unsigned i = 0; i < n; ++i) workers_.emplace_back([this, i] { run(i + 1); });
-    }
-
     ~CopyThreads() {
         {
             std::lock_guard<std::mutex> lk(mu_);
@@ -76,6 +79,7 @@ class CopyThreads {
         for (std::thread& t : workers_) t.join();
     }
 
+  private:
     void run(size_t part) {
         uint64_t seen = 0;
         for (;;) {
@@ -107,6 +111,7 @@ class CopyThreads {
     size_t bytes_ = 0, per_ = 0, pending_ = 0;
     uint64_t gen_ = 0;
     bool stop_ = false;
+    bool started_ = false;
 };
 
 bool host_pinned(const void* p) {
@@ -160,6 +165,7 @@ class Stager {
             }
         }
         buf_ = static_cast<char*>(b);
+        copier_.start();
         return true;
     }
 
@@ -169,7 +175,7 @@ class Stager {
             const int s = take_slot();
             cudaError_t e = cudaEventSynchronize(ev_[s]);  // the slot's previous copy has left it
             if (e != cudaSuccess) return e;
-            CopyThreads::get().copy(slot(s), src + off, n);
+            copier_.copy(slot(s), src + off, n);
             if ((e = cudaMemcpyAsync(dst + off, slot(s), n, cudaMemcpyHostToDevice, st)) != cudaSuccess) return e;
             if ((e = cudaEventRecord(ev_[s], st)) != cudaSuccess) return e;
         }
@@ -196,7 +202,7 @@ class Stager {
             const int s = slot_of[i];
             if ((e = cudaEventSynchronize(ev_[s])) != cudaSuccess) break;
             const size_t off = i * kSlotBytes;
-            CopyThreads::get().copy(dst + off, slot(s), std::min(kSlotBytes, bytes - off));
+            copier_.copy(dst + off, slot(s), std::min(kSlotBytes, bytes - off));
             if (issued < pieces) e = issue(issued++);  // reuses the slot just emptied
         }
         return e;
@@ -214,6 +220,7 @@ class Stager {
     cudaEvent_t ev_[kSlots] = {};
     int next_ = 0;
     bool failed_ = false;
+    CopyThreads copier_;
 };
 
 Stager* stager_create() { return new (std::nothrow) Stager(); }

@@ -299,7 +299,8 @@ GpuCtx* gpu_ctx_create_on(int device) {
               cuda_ok(cudaEventCreate(&g->ev0), "event create") && cuda_ok(cudaEventCreate(&g->ev1), "event create");
     if (ok) g->pool = new (std::nothrow) mxb::DevicePool(device);
     if (ok) g->stager = mxb::stager_create();  // its pinned slots are made on first use
-    if (!ok || !g->pool || !g->stager) {
+    if (ok) g->stager_dl = mxb::stager_create();
+    if (!ok || !g->pool || !g->stager || !g->stager_dl) {
         gpu_ctx_destroy(g);
         return nullptr;
     }
@@ -427,6 +428,7 @@ void gpu_ctx_destroy(GpuCtx* g) {
         mxb::DeviceScope scope(g->device);
         if (g->stream) cudaStreamSynchronize(g->stream);
         mxb::stager_destroy(g->stager);
+        mxb::stager_destroy(g->stager_dl);
         delete g->pool;
         if (g->d_err) cudaFree(g->d_err);
         if (g->ev0) cudaEventDestroy(g->ev0);

@@ -196,6 +196,7 @@ struct GpuCtx {
     int* d_err = nullptr;
     mxb::DevicePool* pool = nullptr;
     mxb::Stager* stager = nullptr;   // pinned slots for copies from / to pageable host memory
+    mxb::Stager* stager_dl = nullptr;  // a second ring for downloads that run beside uploads
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     std::vector<cudaEvent_t> sync_events;  // reusable ordering events (no timing)
     std::vector<GpuCtx*> peers;            // devices 1..n-1 of a multi-GPU context

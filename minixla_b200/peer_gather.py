@@ -40,7 +40,7 @@ def _check(rc: int, what: str) -> None:
 class GatherBuffers:
     """Every rank's [rows_total, cols] fp32 output (row pitch ``ldo``),
     mapped into this process; ``peer_rows(row0)`` are the addresses of row
-    ``row0`` in the other ranks' copies, in rank order without this rank."""
+    ``row0`` in the other ranks' copies, in ``peer_order()``."""
 
     def __init__(self, lib, device: int, rows_total: int, cols: int, ldo: int | None = None, group=None):
         import torch.distributed as dist
@@ -84,8 +84,14 @@ class GatherBuffers:
     def local_rows(self, row0: int) -> int:
         return self.local + 4 * row0 * self.ldo
 
+    def peer_order(self):
+        """The other ranks, starting after this one (rank + 1, rank + 2, ...,
+        wrapping): every rank lists a different peer first, so the ranks'
+        kernels do not all store to the same GPU at the same time."""
+        return [(self.rank + i) % self.world for i in range(1, self.world)]
+
     def peer_rows(self, row0: int):
-        ptrs = [self.remote[r] + 4 * row0 * self.ldo for r in sorted(self.remote)]
+        ptrs = [self.remote[r] + 4 * row0 * self.ldo for r in self.peer_order()]
         return (C.c_void_p * max(1, len(ptrs)))(*ptrs), len(ptrs)
 
     def gemm(self, ctx, A: int, lda: int, B: int, ldb: int, row0: int, M: int, N: int, K: int, steps, n_steps: int,

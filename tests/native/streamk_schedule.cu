@@ -3,10 +3,10 @@
 // tests/test_gemm_plan.py: for every (tiles, k-blocks, pairs) case given on
 // the command line, every k-block of every tile is run by exactly one pair,
 // in one contiguous range per (pair, tile); a split tile is shared by exactly
-// two pairs, p (its first k-blocks, the first item on p's list) and p + 1
-// (the rest, the last item on p + 1's list), which is the hand-off the kernel
-// implements; and the pairs' k-block counts differ by at most one within the
-// stream-K region.  Prints "OK <cases>" or the first violation.
+// two pairs, p (its first k-blocks, on p's list right after its whole-wave
+// tiles) and p + 1 (the rest, the last item on p + 1's list), which is the
+// hand-off the kernel implements; and the pairs' k-block counts differ by at
+// most one within the stream-K region.  Prints "OK <cases>" or the first violation.
 #include <cstdio>
 #include <cstdlib>
 #include <vector>
@@ -33,7 +33,7 @@ static int check(int tiles, int nk, int pairs) {
     std::vector<long long> work(launched, 0);
     for (int pr = 0; pr < launched; ++pr) {
         PairWork w;
-        int n = 0;
+        int n = 0, n_dp_seen = 0;
         for (int idx = 0; pair_work(p, pr, launched, idx, w); ++idx, ++n) {
             if (w.t < 0 || w.t >= tiles || w.kb0 < 0 || w.kb1 > nk || w.kb0 >= w.kb1) {
                 printf("FAIL tiles=%d nk=%d pairs=%d: pair %d item %d bad (%d,%d,%d)\n", tiles, nk, pairs, pr, idx,
@@ -49,8 +49,15 @@ static int check(int tiles, int nk, int pairs) {
                 o = pr;
             }
             if (w.t >= sk.dp_tiles || sk.q == 0) work[pr] += w.kb1 - w.kb0;
+            if (sk.q > 0 && w.t < sk.dp_tiles) {
+                if (idx != n_dp_seen) {  // the whole-wave tiles come first
+                    printf("FAIL tiles=%d nk=%d pairs=%d: pair %d wave tile at item %d\n", tiles, nk, pairs, pr, idx);
+                    return 1;
+                }
+                ++n_dp_seen;
+            }
             const bool whole = w.kb0 == 0 && w.kb1 == nk;
-            if (whole != (w.kind == kWorkFull) || (w.kind == kWorkHead && (w.kb0 != 0 || idx != 0)) ||
+            if (whole != (w.kind == kWorkFull) || (w.kind == kWorkHead && (w.kb0 != 0 || idx != n_dp_seen)) ||
                 (w.kind == kWorkTail && w.kb1 != nk)) {
                 printf("FAIL tiles=%d nk=%d pairs=%d: pair %d item %d kind %d (%d,%d)\n", tiles, nk, pairs, pr, idx,
                        w.kind, w.kb0, w.kb1);

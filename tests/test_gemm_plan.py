@@ -119,10 +119,10 @@ def test_plan_batched(shape, want, monkeypatch):
 # (M, N, K) -> stream-K tiles on 74 CTA pairs (TF32): tiles that do not make a
 # whole last wave are shared out by k-blocks over every pair.
 STREAMK = [
-    ((8192, 8192, 8192), 142),    # 512 tiles of 256 x 512 = 6 x 74 + 68: the last two waves' tiles
-    ((4096, 4096, 4096), 128),    # 128 tiles: all of them (1.73 waves)
+    ((4096, 4096, 4096), 128),    # 128 tiles: all of them (1.73 waves; 20 idle pair-tiles)
     ((4096, 8192, 8192), 108),    # the 8-way split of 32768 x 8192 x 8192: 256 tiles = 3 x 74 + 34
-    ((32768, 8192, 8192), 124),   # 2048 tiles = 27 x 74 + 50
+    ((8192, 8192, 8192), 0),      # 512 tiles = 6 x 74 + 68: 6 idle pair-tiles, under 1 in 25
+    ((32768, 8192, 8192), 0),     # 2048 tiles = 27 x 74 + 50: 24 idle, under 1 in 25
     ((2048, 2048, 2048), 0),      # 64 tiles of 256 x 256: fewer than the pairs
     ((9472, 8192, 8192), 0),      # 592 tiles = 8 x 74 exactly
 ]
@@ -143,7 +143,8 @@ def test_streamk_schedule_covers_every_kblock_once(tmp_path):
     gemm_common.cuh, compiled for the host): every k-block of every tile runs
     on exactly one pair; a split tile is shared by two neighbouring pairs, as
     the first item of one and the last of the next (the accumulator hand-off
-    the kernel implements); the pairs' stream-K k-blocks differ by at most one."""
+    the kernel implements), coming after the pair's whole-wave tiles and last
+    on the next pair's list; the pairs' stream-K k-blocks differ by at most one."""
     import random
     import shutil
     import subprocess

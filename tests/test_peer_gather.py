@@ -300,3 +300,20 @@ def test_fused_allgather_all_gpus():
             assert r["pushed"] == (1 if expect_push else 0), r
     for p in procs:
         assert p.exitcode == 0
+
+
+def test_peer_order_starts_after_this_rank():
+    """Every rank lists its peers starting with the next rank, so at any
+    moment the ranks' first stores go to different GPUs (host-only)."""
+    from minixla_b200.peer_gather import GatherBuffers
+
+    for world in (2, 4, 8):
+        firsts = []
+        for rank in range(world):
+            gb = GatherBuffers.__new__(GatherBuffers)
+            gb.rank, gb.world = rank, world
+            order = gb.peer_order()
+            assert sorted(order) == [r for r in range(world) if r != rank]
+            assert order == [(rank + i) % world for i in range(1, world)]
+            firsts.append(order[0])
+        assert sorted(firsts) == list(range(world))
