@@ -59,7 +59,7 @@ int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) {
         // Not row-shardable: the whole graph runs on device 0.
     }
 
-    const int chunks = stream_chunks();
+    const int chunks = stream_chunks(info.back().size * 4);
     if (chunks > 1 && info.back().dims.size() == 2 && info.back().dims[0] >= 2 * 128) {
         const RowStreamPlan plan = plan_row_stream(order, index, info);
         if (plan.ok) {
@@ -76,7 +76,7 @@ int execute_graph(Node* root, GpuCtx* ctx, Tensor* dst, Tensor** result) {
                 set_error("gpu_execute: host allocation of the result failed");
                 return MXB_E_NOMEM;
             }
-            const int rc = execute_streamed(ctx, order, index, info, plan, chunks, t->data);
+            const int rc = execute_streamed(ctx, order, index, info, plan, chunks, t->data, true);
             if (rc != MXB_OK) {
                 free(t->data);
                 free(t->shape);

@@ -105,7 +105,7 @@ cudaEvent_t sync_event(GpuCtx* ctx, size_t k) {
 // `host_dst` (root.size floats).
 int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
                      const std::unordered_map<const Node*, int>& index, std::vector<Info>& info,
-                     const RowStreamPlan& plan, int chunks, float* host_dst) {
+                     const RowStreamPlan& plan, int chunks, float* host_dst, bool fresh_dst) {
     cudaStream_t cs = ctx->stream, hs = ctx->h2d, ds = ctx->d2h;
     const int M = plan.M;
     const int rows_per = std::max(128, (M + chunks - 1) / chunks);
@@ -196,6 +196,9 @@ int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
             dl_rc = MXB_E_CUDA;
             return;
         }
+        // A fresh destination (gpu_execute's new result tensor): take its page
+        // faults now, while the inputs are still going up.
+        if (fresh_dst) prefault_host(ctx->stager_dl, host_dst, static_cast<size_t>(root.size) * 4);
         for (int c = 0; c < n_chunks; ++c) {
             {
                 std::unique_lock<std::mutex> lk(dl_mu);
@@ -319,9 +322,9 @@ int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
     return rc != MXB_OK ? rc : done;
 }
 
-int stream_chunks() {
-    const char* c = getenv("MINIXLA_STREAM_CHUNKS");
-    return c ? atoi(c) : 8;
+int stream_chunks(long long root_bytes) {
+    if (const char* c = getenv("MINIXLA_STREAM_CHUNKS")) return atoi(c);
+    return root_bytes >= (128ll << 20) ? 16 : 8;
 }
 
 }  // namespace mxb

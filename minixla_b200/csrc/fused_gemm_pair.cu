@@ -356,10 +356,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             }
             if (head) {
                 // A stream-K head: the raw accumulator goes to this pair's slot
-                // ([column / 4][row][4], 512 contiguous bytes per instruction),
-                // kept in L2 for the tail pair; no epilogue.
+                // ([column / 4][row][4], 512 contiguous bytes per instruction);
+                // no epilogue.
                 float* dst = p.sk_ws + (static_cast<long long>(pair) * 2 + rank) * (BN * 128) + (quad * 32 + lane) * 4;
-                const uint64_t pol = l2_policy_evict_last();
+                const uint64_t pol = l2_policy_evict_normal();
                 for (int c = c_first; c < chunks; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + 32 * c, r);

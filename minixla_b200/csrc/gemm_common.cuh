@@ -104,12 +104,23 @@ inline bool streamk_enabled() {
 
 // Used when the idle share of the last wave is at least 1/kStreamKMinLoss of
 // the job (one idle pair-tile in 25): below that the hand-offs cost about
-// what they win back.
+// what they win back (8192^3: 6 idle pair-tiles in 512, no gain measured).
 constexpr int kStreamKMinLoss = 25;
+constexpr int kStreamKMinKb = 64;
 
 inline StreamKSplit streamk_split(int tiles, int num_kb, int pairs) {
     StreamKSplit s;
-    if (!streamk_enabled() || pairs < 2 || tiles <= pairs || tiles % pairs == 0) return s;
+    // At least two whole waves: the pairs run the first ones in step (tiles
+    // that share rows of A or columns of B read the same k-blocks at the same
+    // time, so L2 serves them once), and the stream-K part, whose pairs sit
+    // at different k and read A and B several times over from HBM (4096^3,
+    // all of it stream-K: 712 vs 293 MB of DRAM reads, L2 hits 51 vs 70%),
+    // stays under half the work.
+    // And k-loops of at least kStreamKMinKb blocks: with short ones the
+    // hand-off costs more than the balance wins ((3300, 6001, 997): 229 vs
+    // 217 us; (5120, 4096, 1024): even).
+    if (!streamk_enabled() || pairs < 2 || tiles < 2 * pairs || tiles % pairs == 0 || num_kb < kStreamKMinKb)
+        return s;
     const long long idle = static_cast<long long>(pairs - tiles % pairs);
     if (idle * kStreamKMinLoss < tiles) return s;
     s.dp_tiles = (tiles / pairs - 1) * pairs;

@@ -46,28 +46,12 @@ class CopyThreads {
     CopyThreads(const CopyThreads&) = delete;
     CopyThreads& operator=(const CopyThreads&) = delete;
 
-    void copy(void* dst, const void* src, size_t bytes) {
-        if (workers_.empty() || bytes < (1u << 20)) {
-            memcpy(dst, src, bytes);
-            return;
-        }
-        std::lock_guard<std::mutex> job(job_mu_);
-        const size_t parts = workers_.size() + 1;
-        const size_t per = ((bytes + parts - 1) / parts + 63) & ~static_cast<size_t>(63);
-        {
-            std::lock_guard<std::mutex> lk(mu_);
-            dst_ = static_cast<char*>(dst);
-            src_ = static_cast<const char*>(src);
-            bytes_ = bytes;
-            per_ = per;
-            pending_ = workers_.size();
-            ++gen_;
-        }
-        cv_.notify_all();
-        memcpy(dst, src, std::min(per, bytes));
-        std::unique_lock<std::mutex> lk(mu_);
-        done_.wait(lk, [&] { return pending_ == 0; });
-    }
+    void copy(void* dst, const void* src, size_t bytes) { split(static_cast<char*>(dst), static_cast<const char*>(src), bytes); }
+
+    // Writes one byte per 4 KiB page of fresh memory, so the page faults
+    // (and the kernel's zeroing of the pages) are taken by several threads
+    // ahead of the copies into it.
+    void touch(void* dst, size_t bytes) { split(static_cast<char*>(dst), nullptr, bytes); }
 
     ~CopyThreads() {
         {
@@ -80,6 +64,38 @@ class CopyThreads {
     }
 
   private:
+    static void part_job(char* d, const char* s, size_t n) {
+        if (s) {
+            memcpy(d, s, n);
+        } else {
+            for (size_t off = 0; off < n; off += 4096) reinterpret_cast<volatile char*>(d)[off] = 0;
+        }
+    }
+
+    // Splits one job (a copy, or a touch when src is null) between the caller and the helpers.
+    void split(char* dst, const char* src, size_t bytes) {
+        if (workers_.empty() || bytes < (1u << 20)) {
+            part_job(dst, src, bytes);
+            return;
+        }
+        std::lock_guard<std::mutex> job(job_mu_);
+        const size_t parts = workers_.size() + 1;
+        const size_t per = ((bytes + parts - 1) / parts + 4095) & ~static_cast<size_t>(4095);
+        {
+            std::lock_guard<std::mutex> lk(mu_);
+            dst_ = dst;
+            src_ = src;
+            bytes_ = bytes;
+            per_ = per;
+            pending_ = workers_.size();
+            ++gen_;
+        }
+        cv_.notify_all();
+        part_job(dst, src, std::min(per, bytes));
+        std::unique_lock<std::mutex> lk(mu_);
+        done_.wait(lk, [&] { return pending_ == 0; });
+    }
+
     void run(size_t part) {
         uint64_t seen = 0;
         for (;;) {
@@ -97,7 +113,7 @@ class CopyThreads {
                 per = per_;
             }
             const size_t off = part * per;
-            if (off < b) memcpy(d + off, s + off, std::min(per, b - off));
+            if (off < b) part_job(d + off, s ? s + off : nullptr, std::min(per, b - off));
             std::lock_guard<std::mutex> lk(mu_);
             if (--pending_ == 0) done_.notify_one();
         }
@@ -182,6 +198,11 @@ class Stager {
         return cudaSuccess;
     }
 
+    // Faults in fresh pageable memory that downloads will fill (see touch).
+    void prefault(char* dst, size_t bytes) {
+        if (ready()) copier_.touch(dst, bytes);
+    }
+
     // Returns when the data is in `dst` (as a copy to pageable memory does).
     cudaError_t to_host(char* dst, const char* src, size_t bytes, cudaStream_t st) {
         const size_t pieces = (bytes + kSlotBytes - 1) / kSlotBytes;
@@ -230,6 +251,10 @@ cudaError_t copy_h2d(Stager* s, void* dst, const void* src, size_t bytes, cudaSt
     if (!s || bytes < kStageMinBytes || !staging_enabled() || host_pinned(src) || !s->ready())
         return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, st);
     return s->to_device(static_cast<char*>(dst), static_cast<const char*>(src), bytes, st);
+}
+
+void prefault_host(Stager* s, void* dst, size_t bytes) {
+    if (s && bytes >= kStageMinBytes && staging_enabled() && !host_pinned(dst)) s->prefault(static_cast<char*>(dst), bytes);
 }
 
 cudaError_t copy_d2h(Stager* s, void* dst, const void* src, size_t bytes, cudaStream_t st) {

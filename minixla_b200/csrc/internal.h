@@ -136,6 +136,9 @@ Stager* stager_create();
 void stager_destroy(Stager* s);
 cudaError_t copy_h2d(Stager* s, void* dst, const void* src, size_t bytes, cudaStream_t stream);
 cudaError_t copy_d2h(Stager* s, void* dst, const void* src, size_t bytes, cudaStream_t stream);
+// Faults in fresh pageable host memory with the stager's copy threads (one
+// write per page), ahead of downloads into it; nothing for pinned memory.
+void prefault_host(Stager* s, void* dst, size_t bytes);
 
 // Process-wide count of kernel launches issued by this library.
 void note_launch(unsigned n = 1);

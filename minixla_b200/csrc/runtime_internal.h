@@ -322,8 +322,10 @@ RowStreamPlan plan_row_stream(const std::vector<const Node*>& order, const std::
                               const std::vector<Info>& info);
 int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
                      const std::unordered_map<const Node*, int>& index, std::vector<Info>& info,
-                     const RowStreamPlan& plan, int chunks, float* host_dst);
-int stream_chunks();
+                     const RowStreamPlan& plan, int chunks, float* host_dst, bool fresh_dst = false);
+// Row chunks for a root of `root_bytes`: $MINIXLA_STREAM_CHUNKS, else 16 from
+// 128 MiB of result (finer pipelining of the copies), else 8.
+int stream_chunks(long long root_bytes);
 cudaEvent_t sync_event(GpuCtx* ctx, size_t k);  // the context's k-th reusable ordering event
 
 // exec_sharded.cu

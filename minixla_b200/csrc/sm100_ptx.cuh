@@ -226,10 +226,17 @@ __device__ __forceinline__ bool wait_flag_gpu(const int* flag, int want, uint64_
     return false;
 }
 
-// L2 cache policy that keeps lines resident ahead of others (evict_last).
+// L2 cache policies for st.global.L2::cache_hint: keep the lines ahead of
+// others (evict_last), or treat them like any other line (evict_normal).
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
     uint64_t pol;
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_normal() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
     return pol;
 }
 

@@ -119,12 +119,15 @@ def test_plan_batched(shape, want, monkeypatch):
 # (M, N, K) -> stream-K tiles on 74 CTA pairs (TF32): tiles that do not make a
 # whole last wave are shared out by k-blocks over every pair.
 STREAMK = [
-    ((4096, 4096, 4096), 128),    # 128 tiles: all of them (1.73 waves; 20 idle pair-tiles)
+    ((4096, 4096, 4096), 0),      # 128 tiles: fewer than two whole waves, all in step instead
     ((4096, 8192, 8192), 108),    # the 8-way split of 32768 x 8192 x 8192: 256 tiles = 3 x 74 + 34
+    ((6144, 8192, 8192), 88),     # 384 tiles = 5 x 74 + 14: 60 idle pair-tiles; the last 88 stream-K
     ((8192, 8192, 8192), 0),      # 512 tiles = 6 x 74 + 68: 6 idle pair-tiles, under 1 in 25
     ((32768, 8192, 8192), 0),     # 2048 tiles = 27 x 74 + 50: 24 idle, under 1 in 25
     ((2048, 2048, 2048), 0),      # 64 tiles of 256 x 256: fewer than the pairs
     ((9472, 8192, 8192), 0),      # 592 tiles = 8 x 74 exactly
+    ((5120, 4096, 2048), 86),     # 160 tiles = 2 x 74 + 12
+    ((5120, 4096, 1024), 0),      # ... with a short k-loop (32 blocks)
 ]
 
 

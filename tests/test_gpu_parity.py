@@ -898,10 +898,10 @@ def test_allocation_failure_injection(fail_at):
 
 
 # (M, N, K) whose TF32 CTA-pair tiles do not fill a whole number of waves on
-# 74 pairs: 80 wide tiles (all stream-K), 96 tiles of 256 x 256 with a ragged
-# M, N and K, 128 wide tiles (4096^3), and the 8-way split of config 5
-# (256 wide tiles: 148 run whole, 108 stream-K).
-STREAMK_SHAPES = [(2560, 4096, 1024), (2000, 3001, 997), (4096, 4096, 4096), (4096, 8192, 8192)]
+# 74 pairs: 160 wide tiles (86 stream-K), 156 wide tiles with a ragged M, N
+# and K (82 stream-K), and the 8-way split of config 5 (256 wide tiles: 148
+# run whole, 108 stream-K).
+STREAMK_SHAPES = [(5120, 4096, 2048), (3300, 6001, 2049), (4096, 8192, 8192)]
 
 
 @pytest.mark.parametrize("mnk", STREAMK_SHAPES, ids=[f"{m}x{n}x{k}" for m, n, k in STREAMK_SHAPES])
