@@ -7,6 +7,8 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <string>
+#include <thread>
 #include <unordered_map>
 #include <unordered_set>
 #include <vector>
@@ -108,6 +110,34 @@ ShardPlan plan_shards(const std::vector<const Node*>& order, const std::unordere
     return plan;
 }
 
+// Runs fn(d) for every device d = 0 .. P-1 at the same time, on P host
+// threads (d = 0 on the caller's), each with its device current; returns the
+// first failure's code and carries its message over to the calling thread.
+// Used for the staged host copies, whose cost is host memcpy into each
+// device's pinned ring: one thread per device runs those side by side.
+template <typename Fn>
+static int for_each_device(int P, const std::vector<GpuCtx*>& ctxs, Fn fn) {
+    std::vector<int> rc(P, MXB_OK);
+    std::vector<std::string> msg(P);
+    auto run = [&](int d) {
+        DeviceScope scope(ctxs[d]->device);
+        rc[d] = fn(d);
+        if (rc[d] != MXB_OK) msg[d] = mxb_last_error();
+    };
+    std::vector<std::thread> threads;
+    threads.reserve(P > 1 ? P - 1 : 0);
+    for (int d = 1; d < P; ++d) threads.emplace_back(run, d);
+    run(0);
+    for (std::thread& t : threads) t.join();
+    for (int d = 0; d < P; ++d) {
+        if (rc[d] != MXB_OK) {
+            if (d > 0) set_error("%s", msg[d].c_str());
+            return rc[d];
+        }
+    }
+    return MXB_OK;
+}
+
 static int nccl_check(ncclResult_t r, const char* what) {
     if (r == ncclSuccess) return MXB_OK;
     set_error("%s: %s", what, nccl().error_string ? nccl().error_string(r) : "NCCL error");
@@ -147,23 +177,13 @@ int execute_sharded(GpuCtx* ctx0, const std::vector<const Node*>& order,
             if (!ptr[d][i]) rc = MXB_E_NOMEM;
         }
     }
-    // Leaves: row shards straight from the host; whole leaves once to device 0, then peer copies.
+    // Leaves: whole leaves once to device 0, then peer copies (this thread);
+    // then every device's row shards straight from the host, one host thread
+    // per device.
     size_t ev_k = 0;
     for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
-        if (order[i]->op != OP_INPUT || borrowed[i]) continue;
+        if (order[i]->op != OP_INPUT || borrowed[i] || !full[i]) continue;
         const float* host = order[i]->output->data;
-        if (!full[i]) {
-            for (int d = 0; d < P && rc == MXB_OK; ++d) {
-                if (!ptr[d][i]) continue;
-                DeviceScope scope(ctxs[d]->device);
-                const long long c = cols_of(i);
-                if (!cuda_ok(copy_h2d(ctxs[d]->stager, ptr[d][i], host + r0[d] * c,
-                                      static_cast<size_t>((r1[d] - r0[d]) * c) * 4, ctxs[d]->stream),
-                             "shard upload"))
-                    rc = MXB_E_CUDA;
-            }
-            continue;
-        }
         const size_t bytes = static_cast<size_t>(info[i].size) * 4;
         {
             DeviceScope scope(ctx0->device);
@@ -184,6 +204,19 @@ int execute_sharded(GpuCtx* ctx0, const std::vector<const Node*>& order,
                          "peer replication"))
                 rc = MXB_E_CUDA;
         }
+    }
+    if (rc == MXB_OK) {
+        rc = for_each_device(P, ctxs, [&](int d) {
+            for (size_t i = 0; i < n; ++i) {
+                if (order[i]->op != OP_INPUT || borrowed[i] || full[i] || !ptr[d][i]) continue;
+                const long long c = cols_of(i);
+                if (!cuda_ok(copy_h2d(ctxs[d]->stager, ptr[d][i], order[i]->output->data + r0[d] * c,
+                                      static_cast<size_t>((r1[d] - r0[d]) * c) * 4, ctxs[d]->stream),
+                             "shard upload"))
+                    return MXB_E_CUDA;
+            }
+            return MXB_OK;
+        });
     }
     // Computed nodes, each device on its own rows.
     for (size_t i = 0; i < n && rc == MXB_OK; ++i) {
@@ -263,17 +296,19 @@ int execute_sharded(GpuCtx* ctx0, const std::vector<const Node*>& order,
         const int end = nccl_check(api.group_end(), "ncclGroupEnd");
         if (rc == MXB_OK) rc = end;
     }
-    // Result rows from every device into the host tensor.
+    // Result rows from every device into the host tensor, one host thread per device.
     const size_t root_i = n - 1;
     const long long out_cols = cols_of(root_i);
-    for (int d = 0; d < P && rc == MXB_OK; ++d) {
-        const long long m = r1[d] - r0[d];
-        if (m <= 0) continue;
-        DeviceScope scope(ctxs[d]->device);
-        if (!cuda_ok(copy_d2h(ctxs[d]->stager, host_dst + r0[d] * out_cols, rows(d, root_i),
-                              static_cast<size_t>(m * out_cols) * 4, ctxs[d]->stream),
-                     "shard download"))
-            rc = MXB_E_CUDA;
+    if (rc == MXB_OK) {
+        rc = for_each_device(P, ctxs, [&](int d) {
+            const long long m = r1[d] - r0[d];
+            if (m <= 0) return MXB_OK;
+            return cuda_ok(copy_d2h(ctxs[d]->stager, host_dst + r0[d] * out_cols, rows(d, root_i),
+                                    static_cast<size_t>(m * out_cols) * 4, ctxs[d]->stream),
+                           "shard download")
+                       ? MXB_OK
+                       : MXB_E_CUDA;
+        });
     }
     for (int d = 0; d < P; ++d) {
         DeviceScope scope(ctxs[d]->device);

@@ -64,13 +64,90 @@ struct Cfg {
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-// KSPLIT: tile t is a K slice of output tile t / p.splits; the epilogue warps
-// write the slice raw to workspace and ksplit_reduce_kernel, launched next,
-// sums the slices in slice order and applies the epilogue.
+// KSPLIT: tile t is a K slice of output tile t / p.splits.  With
+// p.ks_cluster (one tile per cluster of p.splits CTAs, one slice per CTA) the
+// epilogue warps leave their slice raw in their own shared memory, the
+// cluster synchronises, and each CTA sums its share of the tile's rows over
+// the slices of every CTA of the cluster through distributed shared memory,
+// in slice order, then applies the epilogue (ksplit_cluster_reduce).  Without
+// it, the slices go raw to workspace and ksplit_reduce_kernel, launched next,
+// sums them the same way.
 //
 // BATCHED: p.batch products of the same shape in one launch; A, B (and their
 // low parts) are 3-D tensor maps whose third coordinate is the product, so a
 // partial tile or k-block never reads the next product's rows.
+// The raw slice of one K-split CTA in its shared memory: 128 rows x 128
+// columns as float4s, row r's float4 f at r * 32 + (f ^ (r & 31)), so that a
+// quarter-warp writing one float4 of eight rows, or reading eight float4s of
+// one row, touches eight different 16-byte bank groups.
+__device__ __forceinline__ uint32_t ks_slot(int row, int f) {
+    return static_cast<uint32_t>(row * 32 + (f ^ (row & 31))) * 16u;
+}
+
+// Thread `row` (0..127) stores 32 raw accumulator columns, chunk c, into the slice buffer.
+__device__ __forceinline__ void ks_dump_chunk(uint8_t* buf, int row, int c, const uint32_t (&r)[32]) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4*>(buf + ks_slot(row, 8 * c + j)) =
+            make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                        __uint_as_float(r[4 * j + 3]));
+}
+
+// After the cluster barrier: CTA `rank` of the tile's cluster sums rows
+// [rank * R, (rank + 1) * R) of the slices of all `splits` CTAs, in slice
+// order (slice 0, + slice 1, ...: the same additions as ksplit_reduce_kernel),
+// applies the node's epilogue and stores.  Warp w of the four epilogue warps
+// takes rows w, w + 4, ...; lane l the four columns 4l .. 4l + 3.
+__device__ __forceinline__ void ksplit_cluster_reduce(const FusedParams& p, const uint8_t* buf, int mb, int nb,
+                                                      int ep_warp, int lane) {
+    const int splits = p.splits;
+    const uint32_t rank = cluster_ctarank();
+    const int per = (128 + splits - 1) / splits;
+    const int r_lo = static_cast<int>(rank) * per, r_hi = min(128, r_lo + per);
+    const int col = nb * 128 + 4 * lane;
+    if (col >= p.N) return;
+    const uint32_t base = smem_addr(buf);
+    uint32_t remote[8];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) remote[s] = s < splits ? mapa_shared(base, static_cast<uint32_t>(s)) : 0u;
+    // Four rows at a time (rows r, r + 4, r + 8, r + 12 of this warp), every
+    // load of a group issued before its stores: the 64 outputs a thread owns
+    // then take four rounds of memory latency instead of sixteen.
+    constexpr int kR = 4;
+    for (int r0 = r_lo + ep_warp; r0 < r_hi; r0 += 4 * kR) {
+        float v[kR][4];
+        int row[kR];
+        bool ok[kR];
+#pragma unroll
+        for (int u = 0; u < kR; ++u) {
+            const int r = r0 + 4 * u;
+            row[u] = mb * 128 + r;
+            ok[u] = r < r_hi && row[u] < p.M;
+            const uint32_t off = ks_slot(ok[u] ? r : r_lo, lane);
+            float4 x = ld_shared_cluster_v4(remote[0] + off);
+            v[u][0] = x.x;
+            v[u][1] = x.y;
+            v[u][2] = x.z;
+            v[u][3] = x.w;
+        }
+        for (int s = 1; s < splits; ++s) {
+#pragma unroll
+            for (int u = 0; u < kR; ++u) {
+                const uint32_t off = ks_slot(ok[u] ? r0 + 4 * u : r_lo, lane);
+                const float4 x = ld_shared_cluster_v4(remote[s] + off);
+                v[u][0] += x.x;
+                v[u][1] += x.y;
+                v[u][2] += x.z;
+                v[u][3] += x.w;
+            }
+        }
+        apply_epilogue_rows<kR>(v, row, ok, col, p);
+#pragma unroll
+        for (int u = 0; u < kR; ++u)
+            if (ok[u]) store_row_chunk<4>(v[u], row[u], col, p);
+    }
+}
+
 template <int BN, int STAGES, bool SPLIT3, bool SEG, bool KSPLIT = false, bool BATCHED = false>
 __global__ void __launch_bounds__(kThreads, 1)
     fused_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -295,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool failed = false;
             if (!KSPLIT && row_ok) {
                 // Short k-loops: fetch C while the MMAs run; long ones: just before the drain.
-                if (p.num_kb <= kShortKb) prefetch_full_operands(row, col0, min(BN, p.N - col0), p, b);
+                if (p.prefetch_early) prefetch_full_operands(row, col0, min(BN, p.N - col0), p, b);
             }
             if (KSPLIT && row_ok) {
                 // Fetch C into L2 for the reduce kernel while the MMAs run.
@@ -310,8 +387,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * BN);
-                float* slice = p.ks_ws + static_cast<long long>(t % p.splits) * p.ks_stride +
-                               static_cast<long long>(row) * p.ks_ld;
+                float* slice = p.ks_cluster ? nullptr
+                                            : p.ks_ws + static_cast<long long>(t % p.splits) * p.ks_stride +
+                                                  static_cast<long long>(row) * p.ks_ld;
                 for (int c = 0; c < chunks; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + 32 * c, r);
@@ -320,7 +398,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tc_fence_before();
                         mbar_arrive(tempty_bar(acc));
                     }
-                    if (row_ok) store_partial(r, slice + col0 + 32 * c, col0 + 32 * c, p.N);
+                    if (p.ks_cluster)
+                        ks_dump_chunk(smem, row_in_tile, c, r);
+                    else if (row_ok)
+                        store_partial(r, slice + col0 + 32 * c, col0 + 32 * c, p.N);
                 }
                 acc ^= 1;
                 if (acc == 0) acc_phase ^= 1u;
@@ -366,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (last) {
                         tmem_st_wait();
                         float* slice = nullptr;
-                        if (KSPLIT)
+                        if (KSPLIT && !p.ks_cluster)
                             slice = p.ks_ws + static_cast<long long>(t % p.splits) * p.ks_stride +
                                     static_cast<long long>(row) * p.ks_ld;
                         for (int c = 0; c < chunks; ++c) {
@@ -375,7 +456,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tmem_ld_wait();
                             const int col = col0 + 32 * c;
                             if (KSPLIT) {
-                                if (row_ok) store_partial(r, slice + col, col, p.N);
+                                if (p.ks_cluster)
+                                    ks_dump_chunk(smem, row_in_tile, c, r);
+                                else if (row_ok)
+                                    store_partial(r, slice + col, col, p.N);
                             } else {
                                 float v[32];
 #pragma unroll
@@ -399,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                if (row_ok && p.num_kb > kShortKb) prefetch_full_operands(row, col0, min(BN, p.N - col0), p, b);
+                if (row_ok && !p.prefetch_early) prefetch_full_operands(row, col0, min(BN, p.N - col0), p, b);
                 const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * BN);
                 for (int c = 0; c < chunks; ++c) {
                     uint32_t r[32];
@@ -423,6 +507,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
 
+    if (KSPLIT && p.ks_cluster) {
+        // Every CTA of the tile's cluster reaches both barriers on every path
+        // (a timed-out wait above only skips work), so neither can hang.
+        __syncwarp();
+        cluster_sync();  // each slice is in its CTA's shared memory
+        if (warp >= 2) {
+            int mb, nb;
+            tile_coords(static_cast<int>(blockIdx.x) / p.splits, p, mb, nb);
+            ksplit_cluster_reduce(p, smem, mb, nb, warp - 2, lane);
+        }
+        __syncwarp();
+        cluster_sync();  // no CTA leaves while the others still read its slice
+    }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -471,6 +568,13 @@ bool batch_wide_tiles() {
 bool ksplit_pdl_enabled() {
     const char* v = getenv("MINIXLA_KSPLIT_PDL");
     return !(v && v[0] == '0');
+}
+
+// MINIXLA_KSPLIT_REDUCE=kernel: slices through workspace and the reduce
+// kernel instead of summed inside the GEMM's clusters.
+bool ksplit_cluster_enabled() {
+    const char* v = getenv("MINIXLA_KSPLIT_REDUCE");
+    return !(v && !strcmp(v, "kernel"));
 }
 
 template <int BN, int STAGES, bool SPLIT3, bool SEG, bool KSPLIT = false, bool BATCHED = false>
@@ -532,6 +636,7 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.num_kb = (g.K + kBK - 1) / kBK;
     p.group_m = 16;
     p.seg_kb = SEG ? kSegKb : p.num_kb;
+    p.prefetch_early = prefetch_early(g.M, g.N, g.K, g.batch > 1 ? g.batch : 1);
     p.row_base = g.row_base;
     p.timeout_ns = g.timeout_ns;
     p.err = g.err;
@@ -541,11 +646,13 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.kb_per_split = p.num_kb;
     if (KSPLIT) {
         static_assert(!KSPLIT || (BN == kKsplitTileCols && kBM == kKsplitTileRows), "K-split tile");
-        if (g.k_splits < 2 || !g.ks_ws) return cudaErrorInvalidValue;
+        if (g.k_splits < 2) return cudaErrorInvalidValue;
         // Whole k-blocks per slice and no empty slice: splits <= k_splits.
         p.kb_per_split = (p.num_kb + g.k_splits - 1) / g.k_splits;
         p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
         p.num_tiles *= p.splits;
+        p.ks_cluster = fused_gemm_ksplit_in_cluster(g) ? 1 : 0;
+        if (!p.ks_cluster && !g.ks_ws) return cudaErrorInvalidValue;
         p.ks_ws = g.ks_ws;
         p.ks_ld = (g.N + 3) / 4 * 4;
         p.ks_stride = static_cast<long long>(g.M) * p.ks_ld;
@@ -564,6 +671,26 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
     }
 
     const int grid = p.num_tiles < g.num_sms ? p.num_tiles : g.num_sms;
+    if (KSPLIT && p.ks_cluster) {
+        // One cluster of p.splits CTAs per tile, one slice per CTA; the slices
+        // are summed inside the kernel.
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(p.num_tiles));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = C::kSmemBytes;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = static_cast<unsigned>(p.splits);
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, kernel, mA, mB, mA2, mB2, p);
+        if (e != cudaSuccess) return e;
+        note_launch();
+        return cudaGetLastError();
+    }
     kernel<<<grid, kThreads, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p);
     note_launch();
     if (KSPLIT) {
@@ -682,6 +809,24 @@ int fused_gemm_streamk_tiles(const GemmLaunch& g) {
     if (tiles >= (1ll << 31)) return 0;
     const StreamKSplit sk = streamk_split(static_cast<int>(tiles), (g.K + kBK - 1) / kBK, g.num_sms / 2);
     return sk.q > 0 ? static_cast<int>(tiles) - sk.dp_tiles : 0;
+}
+
+// Whether a K-split launch of g sums its slices inside the GEMM (one cluster
+// of `splits` CTAs per tile; every tile's cluster resident at once needs
+// tiles x splits <= SMs, which fused_gemm_k_splits keeps unless a split count
+// is forced).  Otherwise the slices need workspace and the reduce kernel.
+// Clusters of up to four: eight-CTA clusters of these ~200 KB CTAs do not all
+// fit at once (512 x 512 x 8192, 16 clusters of 8: 40.9 us against 25.5 us
+// with the reduce kernel), while with two slices the in-cluster sum wins
+// ((8191, 127, 3000): 34.8 vs 39.9 us; (640, 384, 4100), four: 20.4 vs 21.4 us).
+bool fused_gemm_ksplit_in_cluster(const GemmLaunch& g) {
+    if (g.k_splits < 2 || !ksplit_cluster_enabled()) return false;
+    const int num_kb = (g.K + kBK - 1) / kBK;
+    const int per = (num_kb + g.k_splits - 1) / g.k_splits;
+    const int splits = (num_kb + per - 1) / per;
+    const long long tiles = static_cast<long long>((g.M + kKsplitTileRows - 1) / kKsplitTileRows) *
+                            ((g.N + kKsplitTileCols - 1) / kKsplitTileCols);
+    return splits >= 2 && splits <= 4 && tiles * splits <= g.num_sms;
 }
 
 size_t fused_gemm_streamk_bytes(const GemmLaunch& g) {

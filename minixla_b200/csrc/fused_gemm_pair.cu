@@ -46,7 +46,7 @@ namespace {
 // rest as the raw fp32 accumulator, through global memory, so the MMA chain
 // of every output element is unchanged.
 
-template <int STAGES, int BN, bool DUAL, int EPI = 4>
+template <int STAGES, int BN, bool DUAL, int EPI = 4, bool PUSH = false>
 struct PairCfg {
     static_assert(EPI == 4 || EPI == 8, "epilogue warps: one or two per TMEM lane quadrant");
     static constexpr int kThreadsPerCta = 64 + 32 * EPI;         // TMA warp, MMA warp, epilogue warps
@@ -63,13 +63,70 @@ struct PairCfg {
     static constexpr int kTmemCols = kBufs * kAccCols;
     static constexpr int kBarOffset = STAGES * kStageBytes;
     static constexpr int kNumBars = 2 * STAGES + 6;
-    static constexpr int kSmemBytes = 1024 + kBarOffset + kNumBars * 8 + 16;
+    // PUSH: two 8-row x 128-column staging buffers per epilogue warp for the
+    // TMA stores of the row all-gather, 1 KiB aligned after the barriers.
+    static constexpr int kStagingOffset = (kBarOffset + kNumBars * 8 + 16 + 1023) / 1024 * 1024;
+    static constexpr int kStagingPerWarp = 2 * kPushBoxRows * kPushBoxCols * 4;
+    static constexpr int kSmemBytes =
+        1024 + (PUSH ? kStagingOffset + EPI * kStagingPerWarp : kBarOffset + kNumBars * 8 + 16);
     static_assert(BN == 128 || BN == 256 || BN == 512, "pair tile width");
     static_assert(!(DUAL && BN == 512), "two products use 128- or 256-column tiles");
     static_assert(kStageBytes % 1024 == 0, "stages must keep 1 KiB swizzle alignment");
     static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation");
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
+
+// The row all-gather of one warp's 32 finished rows, columns c0 .. c1, by
+// TMA tile stores: the warp reads its rows back from L2 (one 512-byte row
+// segment per instruction) into one of its two staging buffers (8 rows x 128
+// columns) and lane 0 stores the buffer to every peer's copy with one TMA
+// instruction per peer, starting at a different peer per warp.  The copy
+// engine then drives the NVLink writes, so the warp's cost is the read-back
+// and one store per peer per 4 KiB; a buffer is refilled once the stores
+// issued from it two rounds earlier have read it.
+__device__ __forceinline__ void push_rows_tma(const PeerMaps& pm, const FusedParams& p, float* staging, int row0,
+                                              int c0, int c1, int& buf) {
+    __syncwarp();
+    const int lane = threadIdx.x & 31;
+    const int rows = min(32, p.M - row0);
+    if (rows <= 0 || c0 >= c1) return;
+    const int q0 = (row0 >> 5) % p.n_peers;
+    for (int rb = 0; rb < rows; rb += kPushBoxRows) {
+        for (int cb = c0; cb < c1; cb += kPushBoxCols) {
+            float* sb = staging + buf * (kPushBoxRows * kPushBoxCols);
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+            const int col = cb + 4 * lane;
+#pragma unroll
+            for (int r = 0; r < kPushBoxRows; ++r) {
+                const int row = row0 + rb + r;
+                float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (row < p.M && col < c1) {
+                    const float* src = p.out + static_cast<long long>(row) * p.ldo + col;
+                    if (col + 4 <= c1) {
+                        v = *reinterpret_cast<const float4*>(src);
+                    } else {
+                        v.x = src[0];
+                        if (col + 1 < c1) v.y = src[1];
+                        if (col + 2 < c1) v.z = src[2];
+                    }
+                }
+                *reinterpret_cast<float4*>(sb + r * kPushBoxCols + 4 * lane) = v;
+            }
+            fence_proxy_async_shared();
+            __syncwarp();
+            if (lane == 0) {
+                int q = q0;
+                for (int j = 0; j < p.n_peers; ++j) {
+                    tma_store_2d(&pm.m[q], smem_addr(sb), cb, row0 + rb);
+                    q = q + 1 == p.n_peers ? 0 : q + 1;
+                }
+                bulk_commit_group();
+            }
+            buf ^= 1;
+        }
+    }
+}
 
 // PUSH: the epilogue also writes each tile's rows into the peers' copies
 // (FusedParams::peer_out), a separate instance so the other launches keep
@@ -80,8 +137,8 @@ template <int STAGES, int BN, bool DUAL, int EPI, bool PUSH, bool BATCHED = fals
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, DUAL, EPI>::kThreadsPerCta, 1)
     fused_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
-                           const __grid_constant__ FusedParams p) {
-    using C = PairCfg<STAGES, BN, DUAL, EPI>;
+                           const __grid_constant__ FusedParams p, const __grid_constant__ PeerMaps pm) {
+    using C = PairCfg<STAGES, BN, DUAL, EPI, PUSH>;
     static_assert(!(BATCHED && (DUAL || PUSH)), "a batched launch has one product and no peer rows");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -277,6 +334,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
         // Stream-K hand-off: this warp's rows of the tile (lane quadrant,
         // column range) in the head pair's slot and the flag it sets.
         const int sk_warp = (static_cast<int>(rank) * EPI + (warp - 2));
+        float* push_staging = reinterpret_cast<float*>(smem + C::kStagingOffset + (warp - 2) * C::kStagingPerWarp);
+        int push_buf = 0;
         PairWork wk;
         for (int idx = 0; pair_work(p, pair, num_pairs, idx, wk); ++idx) {
             const int t = wk.t;
@@ -337,7 +396,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             }
             // C rows into L2: during the k-loop when it is short, else once the accumulator is ready.
             const bool fetch = !head && row_ok && chunks > c_first;
-            if (fetch && p.num_kb <= kShortKb)
+            if (fetch && p.prefetch_early)
                 prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p, b);
             const bool stop = __any_sync(0xffffffffu, *abort_flag != 0);
             const bool got = !stop && mbar_wait_cluster(tfull_bar(acc), acc_phase, p.timeout_ns);
@@ -346,7 +405,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                 break;
             }
             tc_fence_after();
-            if (fetch && p.num_kb > kShortKb)
+            if (fetch && !p.prefetch_early)
                 prefetch_full_operands(row, col0 + 32 * c_first, 32 * (chunks - c_first), p, b);
             if (chunks <= c_first) {
                 // No columns of this tile for this warp: release the accumulator at once.
@@ -414,13 +473,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             if (PUSH) {
                 // The accumulator is already released: these copies overlap the next tile's k-loop.
                 const int c_end = col0 + 32 * chunks < p.N ? col0 + 32 * chunks : p.N;
-                push_rows(p, mb * 256 + row_in_tile - lane, col0 + 32 * c_first, c_end);
+                if (p.push_tma)
+                    push_rows_tma(pm, p, push_staging, mb * 256 + row_in_tile - lane, col0 + 32 * c_first, c_end,
+                                  push_buf);
+                else
+                    push_rows<8>(p, mb * 256 + row_in_tile - lane, col0 + 32 * c_first, c_end);
             }
             if (C::kBufs == 2) acc ^= 1;
             if (acc == 0) acc_phase ^= 1u;
         }
         // Peer stores performed before the kernel counts as finished.
-        if (PUSH) __threadfence_system();
+        if (PUSH) {
+            if (lane == 0) bulk_wait_group<0>();
+            __syncwarp();
+            __threadfence_system();
+        }
     }
 
     __syncwarp();
@@ -434,9 +501,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
 
 // ------------------------------------------------------------------ host side
 
+// MINIXLA_GATHER_TMA=0: the row all-gather stores through the epilogue
+// warps' own global stores instead of TMA tile stores.
+bool gather_tma_enabled() {
+    const char* v = getenv("MINIXLA_GATHER_TMA");
+    return !(v && v[0] == '0');
+}
+
 template <int STAGES, int BN, bool DUAL, int EPI = 4, bool PUSH = false, bool BATCHED = false>
 cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
-    using C = PairCfg<STAGES, BN, DUAL, EPI>;
+    using C = PairCfg<STAGES, BN, DUAL, EPI, PUSH>;
     auto kernel = fused_gemm_pair_kernel<STAGES, BN, DUAL, EPI, PUSH, BATCHED>;
     if (BATCHED != (g.batch > 1)) return cudaErrorInvalidValue;
     static std::mutex mu;
@@ -513,6 +587,7 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
     p.num_kb = (g.K + kBK - 1) / kBK;
     p.group_m = 8;
     p.seg_kb = p.num_kb;
+    p.prefetch_early = prefetch_early(g.M, g.N, g.K, g.batch > 1 ? g.batch : 1);
     p.row_base = g.row_base;
     p.timeout_ns = g.timeout_ns;
     p.err = g.err;
@@ -528,6 +603,15 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
         }
         p.n_peers = g.n_peers;
         p.push_vec = vec ? 1 : 0;
+    }
+    PeerMaps pm;
+    memset(&pm, 0, sizeof(pm));
+    if (PUSH && p.push_vec && gather_tma_enabled() && g.M >= kPushBoxRows && g.N >= kPushBoxCols) {
+        // This launch's rows in each peer's copy: the same [M, N] block at peer_out[i], pitch ldo.
+        bool ok = true;
+        for (int i = 0; i < g.n_peers && ok; ++i)
+            ok = make_store_map(&pm.m[i], g.peer_out[i], g.M, g.N, g.ldo, kPushBoxCols, kPushBoxRows);
+        p.push_tma = ok ? 1 : 0;
     }
 
     p.batch = 1;
@@ -557,7 +641,7 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
             if (e2 != cudaSuccess) return e2;
         }
     }
-    kernel<<<2 * pairs, C::kThreadsPerCta, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p);
+    kernel<<<2 * pairs, C::kThreadsPerCta, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p, pm);
     note_launch();
     return cudaGetLastError();
 }

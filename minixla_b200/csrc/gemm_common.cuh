@@ -33,8 +33,16 @@ constexpr int kBoxBytes = 32 * 32 * 4;  // one B box: 32 k-rows x 128 bytes
 constexpr int kSegKb = 8;           // k-blocks (of 32) per accumulation segment in 3xTF32 mode
 // With at most this many k-blocks the main loop is short (K <= 1024), so the
 // epilogue prefetches its rows of the ADD operands before the accumulator is
-// ready; longer loops prefetch once it is (earlier lines would be evicted).
+// ready; longer loops prefetch once it is (earlier lines would be evicted) --
+// unless the whole problem fits in a part of L2 (kEarlyPrefetchBytes of A, B,
+// C and the output), where nothing evicts them.
 constexpr int kShortKb = 32;
+constexpr long long kEarlyPrefetchBytes = 64ll << 20;
+
+inline int prefetch_early(long long M, long long N, long long K, long long batch = 1) {
+    const long long bytes = 4 * batch * (M * K + K * N + 2 * M * N);
+    return (K + 31) / 32 <= kShortKb || bytes <= kEarlyPrefetchBytes ? 1 : 0;
+}
 
 struct FusedParams {
     float* out;
@@ -44,6 +52,7 @@ struct FusedParams {
     int tiles_m, tiles_n, num_tiles, num_kb;
     int group_m;
     int seg_kb;                     // k-blocks per accumulation segment (num_kb: one segment)
+    int prefetch_early;             // ADD operands into L2 during the k-loop (prefetch_early())
     long long row_base;             // global index of row 0 of this launch (modulo-rule operands)
     unsigned long long timeout_ns;
     int* err;
@@ -54,6 +63,7 @@ struct FusedParams {
     float* peer_out[kMaxPeers];
     int n_peers;
     int push_vec;                   // 16-byte aligned bases and ldo % 4 == 0: float4 copies
+    int push_tma;                   // push_vec and PeerMaps valid: tile stores through TMA
     // K split (single-CTA TF32 kernel, KSPLIT instances): tile t is output
     // tile t / splits, k-blocks [s * kb_per_split, +kb_per_split) with
     // s = t % splits.  Slice s of the product goes raw to ks_ws + s * ks_stride
@@ -62,6 +72,10 @@ struct FusedParams {
     int kb_per_split;
     float* ks_ws;
     long long ks_stride, ks_ld;
+    // K split summed inside the GEMM: the `splits` CTAs of a tile form one
+    // cluster, leave their slices in shared memory and add them up through
+    // distributed shared memory (no workspace, no second kernel).
+    int ks_cluster;
     // Batched launch (single-CTA BATCHED instances): tile t is tile
     // t % tiles_per_batch of product b = t / tiles_per_batch; out and each
     // FULL operand step s advance by out_bstride / ep_bstride[s] elements per
@@ -129,6 +143,14 @@ inline StreamKSplit streamk_split(int tiles, int num_kb, int pairs) {
     s.extra = static_cast<int>(iters % pairs);
     return s;
 }
+
+// Tensor maps of this launch's rows in every peer's copy of the output
+// (FLOAT32, no rounding, no swizzle; box 8 rows x 128 columns), for the TMA
+// stores of the row all-gather (FusedParams::push_tma).
+constexpr int kPushBoxRows = 8, kPushBoxCols = 128;
+struct PeerMaps {
+    CUtensorMap m[kMaxPeers];
+};
 
 // One unit of a CTA pair's work: k-blocks [kb0, kb1) of tile t.
 enum : int { kWorkFull = 0, kWorkHead = 1, kWorkTail = 2 };
@@ -338,6 +360,78 @@ __device__ __forceinline__ void apply_epilogue(float (&v)[W], int row, int col, 
     }
 }
 
+// The same steps for four columns col .. col + 3 of R rows at once
+// (v[u] is row row[u]; rows with ok[u] false are left alone), step by step
+// across the rows, so the loads of one step for all R rows are in flight
+// together.  Bits as apply_epilogue<4> row by row.
+template <int R>
+__device__ __forceinline__ void apply_epilogue_rows(float (&v)[R][4], const int (&row)[R], const bool (&ok)[R],
+                                                    int col, const FusedParams& p) {
+    const bool full_cols = col + 4 <= p.N;
+    for (int s = 0; s < p.n_steps; ++s) {
+        const int kind = p.steps[s].kind;
+        const float* ptr = p.steps[s].ptr;
+        if (kind == MXB_EP_RELU) {
+#pragma unroll
+            for (int u = 0; u < R; ++u)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[u][i] = v[u][i] > 0.0f ? v[u][i] : 0.0f;
+        } else if (kind == MXB_EP_SCALE) {
+            const float sc = p.steps[s].scale;
+#pragma unroll
+            for (int u = 0; u < R; ++u)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[u][i] = v[u][i] * sc;
+        } else if (kind == MXB_EP_ADD_FULL) {
+            const long long ld = p.steps[s].ld_or_size;
+            float add[R][4];
+#pragma unroll
+            for (int u = 0; u < R; ++u) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) add[u][i] = 0.0f;
+                if (!ok[u]) continue;
+                const float* src = ptr + static_cast<long long>(row[u]) * ld + col;
+                if (full_cols && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+                    const float4 c = __ldcs(reinterpret_cast<const float4*>(src));
+                    add[u][0] = c.x;
+                    add[u][1] = c.y;
+                    add[u][2] = c.z;
+                    add[u][3] = c.w;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        if (col + i < p.N) add[u][i] = __ldcs(src + i);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < R; ++u)
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (ok[u] && col + i < p.N) v[u][i] += add[u][i];
+        } else if (kind == MXB_EP_ADD_ROW) {
+            float add[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) add[i] = col + i < p.N ? __ldg(ptr + col + i) : 0.0f;
+#pragma unroll
+            for (int u = 0; u < R; ++u)
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (col + i < p.N) v[u][i] += add[i];
+        } else if (kind == MXB_EP_ADD_MOD) {
+            const unsigned long long size = static_cast<unsigned long long>(p.steps[s].ld_or_size);
+#pragma unroll
+            for (int u = 0; u < R; ++u) {
+                if (!ok[u]) continue;
+                const unsigned long long base =
+                    static_cast<unsigned long long>(row[u] + p.row_base) * static_cast<unsigned long long>(p.N) + col;
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (col + i < p.N) v[u][i] += __ldg(ptr + (base + i) % size);
+            }
+        }
+    }
+}
+
 template <int W = 32>
 __device__ __forceinline__ void store_row_chunk(const float (&v)[W], int row, int col,
                                                 const FusedParams& p, long long off = 0) {
@@ -516,6 +610,22 @@ bool make_map(CUtensorMap* map, const float* base, long long rows, long long col
     const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, 2, const_cast<float*>(base), dims,
                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// Row-major [rows, cols] fp32 destination of TMA tile stores (FLOAT32, no
+// swizzle), row pitch `ld` elements; box [box_rows][box_cols].
+bool make_store_map(CUtensorMap* map, const float* base, long long rows, long long cols, long long ld, int box_cols,
+                    int box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 

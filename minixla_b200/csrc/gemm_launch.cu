@@ -150,7 +150,7 @@ int launch_gemm(GpuCtx* ctx, const float* A, long long lda, const float* B, long
     float* ws[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
     int rc = MXB_OK;
     g.k_splits = fused_gemm_k_splits(g);
-    if (g.k_splits > 1) {
+    if (g.k_splits > 1 && !fused_gemm_ksplit_in_cluster(g)) {
         // Raw partial sums, one M x round4(N) slice per K slice.
         const size_t slice = static_cast<size_t>(M) * ((N + 3) / 4 * 4);
         ws[3] = static_cast<float*>(ctx->pool->alloc(g.k_splits * slice * sizeof(float), stream));

@@ -118,6 +118,8 @@ GemmPlan plan_fused_gemm(const GemmLaunch& g, int k_splits);
 // How many ways launch_fused_gemm(g) splits K (1: none); the caller supplies
 // the workspace a split needs (GemmLaunch::ks_ws).
 int fused_gemm_k_splits(const GemmLaunch& g);
+// Whether that split sums its slices inside the GEMM's clusters (no workspace).
+bool fused_gemm_ksplit_in_cluster(const GemmLaunch& g);
 constexpr int kKsplitTileRows = 128, kKsplitTileCols = 128;
 cudaError_t launch_split_tf32(const float* x, long long rows, long long cols, long long ld_in,
                               float* small, long long ld_out, int num_sms, cudaStream_t stream);

@@ -255,6 +255,39 @@ __device__ __forceinline__ float4 ld_global_cg_v4(const float* ptr) {
     return v;
 }
 
+// ---------------------------------------------------------------- TMA tile stores
+//
+// 2-D tile store from this CTA's shared memory to global memory (which may
+// be a peer GPU's buffer mapped through CUDA IPC) through a tensor map; the
+// copy runs in the async proxy, so the shared-memory writes it reads must be
+// published first with fence_proxy_async_shared().  No multicast.
+
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(src), "r"(x), "r"(y)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until at most N committed bulk groups of this thread still read
+// their shared-memory source (the buffer may then be overwritten).
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Waits until at most N committed bulk groups of this thread are incomplete.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ---------------------------------------------------------------- CTA pairs (cta_group::2)
 //
 // A 2-CTA cluster runs one MMA over both SMs: each CTA holds its own half of
@@ -278,6 +311,16 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t cluster_addr) {
     float v;
     asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+    return v;
+}
+
+// 128-bit load from a shared::cluster address (this CTA's or a peer's shared memory).
+__device__ __forceinline__ float4 ld_shared_cluster_v4(uint32_t cluster_addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(cluster_addr)
+                 : "memory");
     return v;
 }
 

@@ -387,8 +387,8 @@ def test_k_split(lib, gpu_ctx, mnk, precision, monkeypatch, host_threads):
     column tile and k-block): the result matches
     the oracle, repeats bit for bit (the slices are summed in slice order
     whichever CTA finishes last), equals the row-streamed executor's bit for
-    bit (the split follows the node's full row count), and stays within
-    tolerance of the unsplit kernel."""
+    bit (the split follows the node's full row count) and the separate reduce
+    kernel's, and stays within tolerance of the unsplit kernel."""
     M, N, K = mnk
     A, B, C = _relu_abc(M, N, K, c_normal=True)
     bias = datagen.normal((N,), 5, 0.0, 0.5)
@@ -404,6 +404,11 @@ def test_k_split(lib, gpu_ctx, mnk, precision, monkeypatch, host_threads):
     monkeypatch.setenv("MINIXLA_STREAM_CHUNKS", "8")
     assert np.array_equal(got, run_execute(lib, gpu_ctx, root, precision)), "row-streamed K split differs"
     monkeypatch.setenv("MINIXLA_STREAM_CHUNKS", "1")
+    # The slices summed inside the GEMM's clusters (default) and by the
+    # separate reduce kernel over workspace: the same additions, same bits.
+    monkeypatch.setenv("MINIXLA_KSPLIT_REDUCE", "kernel")
+    assert np.array_equal(got, run_execute(lib, gpu_ctx, root, precision)), "reduce kernel differs from cluster sum"
+    monkeypatch.delenv("MINIXLA_KSPLIT_REDUCE")
     monkeypatch.setenv("MINIXLA_KSPLIT", "0")
     unsplit = run_execute(lib, gpu_ctx, root, precision)
     check(got, unsplit, precision, f"k-split vs unsplit {mnk}")
