@@ -18,7 +18,7 @@ CSRC = PKG / "csrc"
 LIB_DIR = PKG / "_lib"
 LIB = LIB_DIR / "libminixla_b200.so"
 SOURCES = ["runtime.cu", "graph_plan.cu", "gemm_launch.cu", "exec_graph.cu", "exec_streamed.cu", "exec_sharded.cu",
-           "fused_gemm.cu", "fused_gemm_pair.cu", "fused_gemm_pair3.cu", "elementwise.cu", "skinny_gemm.cu", "noalloc.cu", "hostcopy.cu", "peer_ipc.cu"]
+           "fused_gemm.cu", "fused_gemm_pair.cu", "fused_gemm_pair3.cu", "elementwise.cu", "skinny_gemm.cu", "noalloc.cu", "hostcopy.cu", "peer_ipc.cu", "tensor_maps.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

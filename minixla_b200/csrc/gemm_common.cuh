@@ -579,54 +579,28 @@ __device__ __forceinline__ void prefetch_full_operands(int row, int col, int nco
 
 // ------------------------------------------------------------------ tensor maps
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    });
-    return fn;
-}
-
+// Encoders of the tensor maps the kernels read and write; all go through
+// encode_tensor_map (tensor_maps.cu), which caches the descriptors.
 // Row-major [rows, cols] fp32 with row pitch `ld` elements; box [box_rows][box_cols].
+// TFLOAT32: TMA rounds each fp32 element to TF32 (nearest even) on load.
 bool make_map(CUtensorMap* map, const float* base, long long rows, long long cols, long long ld,
               int box_cols, int box_rows, CUtensorMapSwizzle swizzle) {
-    EncodeTiledFn enc = encode_fn();
-    if (!enc) return false;
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
-    const cuuint32_t estr[2] = {1, 1};
-    // TFLOAT32: TMA rounds each fp32 element to TF32 (nearest even) on load.
-    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, 2, const_cast<float*>(base), dims,
-                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
+    const unsigned long long dims[2] = {static_cast<unsigned long long>(cols), static_cast<unsigned long long>(rows)};
+    const unsigned long long strides[1] = {static_cast<unsigned long long>(ld) * 4};
+    const unsigned box[2] = {static_cast<unsigned>(box_cols), static_cast<unsigned>(box_rows)};
+    return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, 2, base, dims, strides, box, swizzle,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 }
 
 // Row-major [rows, cols] fp32 destination of TMA tile stores (FLOAT32, no
 // swizzle), row pitch `ld` elements; box [box_rows][box_cols].
 bool make_store_map(CUtensorMap* map, const float* base, long long rows, long long cols, long long ld, int box_cols,
                     int box_rows) {
-    EncodeTiledFn enc = encode_fn();
-    if (!enc) return false;
-    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
-    const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
-    const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
+    const unsigned long long dims[2] = {static_cast<unsigned long long>(cols), static_cast<unsigned long long>(rows)};
+    const unsigned long long strides[1] = {static_cast<unsigned long long>(ld) * 4};
+    const unsigned box[2] = {static_cast<unsigned>(box_cols), static_cast<unsigned>(box_rows)};
+    return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE);
 }
 
 // `batch` row-major [rows, cols] fp32 matrices, `bstride` elements apart, row
@@ -634,17 +608,13 @@ bool make_store_map(CUtensorMap* map, const float* base, long long rows, long lo
 // edge read as zeros, never as the next matrix's.
 bool make_map_3d(CUtensorMap* map, const float* base, long long batch, long long rows, long long cols,
                  long long ld, long long bstride, int box_cols, int box_rows, CUtensorMapSwizzle swizzle) {
-    EncodeTiledFn enc = encode_fn();
-    if (!enc) return false;
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
-                                static_cast<cuuint64_t>(batch)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(bstride) * 4};
-    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
-    const cuuint32_t estr[3] = {1, 1, 1};
-    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, 3, const_cast<float*>(base), dims, strides, box,
-                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
+    const unsigned long long dims[3] = {static_cast<unsigned long long>(cols), static_cast<unsigned long long>(rows),
+                                        static_cast<unsigned long long>(batch)};
+    const unsigned long long strides[2] = {static_cast<unsigned long long>(ld) * 4,
+                                           static_cast<unsigned long long>(bstride) * 4};
+    const unsigned box[3] = {static_cast<unsigned>(box_cols), static_cast<unsigned>(box_rows), 1};
+    return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_TFLOAT32, 3, base, dims, strides, box, swizzle,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 }
 
 }  // namespace

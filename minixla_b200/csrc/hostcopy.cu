@@ -34,13 +34,20 @@ constexpr size_t kStageMinBytes = 2u << 20;  // smaller copies: the driver's own
 class CopyThreads {
   public:
     CopyThreads() = default;
-    // Starts the helpers (once): a quarter of the cores per pool, as two
-    // pools may run at once, at most seven.
+    // Starts the helpers (once): half the cores, at most seven, even though
+    // an upload ring and a download ring may both run (8192^3 through
+    // gpu_execute on 16 cores: 25.5 ms a step with seven helpers per ring
+    // against 27.8 ms with four; slots of 16 or 32 MiB were slower);
+    // $MINIXLA_STAGE_THREADS (0..15) sets the number of helpers instead.
     void start() {
         if (started_) return;
         started_ = true;
         const unsigned hw = std::thread::hardware_concurrency();
-        const unsigned n = hw >= 8 ? std::min(7u, hw / 4) : 0;
+        unsigned n = hw >= 4 ? std::min(7u, hw / 2) : 0;
+        if (const char* v = getenv("MINIXLA_STAGE_THREADS")) {
+            const int k = atoi(v);
+            if (k >= 0 && k <= 15) n = static_cast<unsigned>(k);
+        }
         for (unsigned i = 0; i < n; ++i) workers_.emplace_back([this, i] { run(i + 1); });
     }
     CopyThreads(const CopyThreads&) = delete;
@@ -150,8 +157,11 @@ bool staging_enabled() {
 // of the last copy that used it.
 class Stager {
   public:
-    static constexpr size_t kSlotBytes = 8u << 20;
     static constexpr int kSlots = 4;
+    // Slot size: 8 MiB, or $MINIXLA_STAGE_SLOT_MB (1..64) read when the ring
+    // is made; bigger slots mean fewer hand-offs to the copy threads per
+    // copy, at kSlots times the pinned memory.
+    size_t slot_bytes_ = 8u << 20;
 
     ~Stager() {
         for (cudaEvent_t& e : ev_) {
@@ -166,8 +176,12 @@ class Stager {
     bool ready() {
         if (buf_) return true;
         if (failed_) return false;
+        if (const char* v = getenv("MINIXLA_STAGE_SLOT_MB")) {
+            const int mb = atoi(v);
+            if (mb >= 1 && mb <= 64) slot_bytes_ = static_cast<size_t>(mb) << 20;
+        }
         void* b = nullptr;
-        if (cudaHostAlloc(&b, kSlots * kSlotBytes, cudaHostAllocDefault) != cudaSuccess) {
+        if (cudaHostAlloc(&b, kSlots * slot_bytes_, cudaHostAllocDefault) != cudaSuccess) {
             cudaGetLastError();
             failed_ = true;
             return false;
@@ -186,8 +200,8 @@ class Stager {
     }
 
     cudaError_t to_device(char* dst, const char* src, size_t bytes, cudaStream_t st) {
-        for (size_t off = 0; off < bytes; off += kSlotBytes) {
-            const size_t n = std::min(kSlotBytes, bytes - off);
+        for (size_t off = 0; off < bytes; off += slot_bytes_) {
+            const size_t n = std::min(slot_bytes_, bytes - off);
             const int s = take_slot();
             cudaError_t e = cudaEventSynchronize(ev_[s]);  // the slot's previous copy has left it
             if (e != cudaSuccess) return e;
@@ -205,10 +219,10 @@ class Stager {
 
     // Returns when the data is in `dst` (as a copy to pageable memory does).
     cudaError_t to_host(char* dst, const char* src, size_t bytes, cudaStream_t st) {
-        const size_t pieces = (bytes + kSlotBytes - 1) / kSlotBytes;
+        const size_t pieces = (bytes + slot_bytes_ - 1) / slot_bytes_;
         std::vector<int> slot_of(pieces, -1);
         auto issue = [&](size_t i) -> cudaError_t {
-            const size_t off = i * kSlotBytes, n = std::min(kSlotBytes, bytes - off);
+            const size_t off = i * slot_bytes_, n = std::min(slot_bytes_, bytes - off);
             const int s = take_slot();
             slot_of[i] = s;
             cudaError_t e = cudaEventSynchronize(ev_[s]);
@@ -222,15 +236,15 @@ class Stager {
         for (size_t i = 0; i < pieces && e == cudaSuccess; ++i) {
             const int s = slot_of[i];
             if ((e = cudaEventSynchronize(ev_[s])) != cudaSuccess) break;
-            const size_t off = i * kSlotBytes;
-            copier_.copy(dst + off, slot(s), std::min(kSlotBytes, bytes - off));
+            const size_t off = i * slot_bytes_;
+            copier_.copy(dst + off, slot(s), std::min(slot_bytes_, bytes - off));
             if (issued < pieces) e = issue(issued++);  // reuses the slot just emptied
         }
         return e;
     }
 
   private:
-    char* slot(int s) { return buf_ + static_cast<size_t>(s) * kSlotBytes; }
+    char* slot(int s) { return buf_ + static_cast<size_t>(s) * slot_bytes_; }
     int take_slot() {
         const int s = next_;
         next_ = (next_ + 1) % kSlots;

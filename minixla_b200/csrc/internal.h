@@ -142,6 +142,14 @@ cudaError_t copy_d2h(Stager* s, void* dst, const void* src, size_t bytes, cudaSt
 // write per page), ahead of downloads into it; nothing for pinned memory.
 void prefault_host(Stager* s, void* dst, size_t bytes);
 
+// cuTensorMapEncodeTiled through a per-process cache keyed by every argument
+// (tensor_maps.cu): dtype / swizzle / l2_promotion are the CUtensorMap* enum
+// values, dims and box have `rank` entries, strides rank - 1 (bytes).
+// MINIXLA_TMAP_CACHE=0 encodes every time.  False when encoding fails.
+bool encode_tensor_map(struct CUtensorMap_st* map, int dtype, int rank, const void* base,
+                       const unsigned long long* dims, const unsigned long long* strides, const unsigned* box,
+                       int swizzle, int l2_promotion);
+
 // Process-wide count of kernel launches issued by this library.
 void note_launch(unsigned n = 1);
 

@@ -157,7 +157,8 @@ def test_streamk_schedule_covers_every_kblock_once(tmp_path):
     exe = tmp_path / "streamk_schedule"
     subprocess.run([nvcc, "-std=c++17", "-O1", "-gencode", "arch=compute_100a,code=sm_100a", "-I",
                     str(root / "include"), "--expt-relaxed-constexpr", "-o", str(exe),
-                    str(root / "tests" / "native" / "streamk_schedule.cu")], check=True, capture_output=True)
+                    str(root / "tests" / "native" / "streamk_schedule.cu"),
+                    str(root / "minixla_b200" / "csrc" / "tensor_maps.cu")], check=True, capture_output=True)
     rng = random.Random(7)
     cases = [(128, 128, 74), (512, 256, 74), (256, 256, 74), (2048, 256, 74), (75, 1, 74), (149, 3, 74),
              (64, 64, 74), (74, 9, 74), (1000, 33, 73), (3, 5, 2)]

@@ -392,14 +392,17 @@ def test_k_split(lib, gpu_ctx, mnk, precision, monkeypatch, host_threads):
     M, N, K = mnk
     A, B, C = _relu_abc(M, N, K, c_normal=True)
     bias = datagen.normal((N,), 5, 0.0, 0.5)
+    odd = datagen.uniform((13,), 6)  # read by eval_fused's modulo rule
     hg = HostGraph()
     root = hg.fused_node(hg.input_node(A), hg.input_node(B),
-                         [(OP_ADD, hg.input_node(C)), (OP_RELU, None), (OP_ADD, hg.input_node(bias))])
+                         [(OP_ADD, hg.input_node(C)), (OP_ADD, hg.input_node(odd)), (OP_RELU, None),
+                          (OP_ADD, hg.input_node(bias))])
     monkeypatch.setenv("MINIXLA_STREAM_CHUNKS", "1")
     got = run_execute(lib, gpu_ctx, root, precision)
     assert np.array_equal(got, run_execute(lib, gpu_ctx, root, precision)), "K-split result not repeatable"
     rows = _sample_rows(M, 256)
-    want = bindings.fused_oracle(A, B, [("add", C), ("relu",), ("add", bias)], rows=rows, threads=host_threads)
+    want = bindings.fused_oracle(A, B, [("add", C), ("add", odd), ("relu",), ("add", bias)], rows=rows,
+                                 threads=host_threads)
     check(got[rows], want, precision, f"k-split {mnk}")
     monkeypatch.setenv("MINIXLA_STREAM_CHUNKS", "8")
     assert np.array_equal(got, run_execute(lib, gpu_ctx, root, precision)), "row-streamed K split differs"
