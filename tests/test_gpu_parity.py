@@ -256,11 +256,13 @@ def _sample_rows(M, n=512, seed=0):
 @pytest.mark.parametrize("precision", [X3, TF32], ids=["3xtf32", "tf32"])
 @pytest.mark.parametrize("S", [512, 1024, 2048, 4096, 8192])
 def test_config2_square_sweep(lib, gpu_ctx, S, precision, host_threads):
+    """Config 2 against the oracle: every output up to 4096^3, and at 8192^3
+    every 128-row tile edge plus 1024 random rows (about 1150 rows)."""
     A, B, C = _relu_abc(S, S, S, c_normal=True)
     hg = HostGraph()
     root = hg.fused_node(hg.input_node(A), hg.input_node(B), [(OP_ADD, hg.input_node(C)), (OP_RELU, None)])
     got = run_execute(lib, gpu_ctx, root, precision)
-    rows = None if S <= 2048 else _sample_rows(S, 384 if S == 8192 else 512)
+    rows = None if S <= 4096 else _sample_rows(S, 1024)
     want = bindings.fused_oracle(A, B, [("add", C), ("relu",)], rows=rows, threads=host_threads)
     check(got if rows is None else got[rows], want, precision, f"{S}^3")
 
