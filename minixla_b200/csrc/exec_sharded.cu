@@ -125,9 +125,16 @@ static int for_each_device(int P, const std::vector<GpuCtx*>& ctxs, Fn fn) {
         if (rc[d] != MXB_OK) msg[d] = mxb_last_error();
     };
     std::vector<std::thread> threads;
-    threads.reserve(P > 1 ? P - 1 : 0);
-    for (int d = 1; d < P; ++d) threads.emplace_back(run, d);
+    std::vector<int> inline_devices;  // devices whose thread could not be made: run here
+    for (int d = 1; d < P; ++d) {
+        try {
+            threads.emplace_back(run, d);
+        } catch (...) {
+            inline_devices.push_back(d);
+        }
+    }
     run(0);
+    for (int d : inline_devices) run(d);
     for (std::thread& t : threads) t.join();
     for (int d = 0; d < P; ++d) {
         if (rc[d] != MXB_OK) {

@@ -191,7 +191,7 @@ int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
     int enqueued = 0;        // chunks whose computed event is recorded
     bool abandon = false;    // the main thread stopped early
     int dl_rc = MXB_OK;
-    std::thread downloader([&] {
+    auto download_all = [&] {
         if (!cuda_ok(cudaSetDevice(ctx->device), "download thread device")) {
             dl_rc = MXB_E_CUDA;
             return;
@@ -215,7 +215,14 @@ int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
                 return;
             }
         }
-    });
+    };
+    // Without a thread (creation refused), the same downloads run after the
+    // uploads and kernels are enqueued, on this thread.
+    std::thread downloader;
+    try {
+        downloader = std::thread(download_all);
+    } catch (...) {
+    }
     for (int c = 0; c < n_chunks && rc == MXB_OK; ++c) {
         const long long r0 = static_cast<long long>(c) * rows_per;
         const long long r1 = std::min<long long>(M, r0 + rows_per);
@@ -302,7 +309,10 @@ int execute_streamed(GpuCtx* ctx, const std::vector<const Node*>& order,
         abandon = true;
     }
     dl_cv.notify_one();
-    downloader.join();
+    if (downloader.joinable())
+        downloader.join();
+    else
+        download_all();
     if (rc == MXB_OK && dl_rc != MXB_OK) {
         set_error("row streaming: a result download failed");
         rc = dl_rc;

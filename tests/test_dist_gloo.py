@@ -101,3 +101,31 @@ def test_shard_rows_partition():
         assert all(spans[i][1] == spans[i + 1][0] for i in range(parts - 1))
         sizes = [b - a for a, b in spans]
         assert max(sizes) - min(sizes) <= 1
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_bench_strong_split_and_checked_rows(world):
+    """bench.py's `strong` leg (config 5, 32768 x 8192 x 8192 split over N
+    GPUs): its row split is the library's (mxb_shard_rows), the shards cover
+    the job exactly once, and the rows each rank checks against the oracle
+    are at least 64, inside the shard, and include both shard edges and both
+    sides of the job's first 256-row tile boundary inside the shard (further
+    boundaries are taken at a stride that keeps about eight of them)."""
+    import bench
+    from minixla_b200 import lib as mlib
+
+    lib = mlib.load()
+    covered = 0
+    for rank in range(world):
+        r0, r1, m_total = bench.shard_rows(world, rank, "strong")
+        assert m_total == 32768 and (r0, r1) == _shard(lib, m_total, world, rank)
+        covered += r1 - r0
+        M = r1 - r0
+        rows = bench.check_rows(M, r0)
+        assert len(rows) >= 64 and rows == sorted(set(rows)) and 0 <= rows[0] and rows[-1] < M
+        assert {0, 1, M - 2, M - 1} <= set(rows)
+        # the first tile boundary of the job inside the shard, both sides
+        first = (r0 + 255) // 256 * 256
+        if r0 < first < r1:
+            assert {first - r0 - 1, first - r0} <= set(rows)
+    assert covered == 32768
