@@ -94,57 +94,71 @@ __device__ __forceinline__ void ks_dump_chunk(uint8_t* buf, int row, int c, cons
 }
 
 // After the cluster barrier: CTA `rank` of the tile's cluster sums rows
-// [rank * R, (rank + 1) * R) of the slices of all `splits` CTAs, in slice
-// order (slice 0, + slice 1, ...: the same additions as ksplit_reduce_kernel),
-// applies the node's epilogue and stores.  Warp w of the four epilogue warps
-// takes rows w, w + 4, ...; lane l the four columns 4l .. 4l + 3.
-__device__ __forceinline__ void ksplit_cluster_reduce(const FusedParams& p, const uint8_t* buf, int mb, int nb,
-                                                      int ep_warp, int lane) {
-    const int splits = p.splits;
+// [rank * R, (rank + 1) * R) of the slices of all S CTAs, in slice order
+// (slice 0, + slice 1, ...: the same additions as ksplit_reduce_kernel),
+// applies the node's epilogue and stores.  All six warps take part (the TMA
+// and MMA warps are idle by then): warp w takes rows w, w + 6, ... (RPT of
+// them), lane l the four columns 4l .. 4l + 3.  Every slice load of every row
+// a thread owns is issued before the first add (S x RPT float4s in flight),
+// so the sum waits on distributed shared memory once.  Issued four rows at a
+// time by the four epilogue warps, each round waited for its loads and then
+// its C loads, and the sum took 16,000 of (8191, 127, 3000)'s 52,000 cycles
+// (28,000 in the k-loop).
+template <int S, int RPT>
+__device__ __forceinline__ void ksplit_cluster_reduce_t(const FusedParams& p, const uint8_t* buf, int mb, int nb,
+                                                        int warp, int lane) {
+    constexpr int kWarps = kThreads / 32;
+    constexpr int kPer = (128 + S - 1) / S;
+    static_assert(RPT * kWarps >= kPer, "rows per thread cover the CTA's share");
     const uint32_t rank = cluster_ctarank();
-    const int per = (128 + splits - 1) / splits;
-    const int r_lo = static_cast<int>(rank) * per, r_hi = min(128, r_lo + per);
+    const int r_lo = static_cast<int>(rank) * kPer, r_hi = min(128, r_lo + kPer);
     const int col = nb * 128 + 4 * lane;
     if (col >= p.N) return;
     const uint32_t base = smem_addr(buf);
-    uint32_t remote[8];
+    float v[RPT][4];
+    int row[RPT];
+    bool ok[RPT];
+    float4 x[S][RPT];
 #pragma unroll
-    for (int s = 0; s < 8; ++s) remote[s] = s < splits ? mapa_shared(base, static_cast<uint32_t>(s)) : 0u;
-    // Four rows at a time (rows r, r + 4, r + 8, r + 12 of this warp), every
-    // load of a group issued before its stores: the 64 outputs a thread owns
-    // then take four rounds of memory latency instead of sixteen.
-    constexpr int kR = 4;
-    for (int r0 = r_lo + ep_warp; r0 < r_hi; r0 += 4 * kR) {
-        float v[kR][4];
-        int row[kR];
-        bool ok[kR];
+    for (int u = 0; u < RPT; ++u) {
+        const int r = r_lo + warp + kWarps * u;
+        row[u] = mb * 128 + r;
+        ok[u] = r < r_hi && row[u] < p.M;
+    }
 #pragma unroll
-        for (int u = 0; u < kR; ++u) {
-            const int r = r0 + 4 * u;
-            row[u] = mb * 128 + r;
-            ok[u] = r < r_hi && row[u] < p.M;
-            const uint32_t off = ks_slot(ok[u] ? r : r_lo, lane);
-            float4 x = ld_shared_cluster_v4(remote[0] + off);
-            v[u][0] = x.x;
-            v[u][1] = x.y;
-            v[u][2] = x.z;
-            v[u][3] = x.w;
+    for (int s = 0; s < S; ++s) {
+        const uint32_t remote = mapa_shared(base, static_cast<uint32_t>(s));
+#pragma unroll
+        for (int u = 0; u < RPT; ++u)
+            x[s][u] = ld_shared_cluster_v4(remote + ks_slot(ok[u] ? r_lo + warp + kWarps * u : r_lo, lane));
+    }
+#pragma unroll
+    for (int u = 0; u < RPT; ++u) {
+        v[u][0] = x[0][u].x;
+        v[u][1] = x[0][u].y;
+        v[u][2] = x[0][u].z;
+        v[u][3] = x[0][u].w;
+#pragma unroll
+        for (int s = 1; s < S; ++s) {
+            v[u][0] += x[s][u].x;
+            v[u][1] += x[s][u].y;
+            v[u][2] += x[s][u].z;
+            v[u][3] += x[s][u].w;
         }
-        for (int s = 1; s < splits; ++s) {
+    }
+    apply_epilogue_rows<RPT>(v, row, ok, col, p);
 #pragma unroll
-            for (int u = 0; u < kR; ++u) {
-                const uint32_t off = ks_slot(ok[u] ? r0 + 4 * u : r_lo, lane);
-                const float4 x = ld_shared_cluster_v4(remote[s] + off);
-                v[u][0] += x.x;
-                v[u][1] += x.y;
-                v[u][2] += x.z;
-                v[u][3] += x.w;
-            }
-        }
-        apply_epilogue_rows<kR>(v, row, ok, col, p);
-#pragma unroll
-        for (int u = 0; u < kR; ++u)
-            if (ok[u]) store_row_chunk<4>(v[u], row[u], col, p);
+    for (int u = 0; u < RPT; ++u)
+        if (ok[u]) store_row_chunk<4>(v[u], row[u], col, p);
+}
+
+// In-cluster sums come in 2, 3 or 4 slices (fused_gemm_ksplit_in_cluster).
+__device__ __forceinline__ void ksplit_cluster_reduce(const FusedParams& p, const uint8_t* buf, int mb, int nb,
+                                                      int warp, int lane) {
+    switch (p.splits) {
+        case 2: ksplit_cluster_reduce_t<2, 11>(p, buf, mb, nb, warp, lane); break;
+        case 3: ksplit_cluster_reduce_t<3, 8>(p, buf, mb, nb, warp, lane); break;
+        default: ksplit_cluster_reduce_t<4, 6>(p, buf, mb, nb, warp, lane); break;
     }
 }
 
@@ -512,10 +526,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // (a timed-out wait above only skips work), so neither can hang.
         __syncwarp();
         cluster_sync();  // each slice is in its CTA's shared memory
-        if (warp >= 2) {
+        {
             int mb, nb;
             tile_coords(static_cast<int>(blockIdx.x) / p.splits, p, mb, nb);
-            ksplit_cluster_reduce(p, smem, mb, nb, warp - 2, lane);
+            ksplit_cluster_reduce(p, smem, mb, nb, warp, lane);
         }
         __syncwarp();
         cluster_sync();  // no CTA leaves while the others still read its slice
@@ -818,7 +832,7 @@ int fused_gemm_streamk_tiles(const GemmLaunch& g) {
 // Clusters of up to four: eight-CTA clusters of these ~200 KB CTAs do not all
 // fit at once (512 x 512 x 8192, 16 clusters of 8: 40.9 us against 25.5 us
 // with the reduce kernel), while with two slices the in-cluster sum wins
-// ((8191, 127, 3000): 34.8 vs 39.9 us; (640, 384, 4100), four: 20.4 vs 21.4 us).
+// ((8191, 127, 3000): 31.7 vs 39.9 us; (640, 384, 4100), four: 20.4 vs 21.4 us).
 bool fused_gemm_ksplit_in_cluster(const GemmLaunch& g) {
     if (g.k_splits < 2 || !ksplit_cluster_enabled()) return false;
     const int num_kb = (g.K + kBK - 1) / kBK;

@@ -22,6 +22,7 @@ CASES = [
     ((8191, 127, 3000, TF32), (SINGLE, 128, 128, 2)),     # few tiles, long K
     ((8191, 127, 3000, X3), (SINGLE, 128, 128, 2)),
     ((4096, 128, 2048, TF32), (SINGLE, 128, 128, 4)),
+    ((760, 890, 4100, TF32), (SINGLE, 128, 128, 3)),     # 42 tiles: three slices per tile
     ((512, 512, 8192, TF32), (SINGLE, 128, 128, 8)),
     ((16, 8192, 8192, TF32), (SINGLE, 128, 128, 2)),      # 9..16 rows: tensor cores in TF32 mode
     ((9, 4096, 4096, TF32), (SINGLE, 128, 128, 4)),

@@ -381,12 +381,13 @@ def test_kernel_variants(lib, gpu_ctx, mnk, variant, precision, monkeypatch, hos
 
 
 @pytest.mark.parametrize("precision", [TF32, X3], ids=["tf32", "3xtf32"])
-@pytest.mark.parametrize("mnk", [(8191, 127, 3000), (2047, 250, 6200), (2048, 256, 8192), (1024, 1024, 8192)])
+@pytest.mark.parametrize("mnk", [(8191, 127, 3000), (2047, 250, 6200), (2048, 256, 8192), (1024, 1024, 8192),
+                                 (760, 890, 4100)])
 def test_k_split(lib, gpu_ctx, mnk, precision, monkeypatch, host_threads):
     """Shapes whose 128 x 128 tiles fill under half the SMs with a long
     K (>= 64 k-blocks) run the single-CTA kernel with K split across CTAs
-    (here two and four ways; (2047, 250, 6200) ends on a partial row tile,
-    column tile and k-block): the result matches
+    (here two, three and four ways; (2047, 250, 6200) and (760, 890, 4100)
+    end on a partial row tile, column tile and k-block): the result matches
     the oracle, repeats bit for bit (the slices are summed in slice order
     whichever CTA finishes last), equals the row-streamed executor's bit for
     bit (the split follows the node's full row count) and the separate reduce
