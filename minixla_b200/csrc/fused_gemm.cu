@@ -764,14 +764,29 @@ int single_cta_width(const GemmLaunch& g) {
 // tile's k-loop (single buffer); it prefetches its rows of C into L2 first.
 // Measured at 8192^3: 784 vs 712 TFLOP/s, and 693 vs 652 under the power
 // cap.  (Eight epilogue warps instead of four drained no faster.)  Used once
-// the wide tiles alone give every CTA pair a tile.
+// the wide tiles alone give every CTA pair a tile, unless they would end in a
+// stream-K tail with a k-loop under kWideStreamKMinKb blocks: there the
+// 256 x 256 tiles, twice as many and so in finer waves, ran faster
+// (held-stream CUDA events, wide with its stream-K tail vs 256 x 256):
+// (4096, 8192, 4096) 411.6 vs 378.9 us, (8192, 4096, 4096) 409.4 vs 380.9,
+// (4096, 8192, 2048) 271.3 vs 212.0, (6144, 8192, 4096) 604.1 vs 594.0,
+// (4096, 6144, 4096) 323.6 vs 319.5; at K = 8192 the two were even
+// ((4096, 8192, 8192) 729.1 vs 732.2) and without a stream-K tail the wide
+// tiles won ((6144)^3 609.3 vs 645.1, 8192^3 1385.5 vs 1492.8).
+constexpr int kWideStreamKMinKb = 256;
+
 bool pair_wide_tiles(const GemmLaunch& g) {
     if (const char* v = getenv("MINIXLA_GEMM_VARIANT")) {
         if (!strcmp(v, "pair512")) return true;
         if (!strcmp(v, "pair")) return false;
     }
     const long long wide_tiles = static_cast<long long>((g.M + 255) / 256) * ((g.N + 511) / 512);
-    return wide_tiles >= g.num_sms / 2;
+    if (wide_tiles < g.num_sms / 2) return false;
+    const int num_kb = (g.K + kBK - 1) / kBK;
+    if (num_kb < kWideStreamKMinKb && wide_tiles < (1ll << 31) &&
+        streamk_split(static_cast<int>(wide_tiles), num_kb, g.num_sms / 2).q > 0)
+        return false;
+    return true;
 }
 
 }  // namespace

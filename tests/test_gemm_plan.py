@@ -18,6 +18,8 @@ CASES = [
     ((8192, 8192, 8192, X3), (PAIR, 256, 256, 1)),
     ((32768, 8192, 8192, TF32), (PAIR, 256, 512, 1)),
     ((2048, 2048, 2048, TF32), (PAIR, 256, 256, 1)),      # too few 256 x 512 tiles
+    ((4096, 8192, 4096, TF32), (PAIR, 256, 256, 1)),      # wide tiles would need a stream-K tail, K < 8192
+    ((4096, 8192, 8192, TF32), (PAIR, 256, 512, 1)),      # ... at K = 8192 they keep it
     ((1024, 1024, 1024, TF32), (SINGLE, 128, 64, 1)),     # 32 k-blocks: no K split
     ((8191, 127, 3000, TF32), (SINGLE, 128, 128, 2)),     # few tiles, long K
     ((8191, 127, 3000, X3), (SINGLE, 128, 128, 2)),
@@ -127,8 +129,9 @@ STREAMK = [
     ((32768, 8192, 8192), 0),     # 2048 tiles = 27 x 74 + 50: 24 idle, under 1 in 25
     ((2048, 2048, 2048), 0),      # 64 tiles of 256 x 256: fewer than the pairs
     ((9472, 8192, 8192), 0),      # 592 tiles = 8 x 74 exactly
-    ((5120, 4096, 2048), 86),     # 160 tiles = 2 x 74 + 12
+    ((5120, 4096, 2048), 98),     # 256 x 256 tiles (see below): 320 = 4 x 74 + 24
     ((5120, 4096, 1024), 0),      # ... with a short k-loop (32 blocks)
+    ((3300, 6001, 2049), 90),     # 312 tiles of 256 x 256 = 4 x 74 + 16, ragged M, N, K
 ]
 
 

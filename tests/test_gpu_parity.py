@@ -909,9 +909,9 @@ def test_allocation_failure_injection(fail_at):
 
 
 # (M, N, K) whose TF32 CTA-pair tiles do not fill a whole number of waves on
-# 74 pairs: 160 wide tiles (86 stream-K), 156 wide tiles with a ragged M, N
-# and K (82 stream-K), and the 8-way split of config 5 (256 wide tiles: 148
-# run whole, 108 stream-K).
+# 74 pairs: 320 tiles of 256 x 256 (98 stream-K), 312 of them with a ragged
+# M, N and K (90 stream-K), and the 8-way split of config 5 (256 wide tiles of
+# 256 x 512: 148 run whole, 108 stream-K), so both tile widths hand off.
 STREAMK_SHAPES = [(5120, 4096, 2048), (3300, 6001, 2049), (4096, 8192, 8192)]
 
 

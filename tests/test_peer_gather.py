@@ -181,7 +181,7 @@ def test_gather_buffers_argument_checks():
 GPU_CASES = [
     (2048, 0, 2048, 256, 1, "1", True),    # 256 x 256 pair tiles, TMA tile stores
     (4096, 0, 4096, 128, 1, "1", True),    # 256 x 512 pair tiles
-    (4096, 0, 6144, 2048, 1, "1", True),   # 192 wide tiles per shard: stream-K tail with the push
+    (4096, 0, 6144, 2048, 1, "1", True),   # 384 tiles of 256 x 256 per shard: stream-K tail (88) with the push
     (2048, 1, 2047, 200, 1, "1", True),    # uneven shards, odd pitch: scalar copies, K tail
     (2048, 0, 2048, 256, 1, "0", False),   # copy form forced
     (2048, 0, 2048, 256, 3, "1", True),    # 3xTF32 CTA-pair kernel pushes too
