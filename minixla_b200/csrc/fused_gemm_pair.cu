@@ -62,13 +62,19 @@ struct PairCfg {
     static constexpr int kBufs = kAccCols <= 256 ? 2 : 1;        // accumulator buffers in TMEM
     static constexpr int kTmemCols = kBufs * kAccCols;
     static constexpr int kBarOffset = STAGES * kStageBytes;
-    static constexpr int kNumBars = 2 * STAGES + 6;
+    // Single-buffer tiles move C and the output through TMA boxes
+    // (FusedParams::tma_c / tma_out): two 32 x 32 boxes per epilogue warp,
+    // each with its mbarrier for C loads.
+    static constexpr bool kTmaC = kBufs == 1 && !DUAL && !PUSH;
+    static constexpr int kNumBars = 2 * STAGES + 6 + 2 * EPI;
     // PUSH: two 8-row x 128-column staging buffers per epilogue warp for the
-    // TMA stores of the row all-gather, 1 KiB aligned after the barriers.
+    // TMA stores of the row all-gather; kTmaC: the two boxes (the same 8 KiB);
+    // 1 KiB aligned after the barriers.
     static constexpr int kStagingOffset = (kBarOffset + kNumBars * 8 + 16 + 1023) / 1024 * 1024;
     static constexpr int kStagingPerWarp = 2 * kPushBoxRows * kPushBoxCols * 4;
+    static_assert(kStagingPerWarp == 2 * 32 * 32 * 4, "a warp's staging holds two 32 x 32 boxes");
     static constexpr int kSmemBytes =
-        1024 + (PUSH ? kStagingOffset + EPI * kStagingPerWarp : kBarOffset + kNumBars * 8 + 16);
+        1024 + ((PUSH || kTmaC) ? kStagingOffset + EPI * kStagingPerWarp : kBarOffset + kNumBars * 8 + 16);
     static_assert(BN == 128 || BN == 256 || BN == 512, "pair tile width");
     static_assert(!(DUAL && BN == 512), "two products use 128- or 256-column tiles");
     static_assert(kStageBytes % 1024 == 0, "stages must keep 1 KiB swizzle alignment");
@@ -137,7 +143,8 @@ template <int STAGES, int BN, bool DUAL, int EPI, bool PUSH, bool BATCHED = fals
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, DUAL, EPI>::kThreadsPerCta, 1)
     fused_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
-                           const __grid_constant__ FusedParams p, const __grid_constant__ PeerMaps pm) {
+                           const __grid_constant__ FusedParams p, const __grid_constant__ PeerMaps pm,
+                           const __grid_constant__ EpiMaps em) {
     using C = PairCfg<STAGES, BN, DUAL, EPI, PUSH>;
     static_assert(!(BATCHED && (DUAL || PUSH)), "a batched launch has one product and no peer rows");
     extern __shared__ uint8_t smem_raw[];
@@ -154,6 +161,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
     auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
     const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
     const uint32_t tload_bar = bar0 + 8u * (2 * STAGES + 5);
+    // Epilogue warp w's boxes (kTmaC): barrier of box i's C load.
+    auto cbox_bar = [&](int w, int i) { return bar0 + 8u * (2 * STAGES + 6 + 2 * (w - 2) + i); };
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -172,10 +181,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
         }
         mbar_init(drain_bar, 1);
         mbar_init(tload_bar, 2 * EPI);  // every epilogue warp of the two CTAs, once per launch
+        for (int i = 0; i < 2 * EPI; ++i) mbar_init(bar0 + 8u * (2 * STAGES + 6 + i), 1);
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if (C::kTmaC && p.tma_c) tma_prefetch_desc(&em.c);
+        if (C::kTmaC && p.tma_out) tma_prefetch_desc(&em.out);
         if (DUAL) {
             tma_prefetch_desc(&tmA2);
             tma_prefetch_desc(&tmB2);
@@ -331,6 +343,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
         const uint32_t tempty_leader1 = mapa_shared(tempty_bar(1), 0);
         int acc = 0;
         uint32_t acc_phase = 0;
+        uint32_t cbox_phase = 0;    // bit i: parity of box i's next C load
+        uint32_t cbox_pending = 0;  // bit i: a C load into box i not yet waited for
+        bool cbox_failed = false;
         // Stream-K hand-off: this warp's rows of the tile (lane quadrant,
         // column range) in the head pair's slot and the flag it sets.
         const int sk_warp = (static_cast<int>(rank) * EPI + (warp - 2));
@@ -441,16 +456,53 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                 if (acc == 0) acc_phase ^= 1u;
                 continue;
             }
+            // Single-buffer tiles (kTmaC): C in (tma_c) and the result out
+            // (tma_out) as 32 x 32 TMA boxes of this warp's 32 rows, through
+            // two 128-byte swizzled boxes of shared memory per warp; each lane
+            // reads and writes its own row there.  Box i holds C of chunk c,
+            // then chunk c's result until its TMA store has read it, then C of
+            // chunk c + 2.  Read and written by each lane from and to its own
+            // row of global memory (32 rows per warp instruction), C and the
+            // output kept the load/store unit busy for 37,000 of the 45,000
+            // cycles a 256 x 512 tile's drain took, the MMA warp waiting for
+            // the accumulator all along.
+            const int box_row0 = mb * 256 + static_cast<int>(rank) * 128 + quad * 32;
+            const bool boxes = C::kTmaC && box_row0 < p.M;
+            const bool cbox = boxes && p.tma_c;
+            const bool obox = boxes && p.tma_out;
+            uint8_t* const box_buf = smem + C::kStagingOffset + (warp - 2) * C::kStagingPerWarp;
+            // Issued by lane 0; every lane keeps the pending bits.
+            auto cbox_load = [&](int c) {
+                const int i = (c - c_first) & 1;
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(cbox_bar(warp, i), 32 * 32 * 4);
+                    tma_load_2d(smem_addr(box_buf + i * 4096), &em.c, cbox_bar(warp, i), col0 + 32 * c, box_row0);
+                }
+                cbox_pending |= 1u << i;
+            };
+            if (cbox) {
+                if (obox && lane == 0) bulk_wait_group_read<0>();  // the previous tile's stores have read both boxes
+                cbox_load(c_first);
+                if (!obox && c_first + 1 < chunks) cbox_load(c_first + 1);
+            }
             for (int c = c_first; c < chunks; ++c) {
                 uint32_t r[32];
                 float w[32];
                 tmem_ld_32x32b_x32(taddr + 32 * c, r);
+                const int i = (c - c_first) & 1;
+                if (cbox && obox && c + 1 < chunks) {
+                    // box i ^ 1 is free once chunk c - 1's store has read it
+                    if (lane == 0) bulk_wait_group_read<0>();
+                    cbox_load(c + 1);
+                } else if (!cbox && obox && lane == 0) {
+                    bulk_wait_group_read<1>();  // chunk c - 2's store has read box i
+                }
                 if (DUAL) {
                     uint32_t r2[32];
                     tmem_ld_32x32b_x32(taddr + BN + 32 * c, r2);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) w[i] = __uint_as_float(r2[i]);
+                    for (int k = 0; k < 32; ++k) w[k] = __uint_as_float(r2[k]);
                 } else {
                     tmem_ld_wait();
                 }
@@ -462,13 +514,57 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                 }
                 float v[32];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
                 const int col = col0 + 32 * c;
+                uint8_t* const rowp = box_buf + i * 4096 + lane * 128;
+                if (cbox) {
+                    const bool got = mbar_wait(cbox_bar(warp, i), (cbox_phase >> i) & 1u, p.timeout_ns);
+                    if (!__all_sync(0xffffffffu, got)) {
+                        if (lane == 0) raise_error(p, abort_flag, kErrEpilogue);
+                        cbox_failed = true;
+                        break;
+                    }
+                    cbox_phase ^= 1u << i;
+                    cbox_pending &= ~(1u << i);
+                    // Step 0 (v += C), the add the FULL step makes; columns
+                    // past N read the box's zero fill and are never stored.
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 x = *reinterpret_cast<const float4*>(rowp + ((j ^ (lane & 7)) << 4));
+                        v[4 * j] += x.x;
+                        v[4 * j + 1] += x.y;
+                        v[4 * j + 2] += x.z;
+                        v[4 * j + 3] += x.w;
+                    }
+                    if (!obox) {
+                        __syncwarp();  // every lane has read box i: it may be refilled
+                        if (c + 2 < chunks) {
+                            if (lane == 0) fence_proxy_async_shared();  // those reads before the TMA write
+                            cbox_load(c + 2);
+                        }
+                    }
+                }
                 if (DUAL)
                     apply_epilogue(v, row, col, row_ok, p, w);
                 else
-                    apply_epilogue(v, row, col, row_ok, p, nullptr, b);
-                if (row_ok) store_row_chunk(v, row, col, p, out_off);
+                    apply_epilogue(v, row, col, row_ok, p, nullptr, b, cbox);
+                if (obox) {
+                    // The result into box i (rows past M and columns past N are
+                    // clipped by the store), then one TMA store of the box.
+                    if (!cbox) __syncwarp();  // lane 0 waited for box i above
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        *reinterpret_cast<float4*>(rowp + ((j ^ (lane & 7)) << 4)) =
+                            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    fence_proxy_async_shared();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&em.out, smem_addr(box_buf + i * 4096), col, box_row0);
+                        bulk_commit_group();
+                    }
+                } else if (row_ok) {
+                    store_row_chunk(v, row, col, p, out_off);
+                }
             }
             if (PUSH) {
                 // The accumulator is already released: these copies overlap the next tile's k-loop.
@@ -479,8 +575,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                 else
                     push_rows<8>(p, mb * 256 + row_in_tile - lane, col0 + 32 * c_first, c_end);
             }
+            if (cbox_failed) break;
             if (C::kBufs == 2) acc ^= 1;
             if (acc == 0) acc_phase ^= 1u;
+        }
+        // A C box load that was not waited for (a wait that ran out above) must
+        // land before the CTA leaves: wait for it once more, bounded.  The
+        // boxes' stores complete before it leaves too.
+        if (C::kTmaC) {
+            for (int i = 0; i < 2; ++i)
+                if (cbox_pending & (1u << i)) mbar_wait(cbox_bar(warp, i), (cbox_phase >> i) & 1u, p.timeout_ns);
+            if (lane == 0) bulk_wait_group<0>();
+            __syncwarp();
         }
         // Peer stores performed before the kernel counts as finished.
         if (PUSH) {
@@ -505,6 +611,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
 // warps' own global stores instead of TMA tile stores.
 bool gather_tma_enabled() {
     const char* v = getenv("MINIXLA_GATHER_TMA");
+    return !(v && v[0] == '0');
+}
+
+// MINIXLA_EPI_TMA=0: the single-buffer tiles' epilogue reads C and writes
+// the output row by row from global memory instead of through TMA boxes.
+bool epi_tma_enabled() {
+    const char* v = getenv("MINIXLA_EPI_TMA");
     return !(v && v[0] == '0');
 }
 
@@ -641,7 +754,16 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
             if (e2 != cudaSuccess) return e2;
         }
     }
-    kernel<<<2 * pairs, C::kThreadsPerCta, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p, pm);
+    EpiMaps em;
+    memset(&em, 0, sizeof(em));
+    if (C::kTmaC && epi_tma_enabled()) {
+        if (g.n_steps > 0 && g.steps[0].kind == MXB_EP_ADD_FULL && (g.steps[0].ld_or_size & 3) == 0 &&
+            (reinterpret_cast<uintptr_t>(g.steps[0].ptr) & 15) == 0)
+            p.tma_c = make_epi_map(&em.c, g.steps[0].ptr, g.M, g.N, g.steps[0].ld_or_size) ? 1 : 0;
+        if ((g.ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(g.out) & 15) == 0)
+            p.tma_out = make_epi_map(&em.out, g.out, g.M, g.N, g.ldo) ? 1 : 0;
+    }
+    kernel<<<2 * pairs, C::kThreadsPerCta, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p, pm, em);
     note_launch();
     return cudaGetLastError();
 }

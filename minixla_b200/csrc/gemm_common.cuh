@@ -64,6 +64,11 @@ struct FusedParams {
     int n_peers;
     int push_vec;                   // 16-byte aligned bases and ldo % 4 == 0: float4 copies
     int push_tma;                   // push_vec and PeerMaps valid: tile stores through TMA
+    // Single-buffer CTA-pair tiles: the epilogue reads step 0's FULL operand
+    // (tma_c, EpiMaps::c valid) and writes the output (tma_out, EpiMaps::out
+    // valid) as 32 x 32 TMA boxes through shared memory.
+    int tma_c;
+    int tma_out;
     // K split (single-CTA TF32 kernel, KSPLIT instances): tile t is output
     // tile t / splits, k-blocks [s * kb_per_split, +kb_per_split) with
     // s = t % splits.  Slice s of the product goes raw to ks_ws + s * ks_stride
@@ -150,6 +155,13 @@ inline StreamKSplit streamk_split(int tiles, int num_kb, int pairs) {
 constexpr int kPushBoxRows = 8, kPushBoxCols = 128;
 struct PeerMaps {
     CUtensorMap m[kMaxPeers];
+};
+
+// The epilogue's tensor maps (make_epi_map): step 0's FULL operand, [M, N],
+// its own pitch (FusedParams::tma_c); the output, [M, N], pitch ldo (tma_out).
+struct EpiMaps {
+    CUtensorMap c;
+    CUtensorMap out;
 };
 
 // One unit of a CTA pair's work: k-blocks [kb0, kb1) of tile t.
@@ -283,9 +295,12 @@ __device__ __forceinline__ int lead_scalars(const float* p) {
     return static_cast<int>((4 - ((reinterpret_cast<uintptr_t>(p) >> 2) & 3)) & 3);
 }
 
+// The node's steps for W columns of one row.  step0_applied: the caller has
+// already added step 0's FULL operand (read from a TMA box).
 template <int W = 32>
 __device__ __forceinline__ void apply_epilogue(float (&v)[W], int row, int col, bool row_ok,
-                                               const FusedParams& p, const float* prod = nullptr, int b = 0) {
+                                               const FusedParams& p, const float* prod = nullptr, int b = 0,
+                                               bool step0_applied = false) {
     static_assert(W % 4 == 0, "whole float4 groups");
     const bool full_cols = col + W <= p.N;
     for (int s = 0; s < p.n_steps; ++s) {
@@ -304,7 +319,7 @@ __device__ __forceinline__ void apply_epilogue(float (&v)[W], int row, int col, 
 #pragma unroll
             for (int i = 0; i < W; ++i) v[i] = v[i] * sc;
         } else if (kind == MXB_EP_ADD_FULL) {
-            if (!row_ok) continue;
+            if (!row_ok || (s == 0 && step0_applied)) continue;
             const long long ld = p.steps[s].ld_or_size;
             const float* src = ptr + static_cast<long long>(row) * ld + col;
             if (b) src += b * p.ep_bstride[s];
@@ -601,6 +616,18 @@ bool make_store_map(CUtensorMap* map, const float* base, long long rows, long lo
     const unsigned box[2] = {static_cast<unsigned>(box_cols), static_cast<unsigned>(box_rows)};
     return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box,
                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE);
+}
+
+// Row-major [rows, cols] fp32 read or written by the epilogue as 32 x 32
+// boxes (FLOAT32: no rounding), 128-byte swizzled in shared memory: row r's
+// 16-byte chunk j sits at position j ^ (r % 8), so a warp whose lane r reads
+// or writes one chunk of row r touches eight different bank groups.
+bool make_epi_map(CUtensorMap* map, const float* base, long long rows, long long cols, long long ld) {
+    const unsigned long long dims[2] = {static_cast<unsigned long long>(cols), static_cast<unsigned long long>(rows)};
+    const unsigned long long strides[1] = {static_cast<unsigned long long>(ld) * 4};
+    const unsigned box[2] = {32, 32};
+    return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
 }
 
 // `batch` row-major [rows, cols] fp32 matrices, `bstride` elements apart, row
