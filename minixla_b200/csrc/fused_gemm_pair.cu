@@ -62,10 +62,11 @@ struct PairCfg {
     static constexpr int kBufs = kAccCols <= 256 ? 2 : 1;        // accumulator buffers in TMEM
     static constexpr int kTmemCols = kBufs * kAccCols;
     static constexpr int kBarOffset = STAGES * kStageBytes;
-    // Single-buffer tiles move C and the output through TMA boxes
-    // (FusedParams::tma_c / tma_out): two 32 x 32 boxes per epilogue warp,
-    // each with its mbarrier for C loads.
-    static constexpr bool kTmaC = kBufs == 1 && !DUAL && !PUSH;
+    // Single-product tiles move C and the output through TMA boxes
+    // (FusedParams::tma_c / tma_out; not in batched launches, whose C has a
+    // third coordinate): two 32 x 32 boxes per epilogue warp, each with its
+    // mbarrier for C loads.
+    static constexpr bool kTmaC = !DUAL && !PUSH;
     static constexpr int kNumBars = 2 * STAGES + 6 + 2 * EPI;
     // PUSH: two 8-row x 128-column staging buffers per epilogue warp for the
     // TMA stores of the row all-gather; kTmaC: the two boxes (the same 8 KiB);
@@ -146,6 +147,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                            const __grid_constant__ FusedParams p, const __grid_constant__ PeerMaps pm,
                            const __grid_constant__ EpiMaps em) {
     using C = PairCfg<STAGES, BN, DUAL, EPI, PUSH>;
+    constexpr bool kBoxes = C::kTmaC && !BATCHED;
     static_assert(!(BATCHED && (DUAL || PUSH)), "a batched launch has one product and no peer rows");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -186,8 +188,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
-        if (C::kTmaC && p.tma_c) tma_prefetch_desc(&em.c);
-        if (C::kTmaC && p.tma_out) tma_prefetch_desc(&em.out);
+        if (kBoxes && p.tma_c) tma_prefetch_desc(&em.c);
+        if (kBoxes && p.tma_out) tma_prefetch_desc(&em.out);
         if (DUAL) {
             tma_prefetch_desc(&tmA2);
             tma_prefetch_desc(&tmB2);
@@ -467,7 +469,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             // cycles a 256 x 512 tile's drain took, the MMA warp waiting for
             // the accumulator all along.
             const int box_row0 = mb * 256 + static_cast<int>(rank) * 128 + quad * 32;
-            const bool boxes = C::kTmaC && box_row0 < p.M;
+            const bool boxes = kBoxes && box_row0 < p.M;
             const bool cbox = boxes && p.tma_c;
             const bool obox = boxes && p.tma_out;
             uint8_t* const box_buf = smem + C::kStagingOffset + (warp - 2) * C::kStagingPerWarp;
@@ -582,7 +584,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
         // A C box load that was not waited for (a wait that ran out above) must
         // land before the CTA leaves: wait for it once more, bounded.  The
         // boxes' stores complete before it leaves too.
-        if (C::kTmaC) {
+        if (kBoxes) {
             for (int i = 0; i < 2; ++i)
                 if (cbox_pending & (1u << i)) mbar_wait(cbox_bar(warp, i), (cbox_phase >> i) & 1u, p.timeout_ns);
             if (lane == 0) bulk_wait_group<0>();
@@ -756,7 +758,7 @@ cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
     }
     EpiMaps em;
     memset(&em, 0, sizeof(em));
-    if (C::kTmaC && epi_tma_enabled()) {
+    if (C::kTmaC && !BATCHED && epi_tma_enabled()) {
         if (g.n_steps > 0 && g.steps[0].kind == MXB_EP_ADD_FULL && (g.steps[0].ld_or_size & 3) == 0 &&
             (reinterpret_cast<uintptr_t>(g.steps[0].ptr) & 15) == 0)
             p.tma_c = make_epi_map(&em.c, g.steps[0].ptr, g.M, g.N, g.steps[0].ld_or_size) ? 1 : 0;
