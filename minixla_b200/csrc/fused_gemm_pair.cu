@@ -482,7 +482,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                 }
                 cbox_pending |= 1u << i;
             };
-            if (cbox) {
+            if (cbox && c_first < chunks) {
                 if (obox && lane == 0) bulk_wait_group_read<0>();  // the previous tile's stores have read both boxes
                 cbox_load(c_first);
                 if (!obox && c_first + 1 < chunks) cbox_load(c_first + 1);
