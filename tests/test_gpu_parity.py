@@ -964,3 +964,32 @@ def test_stream_k_keeps_the_bits(lib, gpu_ctx, mnk, monkeypatch, host_threads):
     rows = sorted({0, 1, 127, 128, 255, 256, 257, M // 2, M - 2, M - 1, *rng.integers(0, M, 48).tolist()})
     want = bindings.fused_oracle(A_h, B_h, [("add", C_h), ("relu",), ("add", bias_h)], rows=rows, threads=host_threads)
     check(outs["1"][rows], want, TF32, f"stream-K {mnk}")
+
+
+@pytest.mark.parametrize("variant", ["pair512", "pair"])
+@pytest.mark.parametrize("mnk", [(300, 520, 100), (2047, 1030, 1500), (8000, 8000, 512)])
+def test_box_epilogue_keeps_the_bits(lib, gpu_ctx, mnk, variant, monkeypatch, host_threads):
+    """The TF32 CTA-pair kernels read C and write the output as 32 x 32 TMA
+    boxes through shared memory (rows past M and columns past N zero-filled on
+    the way in, clipped on the way out).  The result must be bit-equal to the
+    per-lane form (MINIXLA_EPI_TMA=0) on partial row, column and k tiles,
+    including a second FULL add (loaded per lane) and a bias row after relu,
+    and match the oracle within the TF32 tolerance."""
+    monkeypatch.setenv("MINIXLA_GEMM_VARIANT", variant)
+    M, N, K = mnk
+    A, B, C = _relu_abc(M, N, K, c_normal=True)
+    C2 = datagen.uniform((M, N), 41)
+    bias = datagen.normal((N,), 42, 0.0, 0.5)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A), hg.input_node(B),
+                         [(OP_ADD, hg.input_node(C)), (OP_ADD, hg.input_node(C2)), (OP_RELU, None),
+                          (OP_ADD, hg.input_node(bias))])
+    monkeypatch.setenv("MINIXLA_STREAM_CHUNKS", "1")
+    boxed = run_execute(lib, gpu_ctx, root, TF32)
+    monkeypatch.setenv("MINIXLA_EPI_TMA", "0")
+    per_lane = run_execute(lib, gpu_ctx, root, TF32)
+    assert np.array_equal(boxed, per_lane), "the box epilogue changed the bits"
+    rows = sorted({0, 1, 255, 256, M // 2, M - 2, M - 1, *np.random.default_rng(M).integers(0, M, 24).tolist()})
+    want = bindings.fused_oracle(A, B, [("add", C), ("add", C2), ("relu",), ("add", bias)], rows=rows,
+                                 threads=host_threads)
+    check(boxed[rows], want, TF32, f"box epilogue {variant} {mnk}")
