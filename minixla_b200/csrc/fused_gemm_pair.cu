@@ -458,8 +458,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                 if (acc == 0) acc_phase ^= 1u;
                 continue;
             }
-            // Single-buffer tiles (kTmaC): C in (tma_c) and the result out
-            // (tma_out) as 32 x 32 TMA boxes of this warp's 32 rows, through
+            // Single-product, unbatched tiles (kBoxes): C in (tma_c) and the
+            // result out (tma_out) as 32 x 32 TMA boxes of this warp's 32 rows, through
             // two 128-byte swizzled boxes of shared memory per warp; each lane
             // reads and writes its own row there.  Box i holds C of chunk c,
             // then chunk c's result until its TMA store has read it, then C of
@@ -467,7 +467,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
             // row of global memory (32 rows per warp instruction), C and the
             // output kept the load/store unit busy for 37,000 of the 45,000
             // cycles a 256 x 512 tile's drain took, the MMA warp waiting for
-            // the accumulator all along.
+            // the accumulator all along (256 x 256 tiles drain while the next
+            // tile runs, except at the end of a launch).
             const int box_row0 = mb * 256 + static_cast<int>(rank) * 128 + quad * 32;
             const bool boxes = kBoxes && box_row0 < p.M;
             const bool cbox = boxes && p.tma_c;
