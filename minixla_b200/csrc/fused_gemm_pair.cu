@@ -483,8 +483,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairCfg<STAGES, BN, 
                 }
                 cbox_pending |= 1u << i;
             };
+            // The previous tile's box stores have read both boxes (its last
+            // chunk may have used either box), and its lanes' reads of them
+            // come before the TMA writes below.
+            if ((cbox || obox) && c_first < chunks && lane == 0) {
+                if (obox) bulk_wait_group_read<0>();
+                fence_proxy_async_shared();
+            }
             if (cbox && c_first < chunks) {
-                if (obox && lane == 0) bulk_wait_group_read<0>();  // the previous tile's stores have read both boxes
                 cbox_load(c_first);
                 if (!obox && c_first + 1 < chunks) cbox_load(c_first + 1);
             }

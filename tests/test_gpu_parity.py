@@ -993,3 +993,27 @@ def test_box_epilogue_keeps_the_bits(lib, gpu_ctx, mnk, variant, monkeypatch, ho
     want = bindings.fused_oracle(A, B, [("add", C), ("add", C2), ("relu",), ("add", bias)], rows=rows,
                                  threads=host_threads)
     check(boxed[rows], want, TF32, f"box epilogue {variant} {mnk}")
+
+
+@pytest.mark.parametrize("variant", ["pair512", "pair"])
+def test_box_epilogue_output_only(lib, gpu_ctx, variant, monkeypatch, host_threads):
+    """A node whose first epilogue step is not a full add (a bias row, then
+    relu) writes through the output boxes alone.  With 8192 x 1120 outputs
+    each warp runs several tiles and the last column tile has an odd number
+    of 32-column chunks, so a tile may start on the box its predecessor's
+    last store is still reading: bit-equal to the per-lane form and within
+    the TF32 tolerance of the oracle."""
+    monkeypatch.setenv("MINIXLA_GEMM_VARIANT", variant)
+    M, N, K = 8192, 1120, 256
+    A, B, _ = _relu_abc(M, N, K, c_normal=True)
+    bias = datagen.normal((N,), 43, 0.0, 0.5)
+    hg = HostGraph()
+    root = hg.fused_node(hg.input_node(A), hg.input_node(B), [(OP_ADD, hg.input_node(bias)), (OP_RELU, None)])
+    monkeypatch.setenv("MINIXLA_STREAM_CHUNKS", "1")
+    boxed = run_execute(lib, gpu_ctx, root, TF32)
+    monkeypatch.setenv("MINIXLA_EPI_TMA", "0")
+    per_lane = run_execute(lib, gpu_ctx, root, TF32)
+    assert np.array_equal(boxed, per_lane), "the output boxes changed the bits"
+    rows = sorted({0, 255, 256, 4095, 4096, M - 1, *np.random.default_rng(7).integers(0, M, 24).tolist()})
+    want = bindings.fused_oracle(A, B, [("add", bias), ("relu",)], rows=rows, threads=host_threads)
+    check(boxed[rows], want, TF32, f"output boxes {variant}")
