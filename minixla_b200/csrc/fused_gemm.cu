@@ -55,8 +55,14 @@ struct Cfg {
     static constexpr int kStageBytes = (SPLIT3 ? 2 : 1) * kOperandBytes;
     static constexpr int kTmemCols = 2 * BN;
     static constexpr int kBarOffset = STAGES * kStageBytes;
-    static constexpr int kNumBars = 2 * STAGES + 5;
-    static constexpr int kSmemBytes = 1024 + kBarOffset + kNumBars * 8 + 16;
+    // TF32 tiles move C and the output through TMA boxes: two 32 x 32 fp32
+    // boxes per epilogue warp, 1 KiB aligned after the barriers, each with an
+    // mbarrier for its C loads (the last 8 barriers).
+    static constexpr bool kBoxRoom = !SPLIT3;
+    static constexpr int kNumBars = 2 * STAGES + 5 + 8;
+    static constexpr int kBoxOffset = (kBarOffset + kNumBars * 8 + 16 + 1023) / 1024 * 1024;
+    static constexpr int kSmemBytes =
+        1024 + (kBoxRoom ? kBoxOffset + 4 * 8192 : kBarOffset + kNumBars * 8 + 16);
     static_assert(kStageBytes % 1024 == 0, "stages must keep 1 KiB swizzle alignment");
     static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
     static_assert(kTmemCols == 64 || kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512,
@@ -166,8 +172,11 @@ template <int BN, int STAGES, bool SPLIT3, bool SEG, bool KSPLIT = false, bool B
 __global__ void __launch_bounds__(kThreads, 1)
     fused_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
-                      const __grid_constant__ FusedParams p) {
+                      const __grid_constant__ FusedParams p, const __grid_constant__ EpiMaps em) {
     using C = Cfg<BN, STAGES, SPLIT3>;
+    // Plain TF32 tiles: the epilogue's C and output through TMA boxes
+    // (FusedParams::tma_c / tma_out), as in the CTA-pair kernels.
+    constexpr bool kBoxes = C::kBoxRoom && !KSPLIT && !BATCHED;
     static_assert(!KSPLIT || SPLIT3 == SEG, "K split: TF32, or 3xTF32 with segments");
     static_assert(!(KSPLIT && BATCHED), "a batched launch does not split K");
     extern __shared__ uint8_t smem_raw[];
@@ -183,6 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
     auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
     const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+    auto cbox_bar = [&](int w, int i) { return bar0 + 8u * (2 * STAGES + 5 + 2 * (w - 2) + i); };
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -200,6 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(tempty_bar(a), 128);
         }
         mbar_init(drain_bar, 1);
+        for (int i = 0; i < 8; ++i) mbar_init(bar0 + 8u * (2 * STAGES + 5 + i), 1);
         *abort_flag = 0;
         fence_barrier_init();
         tma_prefetch_desc(&tmA);
@@ -208,6 +219,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_desc(&tmA2);
             tma_prefetch_desc(&tmB2);
         }
+        if (kBoxes && p.tma_c) tma_prefetch_desc(&em.c);
+        if (kBoxes && p.tma_out) tma_prefetch_desc(&em.out);
     }
     if (warp == 1) {
         tmem_alloc(smem_addr(tmem_slot), C::kTmemCols);
@@ -364,6 +377,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ------------------------------------------------------------ epilogue
         const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+        uint32_t cbox_phase = 0;    // bit i: parity of box i's next C load
+        uint32_t cbox_pending = 0;  // bit i: a C load into box i not yet waited for
+        bool cbox_failed = false;
         const int row_in_tile = quad * 32 + lane;
         int acc = 0;
         uint32_t acc_phase = 0;
@@ -499,9 +515,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 if (row_ok && !p.prefetch_early) prefetch_full_operands(row, col0, min(BN, p.N - col0), p, b);
                 const uint32_t taddr = lane_base + static_cast<uint32_t>(acc * BN);
+                // C in and the result out as 32 x 32 TMA boxes of this warp's
+                // 32 rows through two shared-memory boxes, as the CTA-pair
+                // kernels' epilogue does (fused_gemm_pair.cu): box i holds C
+                // of chunk c, then chunk c's result until its store has read
+                // it, then C of chunk c + 2.
+                const int box_row0 = mb * kBM + quad * 32;
+                const bool boxes = kBoxes && box_row0 < p.M;
+                const bool cbox = boxes && p.tma_c;
+                const bool obox = boxes && p.tma_out;
+                uint8_t* const box_buf = smem + C::kBoxOffset + (warp - 2) * 8192;
+                auto cbox_load = [&](int c) {
+                    const int i = c & 1;
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(cbox_bar(warp, i), 32 * 32 * 4);
+                        tma_load_2d(smem_addr(box_buf + i * 4096), &em.c, cbox_bar(warp, i), col0 + 32 * c, box_row0);
+                    }
+                    cbox_pending |= 1u << i;
+                };
+                // The previous tile's box stores have read both boxes, and its
+                // lanes' reads of them come before the TMA writes below.
+                if ((cbox || obox) && lane == 0) {
+                    if (obox) bulk_wait_group_read<0>();
+                    fence_proxy_async_shared();
+                }
+                if (cbox) {
+                    cbox_load(0);
+                    if (!obox && chunks > 1) cbox_load(1);
+                }
                 for (int c = 0; c < chunks; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + 32 * c, r);
+                    const int i = c & 1;
+                    if (cbox && obox && c + 1 < chunks) {
+                        // box i ^ 1 is free once chunk c - 1's store has read it
+                        if (lane == 0) bulk_wait_group_read<0>();
+                        cbox_load(c + 1);
+                    } else if (!cbox && obox && lane == 0) {
+                        bulk_wait_group_read<1>();  // chunk c - 2's store has read box i
+                    }
                     tmem_ld_wait();
                     if (c == chunks - 1) {
                         // Accumulator fully read: hand it back to the MMA warp.
@@ -510,14 +562,67 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     float v[32];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                    for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
                     const int col = col0 + 32 * c;
-                    apply_epilogue(v, row, col, row_ok, p, nullptr, b);
-                    if (row_ok) store_row_chunk(v, row, col, p, out_off);
+                    uint8_t* const rowp = box_buf + i * 4096 + lane * 128;
+                    if (cbox) {
+                        const bool got = mbar_wait(cbox_bar(warp, i), (cbox_phase >> i) & 1u, p.timeout_ns);
+                        if (!__all_sync(0xffffffffu, got)) {
+                            if (lane == 0) raise_error(p, abort_flag, kErrEpilogue);
+                            cbox_failed = true;
+                            break;
+                        }
+                        cbox_phase ^= 1u << i;
+                        cbox_pending &= ~(1u << i);
+                        // Step 0 (v += C), the add the FULL step makes; columns
+                        // past N read the box's zero fill and are never stored.
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const float4 x = *reinterpret_cast<const float4*>(rowp + ((j ^ (lane & 7)) << 4));
+                            v[4 * j] += x.x;
+                            v[4 * j + 1] += x.y;
+                            v[4 * j + 2] += x.z;
+                            v[4 * j + 3] += x.w;
+                        }
+                        if (!obox) {
+                            __syncwarp();  // every lane has read box i: it may be refilled
+                            if (c + 2 < chunks) {
+                                if (lane == 0) fence_proxy_async_shared();
+                                cbox_load(c + 2);
+                            }
+                        }
+                    }
+                    apply_epilogue(v, row, col, row_ok, p, nullptr, b, cbox);
+                    if (obox) {
+                        // The result into box i (rows past M and columns past N
+                        // are clipped by the store), then one TMA store of it.
+                        if (!cbox) __syncwarp();  // lane 0 waited for box i above
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            *reinterpret_cast<float4*>(rowp + ((j ^ (lane & 7)) << 4)) =
+                                make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                        fence_proxy_async_shared();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_2d(&em.out, smem_addr(box_buf + i * 4096), col, box_row0);
+                            bulk_commit_group();
+                        }
+                    } else if (row_ok) {
+                        store_row_chunk(v, row, col, p, out_off);
+                    }
                 }
+                if (cbox_failed) break;
                 acc ^= 1;
                 if (acc == 0) acc_phase ^= 1u;
             }
+        }
+        // A C box load not waited for (a wait that ran out above) lands before
+        // the CTA leaves, and so do the boxes' stores.
+        if (kBoxes) {
+            for (int i = 0; i < 2; ++i)
+                if (cbox_pending & (1u << i)) mbar_wait(cbox_bar(warp, i), (cbox_phase >> i) & 1u, p.timeout_ns);
+            if (lane == 0) bulk_wait_group<0>();
+            __syncwarp();
         }
     }
 
@@ -684,6 +789,15 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
         for (int i = 0; i < g.n_steps; ++i) p.ep_bstride[i] = g.ep_bstride[i];
     }
 
+    EpiMaps em;
+    memset(&em, 0, sizeof(em));
+    if (C::kBoxRoom && !KSPLIT && !BATCHED && epi_tma_enabled()) {
+        if (g.n_steps > 0 && g.steps[0].kind == MXB_EP_ADD_FULL && (g.steps[0].ld_or_size & 3) == 0 &&
+            (reinterpret_cast<uintptr_t>(g.steps[0].ptr) & 15) == 0)
+            p.tma_c = make_epi_map(&em.c, g.steps[0].ptr, g.M, g.N, g.steps[0].ld_or_size) ? 1 : 0;
+        if ((g.ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(g.out) & 15) == 0)
+            p.tma_out = make_epi_map(&em.out, g.out, g.M, g.N, g.ldo) ? 1 : 0;
+    }
     const int grid = p.num_tiles < g.num_sms ? p.num_tiles : g.num_sms;
     if (KSPLIT && p.ks_cluster) {
         // One cluster of p.splits CTAs per tile, one slice per CTA; the slices
@@ -700,12 +814,12 @@ cudaError_t run_variant(const GemmLaunch& g, cudaStream_t stream) {
         attr.val.clusterDim.z = 1;
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, kernel, mA, mB, mA2, mB2, p);
+        e = cudaLaunchKernelEx(&cfg, kernel, mA, mB, mA2, mB2, p, em);
         if (e != cudaSuccess) return e;
         note_launch();
         return cudaGetLastError();
     }
-    kernel<<<grid, kThreads, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p);
+    kernel<<<grid, kThreads, C::kSmemBytes, stream>>>(mA, mB, mA2, mB2, p, em);
     note_launch();
     if (KSPLIT) {
         e = cudaGetLastError();

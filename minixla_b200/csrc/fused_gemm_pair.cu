@@ -623,13 +623,6 @@ bool gather_tma_enabled() {
     return !(v && v[0] == '0');
 }
 
-// MINIXLA_EPI_TMA=0: the single-buffer tiles' epilogue reads C and writes
-// the output row by row from global memory instead of through TMA boxes.
-bool epi_tma_enabled() {
-    const char* v = getenv("MINIXLA_EPI_TMA");
-    return !(v && v[0] == '0');
-}
-
 template <int STAGES, int BN, bool DUAL, int EPI = 4, bool PUSH = false, bool BATCHED = false>
 cudaError_t run_pair_variant(const GemmLaunch& g, cudaStream_t stream) {
     using C = PairCfg<STAGES, BN, DUAL, EPI, PUSH>;

@@ -157,6 +157,13 @@ struct PeerMaps {
     CUtensorMap m[kMaxPeers];
 };
 
+// MINIXLA_EPI_TMA=0: the TF32 kernels' epilogue reads C and writes the
+// output row by row from global memory instead of through TMA boxes.
+inline bool epi_tma_enabled() {
+    const char* v = getenv("MINIXLA_EPI_TMA");
+    return !(v && v[0] == '0');
+}
+
 // The epilogue's tensor maps (make_epi_map): step 0's FULL operand, [M, N],
 // its own pitch (FusedParams::tma_c); the output, [M, N], pitch ldo (tma_out).
 struct EpiMaps {
